@@ -1,0 +1,393 @@
+"""Benchmark of the HOFA decode hot path.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl ours|reference]
+
+One step = one HOFA decode step of the attention core for a batch of B
+sequences on every GPU (d_model=1024 -> H=16, d_h=64,
+r=16, cache length L=4096, bf16 activations, float32 GLA state), i.e. one
+``hofa_decode_fwd`` launch per GPU: split-K softmax over the outlier cache,
+GLA state update + readout, RMSNorm, blend.  Sequences are sharded across
+GPUs with no collective (weak scaling); rank 0 prints one JSON line with the
+whole-job tokens/s (device time, max over ranks).
+
+* ``value``: steps timed with CUDA events on device-resident inputs.  The
+  caches of consecutive steps rotate through enough independent sets to
+  exceed 3x the L2 size, so every step streams its cache from HBM.
+* ``e2e``: the same step through the public operator ``fused_hofa_decode``
+  with the step's inputs (new token q/k/v, log decay, mix gate) copied from
+  pinned host memory and the output copied back and read on the host every
+  step; caches and GLA state stay resident (as in any decode loop).
+* ``roofline``: algorithmic HBM bytes of one launch
+  (B*H*(L*(r+d_h)*2 + (d_h-r)*d_h*4*2)) / its average duration, against the
+  measured copy bandwidth in MEASURED_PEAKS.json.
+* ``cpu_baseline`` / ``--impl reference``: the reference's CPU computation of
+  the same step (the oracle restatement of the training layer's decode core,
+  src/HybridOutlierFactorizedAttentionTrain.py:403-436) in float32 on the
+  host cores, timed on a bounded sample.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+import torch.nn.functional as F
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "HOFA decode tokens/s (350M, B=1/4/64) & prefill tok/s; % of HBM/TC roofline"
+H, D, R, L = 16, 64, 16, 4096
+J = D - R
+FALLBACK_HBM_GBS = 6650.0
+
+
+def algorithmic_bytes(B: int) -> int:
+    return B * H * (L * (R + D) * 2 + J * D * 4 * 2)
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def ncu_traffic(B: int):
+    """dram bytes (read + write) per launch from the committed ncu summary of
+    this workload, if present (line ``traffic_bytes_per_launch_B<B>: N``)."""
+    p = os.path.join(ROOT, "profiles", "hofa_decode_config1.md")
+    if not os.path.exists(p):
+        return None
+    key = f"traffic_bytes_per_launch_B{B}:"
+    for line in open(p):
+        if line.strip().startswith(key):
+            try:
+                return int(line.split(":", 1)[1].strip().split()[0].replace(",", ""))
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples while the GPU works."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self.t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-lms", "50", "-i", str(self.gpu)],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.t = threading.Thread(target=self._read, daemon=True)
+        self.t.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.time(), line.strip()))
+
+    def stop(self, t0: float, t1: float):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        rows = [l for (ts, l) in self.lines if t0 - 0.06 <= ts <= t1 + 0.06] or [l for _, l in self.lines[-3:]]
+        sm, smax, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in rows:
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- inputs
+def make_step_inputs(B, device, seed, dtype=torch.bfloat16):
+    """Config-1 inputs: caches from N(0,1) projections, state ~ N(0, 0.1),
+    log decay = logsigmoid(x.W_d)/16 and mix = sigmoid(x.W_m) for one new token."""
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    x = torch.randn(B, 1, 1024, generator=g)
+    Wq, Wk, Wv = (torch.randn(1024, 1024, generator=g) * 0.02 for _ in range(3))
+    Wd, Wm = torch.randn(1024, H, generator=g) * 0.02, torch.randn(1024, H, generator=g) * 0.02
+    for h in range(H):
+        Wq[h * D:h * D + R] *= 8
+        Wk[h * D:h * D + R] *= 8
+    sf = D ** 0.25
+    q = (x @ Wq.T / sf).view(B, 1, H, D).transpose(1, 2)
+    k = (x @ Wk.T / sf).view(B, 1, H, D).transpose(1, 2)
+    v = (x @ Wv.T).view(B, 1, H, D).transpose(1, 2)
+    log_gamma = (F.logsigmoid(x @ Wd) / 16).view(B, 1, H).transpose(1, 2)
+    mix = torch.sigmoid(x @ Wm).view(B, 1, H).transpose(1, 2)
+    return dict(q=q.to(dtype), k=k.to(dtype), v=v.to(dtype), log_gamma=log_gamma.float().contiguous(),
+                mix=mix.to(dtype).contiguous(), norm_w=torch.ones(H, D), Wk=Wk, Wv=Wv)
+
+
+def make_cache(B, device, seed, dtype=torch.bfloat16):
+    """K cache = projections of N(0,1) inputs (the outlier channels of K are
+    x8 and RoPE-rotated; rotation does not change the byte traffic, and the
+    projections are generated on the GPU to keep set-up fast)."""
+    g = torch.Generator(device=device).manual_seed(seed)
+    ck = (torch.randn(B, H, L, R, device=device, generator=g) * 0.64).to(dtype)
+    cv = (torch.randn(B, H, L, D, device=device, generator=g) * 0.64).to(dtype)
+    st = torch.randn(B, H, J, D, device=device, generator=g) * 0.1
+    return ck, cv, st
+
+
+# ----------------------------------------------------------------------------- our arm
+def run_ours(args):
+    import torch.distributed as dist
+    from outlierneuronattention_b200 import _capi
+    from outlierneuronattention_b200.hofa_decode import decode_args, decode_workspace, fused_hofa_decode
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    B = args.batch
+    props = torch.cuda.get_device_properties(dev)
+    l2 = props.L2_cache_size if hasattr(props, "L2_cache_size") else 126 * 2 ** 20
+    per_set = algorithmic_bytes(B)
+    nsets = max(2, math.ceil(3 * l2 / per_set))
+
+    inp = make_step_inputs(B, dev, seed=1000 + rank)
+    q, k, v = inp["q"].to(dev), inp["k"].to(dev), inp["v"].to(dev)
+    lg, mix, nw = inp["log_gamma"].to(dev), inp["mix"].to(dev), inp["norm_w"].to(dev)
+    sets = [make_cache(B, dev, seed=7 * rank + i) for i in range(nsets)]
+    outs = [torch.empty(B, H, J, D, device=dev) for _ in range(nsets)]
+    y = torch.empty_like(q)
+    ws = decode_workspace(dev, B, H, D)
+    split = args.split_k or 0
+    fmt = _capi.FORMATS[_capi.DecodeArgs]
+    bufs = [fmt.pack(*decode_args(q, k, v, ck, cv, st, outs[i], lg, mix, nw, R, L, 2.0, y, split_k=split,
+                                  workspace=ws))
+            for i, (ck, cv, st) in enumerate(sets)]
+    fn = _capi.lib().hofa_decode_fwd
+
+    stream = torch.cuda.Stream(dev)
+    sh = stream.cuda_stream
+
+    def launch_steps(n, start=0):
+        for i in range(n):
+            st = fn(bufs[(start + i) % nsets], sh)
+            if st != 0:
+                raise RuntimeError(_capi.lib().hofa_last_error().decode())
+
+    # graph of `chunk` consecutive steps (removes host launch overhead)
+    chunk = min(args.steps, 1000)
+    with torch.cuda.stream(stream):
+        launch_steps(nsets)
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            launch_steps(chunk)
+    torch.cuda.synchronize()
+
+    def run(nsteps):
+        full, rem = divmod(nsteps, chunk)
+        for _ in range(full):
+            graph.replay()
+        if rem:
+            launch_steps(rem)
+
+    sampler = ClockSampler(int(os.environ.get("CUDA_VISIBLE_DEVICES", str(local)).split(",")[local])
+                           if "CUDA_VISIBLE_DEVICES" in os.environ else local)
+    sampler.start()
+    t_load0 = time.time()
+    with torch.cuda.stream(stream):
+        # warm-up: the requested steps, and at least ~0.4 s of work so clocks settle under load
+        run(args.warmup)
+        tw = time.time()
+        while time.time() - tw < 0.4:
+            run(chunk)
+            stream.synchronize()
+        stream.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t_timed0 = time.time()
+        e0.record(stream)
+        run(args.steps)
+        e1.record(stream)
+        stream.synchronize()
+        t_timed1 = time.time()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = sampler.stop(t_timed0 if t_timed1 - t_timed0 > 0.15 else t_load0, t_timed1)
+    ms = e0.elapsed_time(e1)
+    ms_t = torch.tensor([ms], device=dev)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = ms_t.item()
+    ms_step = ms_max / args.steps
+    value = B * world * args.steps / (ms_max / 1e3)
+
+    # ---- e2e through the public operator with host buffers ----------------
+    host = {n: t.pin_memory() for n, t in (("q", inp["q"]), ("k", inp["k"]), ("v", inp["v"]),
+                                             ("lg", inp["log_gamma"]), ("mix", inp["mix"]))}
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    dlg, dmix = torch.empty_like(lg), torch.empty_like(mix)
+    yh = torch.empty(B, H, 1, D, dtype=q.dtype).pin_memory()
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    d2h = yh.numel() * yh.element_size()
+    ck0, cv0, st0 = sets[0]
+    e2e_steps = max(args.steps, 50)
+
+    def e2e_step(i):
+        dq.copy_(host["q"], non_blocking=True)
+        dk.copy_(host["k"], non_blocking=True)
+        dv.copy_(host["v"], non_blocking=True)
+        dlg.copy_(host["lg"], non_blocking=True)
+        dmix.copy_(host["mix"], non_blocking=True)
+        s_in, s_out = (st0, outs[0]) if i % 2 == 0 else (outs[0], st0)
+        yy = fused_hofa_decode(dq, dk, dv, ck0, cv0, s_in, s_out, dlg, dmix, nw, R, L, 2.0,
+                               split_k=split or None)
+        yh.copy_(yy, non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+        return float(yh[0, 0, 0, 0])
+
+    for i in range(5):
+        e2e_step(i)
+    if world > 1:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for i in range(e2e_steps):
+        e2e_step(i)
+    e2e_s = time.perf_counter() - t0
+    e2e_t = torch.tensor([e2e_s], device=dev)
+    if world > 1:
+        dist.all_reduce(e2e_t, op=dist.ReduceOp.MAX)
+    e2e_value = B * world * e2e_steps / e2e_t.item()
+
+    # ---- roofline of the decode kernel (this arm's only kernel) ------------
+    peak, peak_kind = peaks()
+    achieved = algorithmic_bytes(B) / (ms_step / 1e3) / 1e9
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "peak_source": f"{peak_kind} hbm_gbs",
+                "traffic": ncu_traffic(B), "algorithmic_bytes_per_launch": algorithmic_bytes(B)}
+
+    out = {"metric": METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+           "warmup": args.warmup, "ms_per_step": round(ms_step, 6), "higher_is_better": True, "scaling": "weak",
+           "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+           "config": {"workload": f"config1-decode-B{B}-L{L}", "d_model": 1024, "heads": H, "d_head": D, "r": R,
+                      "cache_len": L, "batch_per_gpu": B, "global_batch": B * world,
+                      "split_k": split or int(_capi.lib().hofa_decode_choose_split(B, H, L, props.multi_processor_count)),
+                      "l2": f"inputs larger than L2: {nsets} rotating cache sets x {per_set / 1e6:.1f} MB",
+                      "parallelism": f"batch-sharded decode over {world} GPU(s), no collective"},
+           "roofline": roofline,
+           "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                   "d2h_bytes_per_step": d2h, "api": "outlierneuronattention_b200.fused_hofa_decode"},
+           "gpu_launches": args.steps, "clocks": clocks}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        out["cpu_baseline"] = cpu_baseline(B, args.cpu_seconds)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+
+
+# ----------------------------------------------------------------------------- CPU arm
+def cpu_baseline(B: int, seconds: float):
+    """The reference's CPU computation of one decode step (oracle port of the
+    training layer's decode core) on config-1 tensors, float32, all threads."""
+    from oracle.hofa_oracle import FP32_EPS, decode_core
+    torch.set_num_threads(max(1, len(os.sched_getaffinity(0))))
+    inp = make_step_inputs(B, "cpu", seed=1000, dtype=torch.float32)
+    g = torch.Generator().manual_seed(5)
+    ck = torch.randn(B, H, L, R, generator=g) * 0.64
+    cv = torch.randn(B, H, L, D, generator=g) * 0.64
+    st = torch.randn(B, H, J, D, generator=g) * 0.1
+    step = lambda s: decode_core(inp["q"], inp["k"], inp["v"], ck, cv, s, inp["log_gamma"], inp["mix"].float(),
+                                 inp["norm_w"], R, L, 2.0, eps=FP32_EPS, dtype=torch.float32)
+    for _ in range(3):
+        step(st)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        _, st = step(st)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds and n >= 3:
+            break
+    value = B * n / el
+    return {"value": round(value, 2), "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
+            "sample": f"{n} decode steps of config 1 (B={B}, L={L}) in float32, {el:.1f} s",
+            "ms_per_step": round(1e3 * el / n, 3)}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    cb = cpu_baseline(args.batch, args.cpu_seconds)
+    out = {"impl": "reference", "metric": METRIC, "value": cb["value"], "unit": "tokens/s", "n_gpus": args.gpus,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": cb["ms_per_step"], "higher_is_better": True,
+           "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+           "config": {"workload": f"config1-decode-B{args.batch}-L{L}", "d_model": 1024, "heads": H, "d_head": D,
+                      "r": R, "cache_len": L, "batch_per_gpu": args.batch,
+                      "parallelism": "host CPU (reference PyTorch CPU path, oracle port)"},
+           "cpu_baseline": {"value": cb["value"], "unit": "tokens/s", "cores": cb["cores"], "kind": "port",
+                            "sample": cb["sample"]},
+           "e2e": {"value": cb["value"], "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=50)
+    ap.add_argument("--batch", type=int, default=4)
+    ap.add_argument("--split-k", type=int, default=0)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,97 @@
+// Internal launch interface between the C ABI (capi.cu) and the kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace hofa {
+
+struct DecodeParams {
+  const void* q; const void* k; const void* v;
+  const void* cache_k; const void* cache_v;
+  const float* state_in; float* state_out;
+  const void* log_gamma; const void* mix_g; const void* norm_w; const void* log_alpha;
+  void* y;
+  int B, H, D, R;
+  int L;                      // cache capacity (rows)
+  int seq_len;
+  const int* seq_len_dev;
+  float qk_scale_log2;        // sm_scale * log2(e)
+  float eps;
+  int split_k;
+  int64_t sq[3], sk[3], sv[3];  // b, h, d
+  int64_t sck[4], scv[4];       // b, h, t, d
+  int64_t sst[3], sso[3];       // b, h, row  (d stride is 1)
+  int64_t slg[2], smg[2];       // b, h
+  int64_t snw[2];               // h, d
+  int64_t sla[3];               // b, h, j
+  int64_t sy[3];                // b, h, d
+  int dt_lg, dt_mg, dt_nw, dt_la;
+  float* ws_part;
+  int* ws_count;
+  int* ws_status;
+};
+
+cudaError_t launch_decode(const DecodeParams& p, int dtype, bool vec, bool alpha, cudaStream_t st);
+
+struct GlaParams {
+  const void* q; const void* k; const void* v;
+  const void* log_gamma; const void* log_alpha; const void* mix_g; const void* gla_scale;
+  const float* state_init;
+  void* y;
+  float* state_out;
+  int B, H, T, D, R, J;
+  int chunk;
+  int nseg;                   // segments per (b,h)
+  int seg_len;                // tokens per segment (multiple of chunk)
+  float eps;
+  bool fuse;                  // mix_g and gla_scale present
+  int64_t sq[4], sk[4], sv[4], sy[4];
+  int64_t slg[3], smg[3];
+  int64_t sla[3];
+  int64_t sgs[2];
+  int64_t ssi[3], sso[4];     // state_init b,h,row ; state_out b,h,row,d
+  int dt_lg, dt_mg, dt_la, dt_gs;
+  float* ws_state;            // [B,H,nseg,J,D] local end states
+  float* ws_decay;            // [B,H,nseg,J] log of the segment's total decay
+};
+
+cudaError_t launch_gla(const GlaParams& p, int dtype, cudaStream_t st);
+
+struct OutlierParams {
+  const void* q; const void* k; const void* v; const void* mix_g;
+  void* out;
+  int B, H, Tq, Tk, D, R;
+  int q_offset;
+  float qk_scale_log2;
+  bool accumulate;
+  int64_t sq[4], sk[4], sv[4], so[4];
+  int64_t smg[3];
+  int dt_mg;
+};
+
+cudaError_t launch_outlier(const OutlierParams& p, int dtype, cudaStream_t st);
+
+struct PrepParams {
+  void* q; void* k; const void* v;
+  const void* gate_w; const void* gate_b;
+  const void* mix_w; const void* mix_b; const void* fixed_mix;
+  const void* cos; const void* sin;
+  void* log_gamma; void* mix_out;
+  void* cache_k; void* cache_v;
+  int B, H, N, D, R;
+  int pos0; const int* pos0_dev;
+  int L;                       // cache rows (bound for the append)
+  int P;                       // rows of the RoPE tables
+  bool rope;
+  int64_t sq[4], sk[4], sv[4];
+  int64_t sgw[2], sgb, smw[2], smb, sfm;
+  int64_t scos[2], ssin[2];
+  int64_t slg[3], smo[3];
+  int64_t sck[4], scv[4];
+  int dt_gw, dt_gb, dt_mw, dt_mb, dt_fm, dt_cs, dt_lg, dt_mo;
+};
+
+cudaError_t launch_prep(const PrepParams& p, int dtype, cudaStream_t st);
+
+}  // namespace hofa

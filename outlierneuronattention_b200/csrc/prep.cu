@@ -1,0 +1,136 @@
+// Gates + RoPE + cache export for one (b, h, token) per warp.
+//
+// Replaces the layer's elementwise glue around the attention core
+// (src/HybridOutlierFactorizedAttention.py):
+//   * _compute_gates_optimized (:67-95): gate = q.Wg[h,:D] + k.Wg[h,D:] + bg[h]
+//     and mix = sigmoid(q.Wm[h,:D] + k.Wm[h,D:] + bm[h]) on the UN-rotated q, k
+//     (or sigmoid(fixed_mix[h]) for the fixed-blend ablation);
+//   * log_gamma = logsigmoid(-gate) (:177, :361);
+//   * rotate-half RoPE of channels [0, R) of q and k in place, at absolute
+//     position pos0 + n, from the module's cos/sin tables (:180-188,
+//     :365-375; src/modules/modules.py:33-45);
+//   * the outlier cache rows: cache_k[.., pos, :R] = rotated k,
+//     cache_v[.., pos, :] = v (:196-198 prefill export, :382-384 decode append).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace hofa {
+
+namespace {
+
+constexpr int kPrepWarps = 8;
+
+template <typename T, int D>
+__global__ void __launch_bounds__(kPrepWarps * 32)
+prep_kernel(const PrepParams p) {
+  constexpr int PL = D / 32 > 0 ? D / 32 : 1;  // channels per lane
+  __shared__ float xs[kPrepWarps][2][D];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int64_t gw = (int64_t)blockIdx.x * kPrepWarps + warp;
+  const int64_t total = (int64_t)p.B * p.H * p.N;
+  if (gw >= total) return;
+  const int n = (int)(gw % p.N);
+  const int h = (int)((gw / p.N) % p.H);
+  const int b = (int)(gw / ((int64_t)p.N * p.H));
+
+  T* qp = reinterpret_cast<T*>(p.q) + b * p.sq[0] + h * p.sq[1] + (int64_t)n * p.sq[2];
+  T* kp = reinterpret_cast<T*>(p.k) + b * p.sk[0] + h * p.sk[1] + (int64_t)n * p.sk[2];
+
+  float qv[PL], kv[PL];
+  float g = 0.f, ml = 0.f;
+#pragma unroll
+  for (int u = 0; u < PL; ++u) {
+    const int c = lane + 32 * u;
+    qv[u] = kv[u] = 0.f;
+    if (c < D) {
+      qv[u] = to_f(qp[(int64_t)c * p.sq[3]]);
+      kv[u] = to_f(kp[(int64_t)c * p.sk[3]]);
+      g = fmaf(qv[u], ld_any(p.gate_w, p.dt_gw, h * p.sgw[0] + c * p.sgw[1]), g);
+      g = fmaf(kv[u], ld_any(p.gate_w, p.dt_gw, h * p.sgw[0] + (D + c) * p.sgw[1]), g);
+      if (p.mix_w != nullptr) {
+        ml = fmaf(qv[u], ld_any(p.mix_w, p.dt_mw, h * p.smw[0] + c * p.smw[1]), ml);
+        ml = fmaf(kv[u], ld_any(p.mix_w, p.dt_mw, h * p.smw[0] + (D + c) * p.smw[1]), ml);
+      }
+      xs[warp][0][c] = qv[u];
+      xs[warp][1][c] = kv[u];
+    }
+  }
+  g = warp_sum(g);
+  ml = warp_sum(ml);
+  if (lane == 0) {
+    g += ld_any(p.gate_b, p.dt_gb, h * p.sgb);
+    // logsigmoid(-g) = -softplus(g) = -(max(g,0) + log1p(exp(-|g|)))
+    const float lgam = -(fmaxf(g, 0.f) + log1pf(expf(-fabsf(g))));
+    st_any(p.log_gamma, p.dt_lg, b * p.slg[0] + h * p.slg[1] + (int64_t)n * p.slg[2], lgam);
+    if (p.mix_out != nullptr) {
+      float mlog;
+      if (p.mix_w != nullptr) mlog = ml + ld_any(p.mix_b, p.dt_mb, h * p.smb);
+      else mlog = ld_any(p.fixed_mix, p.dt_fm, h * p.sfm);
+      const float mix = 1.f / (1.f + expf(-mlog));
+      st_any(p.mix_out, p.dt_mo, b * p.smo[0] + h * p.smo[1] + (int64_t)n * p.smo[2], mix);
+    }
+  }
+  __syncwarp();
+
+  int pos = (p.pos0_dev != nullptr ? *p.pos0_dev : p.pos0) + n;
+  const int R = p.R, half = R / 2;
+  if (p.rope && R > 0) {
+    const int prow = pos < 0 ? 0 : (pos < p.P ? pos : p.P - 1);
+#pragma unroll
+    for (int u = 0; u < PL; ++u) {
+      const int c = lane + 32 * u;
+      if (c < R) {
+        const float cs = ld_any(p.cos, p.dt_cs, (int64_t)prow * p.scos[0] + c * p.scos[1]);
+        const float sn = ld_any(p.sin, p.dt_cs, (int64_t)prow * p.ssin[0] + c * p.ssin[1]);
+        const float qr = (c < half) ? -xs[warp][0][c + half] : xs[warp][0][c - half];
+        const float kr = (c < half) ? -xs[warp][1][c + half] : xs[warp][1][c - half];
+        qv[u] = qv[u] * cs + qr * sn;
+        kv[u] = kv[u] * cs + kr * sn;
+        qp[(int64_t)c * p.sq[3]] = from_f<T>(qv[u]);
+        kp[(int64_t)c * p.sk[3]] = from_f<T>(kv[u]);
+      }
+    }
+  }
+  if (p.cache_k != nullptr && pos >= 0 && pos < p.L) {
+    T* ck = reinterpret_cast<T*>(p.cache_k) + b * p.sck[0] + h * p.sck[1] + (int64_t)pos * p.sck[2];
+#pragma unroll
+    for (int u = 0; u < PL; ++u) {
+      const int c = lane + 32 * u;
+      if (c < R) ck[(int64_t)c * p.sck[3]] = from_f<T>(kv[u]);
+    }
+  }
+  if (p.cache_v != nullptr && pos >= 0 && pos < p.L) {
+    const T* vp = reinterpret_cast<const T*>(p.v) + b * p.sv[0] + h * p.sv[1] + (int64_t)n * p.sv[2];
+    T* cv = reinterpret_cast<T*>(p.cache_v) + b * p.scv[0] + h * p.scv[1] + (int64_t)pos * p.scv[2];
+#pragma unroll
+    for (int u = 0; u < PL; ++u) {
+      const int c = lane + 32 * u;
+      if (c < D) cv[(int64_t)c * p.scv[3]] = vp[(int64_t)c * p.sv[3]];
+    }
+  }
+}
+
+template <typename T>
+cudaError_t launch_t(const PrepParams& p, cudaStream_t st) {
+  const int64_t total = (int64_t)p.B * p.H * p.N;
+  const dim3 grid((unsigned)((total + kPrepWarps - 1) / kPrepWarps));
+  switch (p.D) {
+    case 32: prep_kernel<T, 32><<<grid, kPrepWarps * 32, 0, st>>>(p); break;
+    case 64: prep_kernel<T, 64><<<grid, kPrepWarps * 32, 0, st>>>(p); break;
+    case 128: prep_kernel<T, 128><<<grid, kPrepWarps * 32, 0, st>>>(p); break;
+    default: return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace
+
+cudaError_t launch_prep(const PrepParams& p, int dtype, cudaStream_t st) {
+  switch (dtype) {
+    case HOFA_DTYPE_BF16: return launch_t<__nv_bfloat16>(p, st);
+    case HOFA_DTYPE_F16: return launch_t<__half>(p, st);
+    default: return launch_t<float>(p, st);
+  }
+}
+
+}  // namespace hofa

@@ -1,0 +1,133 @@
+"""The drop-in layer on the GPU against the reference's own outputs.
+
+``tests/golden/*.pt`` hold per-token outputs, outlier caches and GLA states
+of the reference layer (HybridOutlierFactorizedAttentionTrain.forward_step,
+float64).  The drop-in ``HybridOutlierFactorizedAttention`` loads the same
+state dict and must reproduce them through ``forward`` (prefill, any prefix
+length) followed by ``forward_step`` (decode) in every cache mode of the
+reference module (pre-allocated, concatenating, starting from no cache).
+
+Tolerances: float32 runs <= 1e-4 max-abs; bf16 (autocast) runs <= 2e-2.
+"""
+import pytest
+import torch
+
+from conftest import GOLDEN_CASES, load_golden
+from oracle.hofa_oracle import LayerShape, OracleLayer
+
+pytestmark = pytest.mark.gpu
+
+
+def make_layer(g, dtype=torch.float32):
+    from outlierneuronattention_b200 import HybridOutlierFactorizedAttention, ModelConfig
+    c = g["config"]
+    cfg = ModelConfig(d_model=c["d_model"], num_heads=c["num_heads"], num_layers=1, r=c["r"],
+                      chunk_size=c["chunk_size"], use_rope=c["use_rope"], rope_base=c["rope_base"],
+                      learnable_alpha=c["learnable_alpha"], fixed_blend_weight=c["fixed_blend_weight"])
+    m = HybridOutlierFactorizedAttention(cfg)
+    missing, unexpected = m.load_state_dict(g["state_dict"], strict=True), None
+    return m.to(device="cuda", dtype=dtype).eval()
+
+
+def err(a, b):
+    return (a.double().cpu() - b.double().cpu()).abs().max().item()
+
+
+@pytest.mark.parametrize("name", GOLDEN_CASES)
+def test_prefill_then_preallocated_decode_fp32(name):
+    g = load_golden(name)
+    m = make_layer(g)
+    x = g["x"].cuda()
+    B, T, _ = x.shape
+    H, D, r = m.num_heads, m.d_head, m.r
+    T0 = 50
+    with torch.no_grad():
+        y0, cache, state = m(x[:, :T0], return_state=True)
+        assert err(y0, g["y"][:, :T0]) <= 1e-4
+        assert err(state[0], g["states"][T0]) <= 1e-4
+        ys = [y0]
+        if r > 0:
+            Kc = torch.zeros(B, H, T, r, device="cuda")
+            Vc = torch.zeros(B, H, T, D, device="cuda")
+            Kc[:, :, :T0] = cache[0]
+            Vc[:, :, :T0] = cache[1]
+            cache = (Kc, Vc)
+        for t in range(T0, T):
+            y, cache, state = m.forward_step(x[:, t:t + 1], cache, state, cache_seq_len=t)
+            ys.append(y)
+        assert err(torch.cat(ys, 1), g["y"]) <= 1e-4
+        assert err(state[0], g["states"][T]) <= 1e-4
+        if r > 0:
+            assert err(cache[0], g["cache_k"]) <= 1e-4
+            assert err(cache[1], g["cache_v"]) <= 1e-4
+
+
+@pytest.mark.parametrize("name", ["hofa_r16", "hofa_r16_alpha", "gla_r0"])
+def test_decode_from_empty_cache_concat_mode_fp32(name):
+    """forward_step from cache_O=None, then the concatenating cache mode."""
+    g = load_golden(name)
+    m = make_layer(g)
+    x = g["x"].cuda()
+    cache, state, ys = None, None, []
+    with torch.no_grad():
+        for t in range(x.shape[1]):
+            y, cache, state = m.forward_step(x[:, t:t + 1], cache, state)
+            ys.append(y)
+    assert err(torch.cat(ys, 1), g["y"]) <= 1e-4
+    assert err(state[0], g["states"][x.shape[1]]) <= 1e-4
+
+
+@pytest.mark.parametrize("name", ["hofa_r16", "hofa_dh128_r32"])
+@pytest.mark.parametrize("T0", [50, 64, 72])
+def test_bf16_autocast_prefill_matches_reference(name, T0):
+    g = load_golden(name)
+    m = make_layer(g)
+    x = g["x"].cuda()
+    with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+        y, cache, state = m(x[:, :T0].to(torch.bfloat16), return_state=True)
+    assert y.dtype == torch.bfloat16
+    assert err(y, g["y"][:, :T0]) <= 2e-2
+    assert err(state[0], g["states"][T0]) <= 2e-2 * max(1.0, g["states"][T0].abs().max().item())
+
+
+def test_config0_fp32_against_oracle():
+    """BASELINE config 0 shape (B=2, T=512, d_model=512, H=8, d_h=64, r=16,
+    chunk 64) in float32, random gates and the outlier x8 weights."""
+    from outlierneuronattention_b200 import HybridOutlierFactorizedAttention, ModelConfig
+    torch.manual_seed(0)
+    cfg = ModelConfig(d_model=512, num_heads=8, num_layers=1, r=16, chunk_size=64)
+    m = HybridOutlierFactorizedAttention(cfg)
+    gen = torch.Generator().manual_seed(0)
+    with torch.no_grad():
+        for lin in (m.W_q, m.W_k, m.W_v, m.out_proj):
+            lin.weight.copy_(torch.randn(lin.weight.shape, generator=gen) * 0.02)
+        for h in range(8):
+            m.W_q.weight[h * 64:h * 64 + 16] *= 8
+            m.W_k.weight[h * 64:h * 64 + 16] *= 8
+        m.gate_proj.weight.copy_(torch.randn(m.gate_proj.weight.shape, generator=gen) * 0.02)
+        m.mix_proj.weight.copy_(torch.randn(m.mix_proj.weight.shape, generator=gen) * 0.02)
+    sd = {k: v.clone() for k, v in m.state_dict().items()}
+    x = torch.randn(2, 512, 512, generator=gen)
+    oracle = OracleLayer(LayerShape(512, 8, 16, 64), sd)
+    ref_y, ref_cache, ref_state = oracle.forward(x.double(), return_state=True)
+    m = m.cuda().eval()
+    with torch.no_grad():
+        y, cache, state = m(x.cuda(), return_state=True)
+    assert err(y, ref_y) <= 1e-4
+    assert err(cache[0], ref_cache[0]) <= 1e-4
+    assert err(cache[1], ref_cache[1]) <= 1e-4
+    assert err(state[0], ref_state) <= 1e-4 * max(1.0, ref_state.abs().max().item())
+    # one more token through forward_step == the oracle's decode step
+    xs = torch.randn(2, 1, 512, generator=gen)
+    with torch.no_grad():
+        ys, _, st2 = m.forward_step(xs.cuda(), cache, state)
+    oy, _, ost = oracle.forward_step(xs.double(), ref_cache, ref_state)
+    assert err(ys, oy) <= 1e-4
+    assert err(st2[0], ost) <= 1e-4 * max(1.0, ost.abs().max().item())
+
+
+def test_module_has_reference_parameter_names():
+    from outlierneuronattention_b200 import HybridOutlierFactorizedAttention, ModelConfig
+    g = load_golden("hofa_r16_alpha")
+    m = make_layer(g)
+    assert set(m.state_dict()) == set(g["state_dict"])

@@ -1,0 +1,157 @@
+"""Parity of the prefill kernels against the CPU oracle on identical seeded
+inputs:
+
+* hofa_prefill_gla_fwd (chunk_gla_inlier_fwd) vs ``chunk_gla_core``
+  (restating src/chunk_gla_inlier.py:153-237);
+* hofa_prefill_outlier_fwd (exact_attention_triton) vs
+  ``outlier_attention_core`` (restating src/exact_attention.py:163-188).
+
+Tolerances: bf16/fp16 outputs <= 2e-2 max-abs on the normalised output
+(raw GLA output: 2e-2 relative to its max); float32 inputs <= 1e-4; final
+GLA state (float32) <= 1e-3 relative in bf16 runs, 1e-5 in float32 runs.
+"""
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from oracle.hofa_oracle import chunk_gla_core, outlier_attention_core
+
+pytestmark = pytest.mark.gpu
+
+
+def rand_qkv(B, H, T, D, dtype, seed, scale=0.5):
+    g = torch.Generator().manual_seed(seed)
+    q, k, v = (torch.randn(B, H, T, D, generator=g) * scale for _ in range(3))
+    lg = F.logsigmoid(torch.randn(B, H, T, generator=g) * 2.0 + 1.0)
+    mix = torch.sigmoid(torch.randn(B, H, T, generator=g))
+    gs = 1.0 + 0.2 * torch.randn(1, H, 1, D, generator=g)
+    cast = lambda t: t.to(dtype)
+    return cast(q), cast(k), cast(v), lg, cast(mix), gs
+
+
+def maxabs(a, b):
+    return (a.double().cpu() - b.double()).abs().max().item()
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("T", [1, 63, 64, 65, 200, 1000])
+def test_gla_fused_epilogue(dtype, T):
+    from outlierneuronattention_b200 import chunk_gla_inlier_fwd
+    B, H, D, r = 2, 3, 64, 16
+    q, k, v, lg, mix, gs = rand_qkv(B, H, T, D, dtype, seed=T)
+    Y, st = chunk_gla_inlier_fwd(q.cuda(), k.cuda(), v.cuda(), lg.cuda(), r, 64, mix_g=mix.cuda(), gla_scale=gs.cuda())
+    Yr, Sr = chunk_gla_core(q, k, v, lg, r, 64, mix_g=mix, gla_scale=gs, eps=1e-5)
+    assert st.shape == (B, H, 64, 64)
+    tol = 1e-4 if dtype == torch.float32 else 2e-2
+    assert maxabs(Y, Yr) <= tol
+    s = st[:, :, :D - r, :D]
+    rel = (s.double().cpu() - Sr).abs().max().item() / Sr.abs().max().item()
+    assert rel <= (1e-5 if dtype == torch.float32 else 1e-3)
+    assert st[:, :, D - r:].abs().max().item() == 0
+
+
+@pytest.mark.parametrize("nseg", [1, 2, 3, 7])
+def test_gla_segments_and_initial_state(nseg):
+    from outlierneuronattention_b200.chunk_gla_inlier import gla_forward
+    B, H, T, D, r = 2, 2, 700, 64, 16
+    q, k, v, lg, mix, gs = rand_qkv(B, H, T, D, torch.float32, seed=100 + nseg)
+    s0 = torch.randn(B, H, D - r, D) * 0.3
+    st = torch.empty(B, H, D - r, D, device="cuda")
+    Y = gla_forward(q.cuda(), k.cuda(), v.cuda(), lg.cuda(), r, mix_g=mix.cuda(), gla_scale=gs.cuda(),
+                    state_out=st, initial_state=s0.cuda(), num_segments=nseg)
+    Yr, Sr = chunk_gla_core(q, k, v, lg, r, 64, mix_g=mix, gla_scale=gs, eps=1e-5, state_init=s0)
+    assert maxabs(Y, Yr) <= 1e-4
+    assert maxabs(st, Sr) <= 1e-4 * max(1.0, Sr.abs().max().item())
+
+
+@pytest.mark.parametrize("D,r", [(128, 16), (128, 64), (32, 8), (64, 0), (64, 32)])
+def test_gla_shapes_raw_output(D, r):
+    from outlierneuronattention_b200 import chunk_gla_inlier_fwd
+    B, H, T = 2, 2, 300
+    q, k, v, lg, _, _ = rand_qkv(B, H, T, D, torch.bfloat16, seed=D * 7 + r)
+    Y, st = chunk_gla_inlier_fwd(q.cuda(), k.cuda(), v.cuda(), lg.cuda(), r, 64)
+    Yr, Sr = chunk_gla_core(q, k, v, lg, r, 64)
+    assert maxabs(Y, Yr) <= 2e-2 * Yr.abs().max().item()
+    s = st[:, :, :D - r, :D]
+    assert (s.double().cpu() - Sr).abs().max().item() <= 1e-3 * Sr.abs().max().item()
+
+
+def test_gla_learnable_alpha_strong_decay():
+    """Per-channel decay exponents with strong decay (factored forms overflow there)."""
+    from outlierneuronattention_b200 import chunk_gla_inlier_fwd
+    B, H, T, D, r = 1, 2, 256, 64, 16
+    q, k, v, _, mix, gs = rand_qkv(B, H, T, D, torch.float32, seed=55)
+    lg = F.logsigmoid(torch.randn(B, H, T) * 2.0 - 3.0)  # gamma ~ 0.05
+    la = torch.randn(1, H, 1, D - r) * 0.5
+    Y, st = chunk_gla_inlier_fwd(q.cuda(), k.cuda(), v.cuda(), lg.cuda(), r, 64, log_alpha=la.cuda(),
+                                 mix_g=mix.cuda(), gla_scale=gs.cuda())
+    Yr, Sr = chunk_gla_core(q, k, v, lg, r, 64, log_alpha=la, mix_g=mix, gla_scale=gs, eps=1e-5)
+    assert torch.isfinite(Y).all()
+    assert maxabs(Y, Yr) <= 1e-4
+    assert maxabs(st[:, :, :D - r, :D], Sr) <= 1e-5 * max(1.0, Sr.abs().max().item())
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32, torch.float16])
+@pytest.mark.parametrize("T", [1, 100, 257])
+def test_outlier_attention(dtype, T):
+    from outlierneuronattention_b200 import exact_attention_triton
+    B, H, D, r = 2, 3, 64, 16
+    q, k, v, _, mix, _ = rand_qkv(B, H, T, D, dtype, seed=T + 1, scale=1.0)
+    base = (torch.randn(B, H, T, D) * 0.1).to(dtype)
+    out = base.cuda().clone()
+    exact_attention_triton(q.cuda(), k.cuda(), v.cuda(), r, 2.0, mix.cuda(), out=out)
+    ref = outlier_attention_core(q, k, v, r, 2.0, mix, out=base)
+    assert maxabs(out, ref) <= (1e-4 if dtype == torch.float32 else 2e-2)
+
+
+@pytest.mark.parametrize("D,r", [(128, 32), (32, 8), (64, 32), (128, 64), (64, 12)])
+def test_outlier_attention_shapes(D, r):
+    from outlierneuronattention_b200 import exact_attention_triton
+    B, H, T = 1, 2, 190
+    q, k, v, _, mix, _ = rand_qkv(B, H, T, D, torch.bfloat16, seed=D + r, scale=1.0)
+    out = exact_attention_triton(q.cuda(), k.cuda(), v.cuda(), r, math.sqrt(D / r), mix.cuda())
+    ref = outlier_attention_core(q, k, v, r, math.sqrt(D / r), mix)
+    assert maxabs(out, ref) <= 2e-2
+
+
+def test_outlier_attention_query_suffix_with_offset():
+    from outlierneuronattention_b200 import exact_attention_triton
+    B, H, T, D, r = 1, 2, 300, 64, 16
+    q, k, v, _, mix, _ = rand_qkv(B, H, T, D, torch.bfloat16, seed=77, scale=1.0)
+    out = exact_attention_triton(q[:, :, 170:].cuda(), k.cuda(), v.cuda(), r, 2.0, mix[:, :, 170:].cuda(),
+                                 q_offset=170, accumulate=False)
+    ref = outlier_attention_core(q[:, :, 170:], k, v, r, 2.0, mix[:, :, 170:], q_offset=170)
+    assert maxabs(out, ref) <= 2e-2
+
+
+def test_config2_full_size_sampled_heads():
+    """BASELINE config 2 (B=4, T=8192, H=16, d_h=64, r=16) in bf16 on the GPU;
+    two heads are checked against the oracle (the full float64 oracle would
+    take minutes): all rows of the GLA, and the first/last 128 query rows of
+    the attention."""
+    from outlierneuronattention_b200 import chunk_gla_inlier_fwd, exact_attention_triton
+    B, H, T, D, r = 4, 16, 8192, 64, 16
+    g = torch.Generator(device="cuda").manual_seed(2)
+    q = torch.randn(B, H, T, D, device="cuda", generator=g).to(torch.bfloat16)
+    k = torch.randn(B, H, T, D, device="cuda", generator=g).to(torch.bfloat16)
+    v = torch.randn(B, H, T, D, device="cuda", generator=g).to(torch.bfloat16)
+    lg = F.logsigmoid(torch.randn(B, H, T, device="cuda", generator=g) + 2.0)
+    mix = torch.sigmoid(torch.randn(B, H, T, device="cuda", generator=g)).to(torch.bfloat16)
+    gs = torch.ones(1, H, 1, D, device="cuda")
+    Y, st = chunk_gla_inlier_fwd(q, k, v, lg, r, 64, mix_g=mix, gla_scale=gs)
+    Y_gla = Y.clone()
+    exact_attention_triton(q, k, v, r, 2.0, mix, out=Y)
+    torch.cuda.synchronize()
+    assert torch.isfinite(Y).all()
+    for (b, h) in ((0, 0), (3, 15)):
+        sl = lambda t: t[b:b + 1, h:h + 1].cpu()
+        Yr, Sr = chunk_gla_core(sl(q), sl(k), sl(v), sl(lg), r, 64, mix_g=sl(mix), gla_scale=gs[:, h:h + 1].cpu(), eps=1e-5)
+        assert maxabs(sl(Y_gla), Yr) <= 2e-2
+        assert (sl(st)[:, :, :D - r, :D].double() - Sr).abs().max().item() <= 1e-3 * Sr.abs().max().item()
+        for q0 in (0, T - 128):
+            qs = sl(q)[:, :, q0:q0 + 128]
+            ref = outlier_attention_core(qs, sl(k), sl(v), r, 2.0, sl(mix)[:, :, q0:q0 + 128],
+                                         out=sl(Y_gla)[:, :, q0:q0 + 128], q_offset=q0)
+            assert maxabs(sl(Y)[:, :, q0:q0 + 128], ref) <= 2e-2
