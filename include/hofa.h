@@ -142,8 +142,15 @@ typedef struct hofa_outlier_args {
 } hofa_outlier_args;
 
 /* Replaces exact_attention_triton (src/exact_attention.py:163-188) and its
- * kernel _fwd_kernel (:45-161). */
+ * kernel _fwd_kernel (:45-161).  bf16/f16 inputs with D in {64, 128} and
+ * R in {16, 32, 64} run on the tcgen05 tensor-core kernel (TMA-fed, TMEM
+ * accumulators); other shapes and float32 inputs on a CUDA-core kernel. */
 int hofa_prefill_outlier_fwd(const hofa_outlier_args* args, void* stream);
+
+/* Device status of the tensor-core outlier kernel since the last read (0 = no
+ * fault; 1 = a bounded wait for a copy or an MMA ran out and the affected
+ * tile rows were not written), then clears it.  Synchronises `stream`. */
+int hofa_prefill_read_status(void* stream, int32_t* status_out);
 
 /* ------------------------------------------------------------------------ */
 /* Gates + RoPE + cache export (prefill and decode step).                     */

@@ -141,6 +141,8 @@ def lib():
                 L.hofa_decode_choose_split.argtypes = [c_int32] * 4
                 L.hofa_decode_read_status.restype = ctypes.c_int
                 L.hofa_decode_read_status.argtypes = [c_void_p, c_void_p, ctypes.POINTER(c_int32)]
+                L.hofa_prefill_read_status.restype = ctypes.c_int
+                L.hofa_prefill_read_status.argtypes = [c_void_p, ctypes.POINTER(c_int32)]
                 L.hofa_gla_workspace_size.restype = c_size_t
                 L.hofa_gla_workspace_size.argtypes = [c_int32] * 7
                 if L.hofa_abi_version() != 1:

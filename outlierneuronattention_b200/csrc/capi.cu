@@ -8,6 +8,7 @@
 
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 
@@ -16,6 +17,7 @@
 
 namespace hofa {
 int gla_internal_chunk(int D);
+cudaError_t read_outlier_tc_status(int* out, cudaStream_t st);
 cudaError_t launch_outlier_generic(const OutlierParams& p, int dtype, cudaStream_t st);
 cudaError_t launch_outlier_tc(const OutlierParams& p, int dtype, cudaStream_t st, bool* taken);
 }  // namespace hofa
@@ -123,9 +125,15 @@ int num_sms() {
   return g_num_sms[dev];
 }
 
+bool getenv_flag(const char* name) {
+  const char* v = getenv(name);
+  return v != nullptr && v[0] != '\0' && v[0] != '0';
+}
+
 bool supported_d(int64_t D) { return D == 32 || D == 64 || D == 128; }
 
 constexpr int kMaxSplit = 64;
+constexpr int kAutoSplitMax = 16;
 constexpr int kMaxSegments = 64;
 
 size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -143,11 +151,13 @@ int32_t hofa_abi_version(void) { return HOFA_ABI_VERSION; }
 int32_t hofa_decode_choose_split(int32_t B, int32_t H, int32_t seq_len, int32_t sms) {
   if (B <= 0 || H <= 0) return 1;
   if (sms <= 0) sms = 148;
+  // one wave of the cache-streaming kernel (two CTAs per SM), at most 16
+  // splits (one thread-block cluster per head), at least 256 tokens a split
   const int64_t heads = (int64_t)B * H;
-  int64_t s = (2 * (int64_t)sms + heads - 1) / heads;
+  int64_t s = (2 * (int64_t)sms) / heads;
   const int64_t by_len = seq_len / 256 > 1 ? seq_len / 256 : 1;
   if (s > by_len) s = by_len;
-  if (s > kMaxSplit) s = kMaxSplit;
+  if (s > kAutoSplitMax) s = kAutoSplitMax;
   if (s < 1) s = 1;
   return (int32_t)s;
 }
@@ -268,7 +278,10 @@ int hofa_decode_fwd(const hofa_decode_args* a, void* stream) {
       for (int i = 0; i < 3; ++i) vec = vec && ((c->stride[i] * es) % 16 == 0 || c->shape[i] == 1);
     }
   }
-  cudaError_t e = hofa::launch_decode(p, dt, vec, alpha, reinterpret_cast<cudaStream_t>(stream));
+  // TMA bulk path: additionally, every (b,h) slab of cache rows is contiguous
+  const bool bulk = vec && a->cache_k.stride[2] == R && a->cache_v.stride[2] == D && !getenv_flag("HOFA_DECODE_NO_BULK");
+  const int path = bulk ? 2 : (vec ? 1 : 0);
+  cudaError_t e = hofa::launch_decode(p, dt, path, alpha, reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "hofa_decode_fwd launch");
   return HOFA_OK;
 }
@@ -420,6 +433,15 @@ int hofa_prefill_outlier_fwd(const hofa_outlier_args* a, void* stream) {
   cudaError_t e = hofa::launch_outlier_tc(p, dt, st, &taken);
   if (!taken) e = hofa::launch_outlier_generic(p, dt, st);
   if (e != cudaSuccess) return cuda_fail(e, "hofa_prefill_outlier_fwd launch");
+  return HOFA_OK;
+}
+
+int hofa_prefill_read_status(void* stream, int32_t* status_out) {
+  if (status_out == nullptr) return fail(HOFA_ERR_INVALID_ARGUMENT, "NULL argument");
+  int v = 0;
+  cudaError_t e = hofa::read_outlier_tc_status(&v, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "hofa_prefill_read_status");
+  *status_out = v;
   return HOFA_OK;
 }
 

@@ -4,11 +4,10 @@
 // either one (B,H) Triton program per head or a split kernel (B,H,split_k)
 // plus a reduce kernel (B,H).  Here one grid (split_k, H, B) does everything:
 //
-//   * every CTA streams a contiguous slice of the (b,h) outlier cache
-//     (K rows of R channels, V rows of D channels) with 16-byte loads: a warp
-//     scores 32 tokens at a time (lane t owns token t's key row), keeps a
-//     running softmax (max, sum) and accumulates p*V with each lane owning
-//     8 value channels of a few tokens;
+//   * every CTA streams a contiguous slice of the (b,h) outlier cache (K rows
+//     of R channels, V rows of D channels).  A warp scores 32 tokens at a time
+//     (lane t owns token t's key row), keeps a running softmax (max, sum) and
+//     accumulates p*V with each lane owning 8 value channels of a few tokens;
 //   * the same CTA updates its share of the GLA state rows
 //     (S' = gamma*S + k_I v^T, written to state_out) and the matching part of
 //     the inclusive readout y_I = q_I S';
@@ -16,124 +15,71 @@
 //     (b,h) to arrive (atomic ticket, no spin-wait) combines them, applies
 //     RMSNorm * gla_scale and the blend mix*y_O + (1-mix)*y_I_norm, writes Y
 //     and re-arms the ticket for the next launch.
+//
+// Two cache-streaming variants share that structure:
+//   decode_bulk_kernel  -- cache rows contiguous in memory (the layer's
+//       pre-allocated [B,H,L,*] caches): a producer warp streams 64-token
+//       chunks with 1-D TMA bulk copies (cp.async.bulk) into an 8-stage
+//       shared-memory ring guarded by mbarriers, four consumer warps reduce
+//       them; up to 80 KB per CTA is in flight.  The splits of a head run as
+//       one thread-block cluster and combine through distributed shared
+//       memory.
+//   decode_reg_kernel   -- any strides: 16-byte (or scalar) register loads.
 #include <float.h>
+
+#include <cooperative_groups.h>
 
 #include "common.cuh"
 #include "kernels.h"
+#include "sm100.cuh"
+
+namespace cg = cooperative_groups;
 
 namespace hofa {
 
 namespace {
 
-constexpr int kDecThreads = 128;
-constexpr int kDecWarps = kDecThreads / 32;
+constexpr int kConsumerWarps = 4;
+constexpr int kConsumers = kConsumerWarps * 32;
+constexpr int kChunk = 32;           // tokens per warp tile
+constexpr int kMaxClusterSplit = 16;  // splits combined through a thread-block cluster
 
-template <typename T, int D, bool VEC, bool ALPHA>
-__global__ void __launch_bounds__(kDecThreads)
-decode_kernel(const DecodeParams p) {
-  constexpr int G = D / 8;        // 8-channel groups in one V row
-  constexpr int TS = 32 / G;      // tokens covered by one warp-wide V load
-  constexpr int VI = 32 / TS;     // V loads per lane for a 32-token tile
-  constexpr int D4 = D / 4;       // float4 per state row
-  constexpr int RSUB = kDecThreads / D4;
+struct DecShared {
+  float m[kConsumerWarps], l[kConsumerWarps];
+  float red[8];
+  int last;
+};
 
-  const int s = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int R = p.R, J = D - p.R;
-  const int bh = b * p.H + h;
-
-  __shared__ float sm_m[kDecWarps], sm_l[kDecWarps];
-  __shared__ __align__(16) float sm_acc[kDecWarps][D];
-  __shared__ __align__(16) float sm_y[RSUB][D];
-  __shared__ float sm_red[kDecWarps];
-  __shared__ __align__(16) float sm_q[D];
-  __shared__ int sm_last;
-
-  // ---------------- outlier softmax over this CTA's cache slice ----------
-  int seq_len = p.seq_len;
-  if (p.seq_len_dev != nullptr) {
-    seq_len = *p.seq_len_dev;
-    if (seq_len < 1 || seq_len > p.L) {
-      if (s == 0 && tid == 0) atomicExch(p.ws_status, 1);
-      seq_len = seq_len < 1 ? 1 : p.L;
-    }
+// Online-softmax update of one warp with a 32-token tile: `sc` is this
+// lane's score (log2 domain, -inf when invalid); vr[i] holds V channels
+// [8cg, 8cg+8) of token i*TS+ts of the tile.
+template <typename T, int D>
+__device__ __forceinline__ void tile_update(float sc, const Vec8<T> (&vr)[D / 8], float& m_run, float& l_run,
+                                            float (&acc)[8], int ts) {
+  constexpr int G = D / 8, TS = 32 / G, VI = 32 / TS;
+  const float mt = warp_max(sc);
+  const float mn = fmaxf(m_run, mt);
+  const float corr = exp2f(m_run - mn);
+  const float pl = exp2f(sc - mn);
+  l_run = l_run * corr + pl;
+#pragma unroll
+  for (int c = 0; c < 8; ++c) acc[c] *= corr;
+#pragma unroll
+  for (int i = 0; i < VI; ++i) {
+    const float pi = __shfl_sync(0xffffffffu, pl, i * TS + ts);
+    float f[8];
+    vec8_to_f(vr[i], f);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) acc[c] = fmaf(pi, f[c], acc[c]);
   }
-  if (R == 0) seq_len = 0;
-  int tps = (seq_len + p.split_k - 1) / p.split_k;
-  tps = (tps + 31) & ~31;
-  const int t_begin = s * tps;
-  const int t_end = min(seq_len, t_begin + tps);
+  m_run = mn;
+}
 
-  // q_O pre-scaled to the base-2 logit domain; read by every lane (broadcast)
-  if (tid < D) {
-    sm_q[tid] = (tid < R) ? to_f(reinterpret_cast<const T*>(p.q)[b * p.sq[0] + h * p.sq[1] + tid * p.sq[2]]) *
-                                p.qk_scale_log2
-                          : 0.f;
-  }
-  __syncthreads();
-
-  const int cg = lane % G, ts = lane / G;
-  float m_run = -INFINITY, l_run = 0.f;
-  float acc[8];
-#pragma unroll
-  for (int c = 0; c < 8; ++c) acc[c] = 0.f;
-
-  const T* kb = reinterpret_cast<const T*>(p.cache_k) + b * p.sck[0] + h * p.sck[1];
-  const T* vb = reinterpret_cast<const T*>(p.cache_v) + b * p.scv[0] + h * p.scv[1];
-
-  for (int t0 = t_begin + warp * 32; t0 < t_end; t0 += kDecWarps * 32) {
-    const int t = t0 + lane;
-    const bool valid = t < t_end;
-    // value loads first: they do not depend on the scores
-    Vec8<T> vr[VI];
-#pragma unroll
-    for (int i = 0; i < VI; ++i) {
-      const int tv = t0 + i * TS + ts;
-      if (tv < t_end) {
-        if constexpr (VEC) vr[i] = ld_vec8<T>(vb + (int64_t)tv * p.scv[2] + cg * 8);
-        else vr[i] = ld_strided8<T>(vb + (int64_t)tv * p.scv[2] + (int64_t)cg * 8 * p.scv[3], p.scv[3]);
-      } else {
-        vr[i] = zero_vec8<T>();
-      }
-    }
-    float sc = -INFINITY;
-    if (valid) {
-      float dot = 0.f;
-      if constexpr (VEC) {
-#pragma unroll
-        for (int g = 0; g < G; ++g) {
-          if (g * 8 < R) {
-            float f[8];
-            vec8_to_f(ld_vec8<T>(kb + (int64_t)t * p.sck[2] + g * 8), f);
-#pragma unroll
-            for (int c = 0; c < 8; ++c) dot = fmaf(sm_q[g * 8 + c], f[c], dot);
-          }
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < D; ++c)
-          if (c < R) dot = fmaf(sm_q[c], to_f(kb[(int64_t)t * p.sck[2] + (int64_t)c * p.sck[3]]), dot);
-      }
-      sc = dot;
-    }
-    const float mt = warp_max(sc);
-    const float mn = fmaxf(m_run, mt);
-    const float corr = exp2f(m_run - mn);
-    const float pl = exp2f(sc - mn);
-    l_run = l_run * corr + pl;
-#pragma unroll
-    for (int c = 0; c < 8; ++c) acc[c] *= corr;
-#pragma unroll
-    for (int i = 0; i < VI; ++i) {
-      const float pi = __shfl_sync(0xffffffffu, pl, i * TS + ts);
-      float f[8];
-      vec8_to_f(vr[i], f);
-#pragma unroll
-      for (int c = 0; c < 8; ++c) acc[c] = fmaf(pi, f[c], acc[c]);
-    }
-    m_run = mn;
-  }
-  // lanes sharing a channel group hold disjoint tokens: sum them
+// Warp result -> shared (acc summed over the lanes that share a channel group).
+template <int D>
+__device__ __forceinline__ void warp_flush(float m_run, float l_run, float (&acc)[8], int lane, int warp,
+                                          DecShared& sh, float (*sm_acc)[D]) {
+  constexpr int G = D / 8;
 #pragma unroll
   for (int o = G; o < 32; o <<= 1) {
 #pragma unroll
@@ -144,12 +90,19 @@ decode_kernel(const DecodeParams p) {
 #pragma unroll
     for (int c = 0; c < 8; ++c) sm_acc[warp][lane * 8 + c] = acc[c];
   }
-  if (lane == 0) { sm_m[warp] = m_run; sm_l[warp] = l_run; }
+  if (lane == 0) { sh.m[warp] = m_run; sh.l[warp] = l_run; }
+}
 
-  // ---------------- GLA rows owned by this split --------------------------
+// GLA rows [r0, r1) of (b,h): S' = gamma*S + k_I v^T -> state_out, and this
+// split's part of y_I = q_I S' -> sm_y (one row of partial sums per thread group).
+template <typename T, int D, bool ALPHA>
+__device__ __forceinline__ void gla_rows(const DecodeParams& p, int s, int b, int h, int tid, float (*sm_y)[D]) {
+  constexpr int D4 = D / 4;
+  const int R = p.R, J = D - p.R;
   const int rows_per = (J + p.split_k - 1) / p.split_k;
   const int r0 = s * rows_per, r1 = min(J, r0 + rows_per);
   const int c4 = tid % D4, rsub = tid / D4;
+  constexpr int RSUB = kConsumers / D4;
   float ya[4] = {0.f, 0.f, 0.f, 0.f};
   if (r0 < r1) {
     const T* qp = reinterpret_cast<const T*>(p.q) + b * p.sq[0] + h * p.sq[1];
@@ -166,8 +119,9 @@ decode_kernel(const DecodeParams p) {
       const float kr = to_f(kp[(int64_t)(R + row) * p.sk[2]]);
       const float qr = to_f(qp[(int64_t)(R + row) * p.sq[2]]);
       float gam = gam_h;
-      if constexpr (ALPHA) gam = expf(lg * expf(ld_any(p.log_alpha, p.dt_la, b * p.sla[0] + h * p.sla[1] + row * p.sla[2])));
-      const float4 s4 = *reinterpret_cast<const float4*>(sin_ + (int64_t)row * p.sst[2] + 4 * c4);
+      if constexpr (ALPHA)
+        gam = expf(lg * expf(ld_any(p.log_alpha, p.dt_la, b * p.sla[0] + h * p.sla[1] + row * p.sla[2])));
+      const float4 s4 = __ldg(reinterpret_cast<const float4*>(sin_ + (int64_t)row * p.sst[2] + 4 * c4));
       float4 n4;
       n4.x = fmaf(gam, s4.x, kr * v4[0]);
       n4.y = fmaf(gam, s4.y, kr * v4[1]);
@@ -182,18 +136,33 @@ decode_kernel(const DecodeParams p) {
   }
 #pragma unroll
   for (int c = 0; c < 4; ++c) sm_y[rsub][4 * c4 + c] = ya[c];
-  __syncthreads();
+}
 
-  // ---------------- CTA partial: (m, l, acc[D], y_I[D]) -------------------
+// CTA partial (m, l, acc[D], y_I[D]), cross-split combine, RMSNorm, blend,
+// store.  Called by every thread of the CTA after a __syncthreads() that
+// publishes sh / sm_acc / sm_y.  The splits of one (b,h) combine either
+//   CLUSTER: the split CTAs of a head form one thread-block cluster; each
+//            leaves its partial in shared memory, rank 0 reads the peers'
+//            partials through distributed shared memory (no global round
+//            trip, no fences, no atomics), or
+//   workspace: partials go to global memory and the last CTA to take a
+//            ticket combines them (any split count).
+template <typename T, int D, bool CLUSTER>
+__device__ __forceinline__ void finish(const DecodeParams& p, int s, int b, int h, int tid, int lane, int warp,
+                                       int nwarps, DecShared& sh, float (*sm_acc)[D], float (*sm_y)[D],
+                                       float* sm_part) {
+  constexpr int RSUB = kConsumers / (D / 4);
+  constexpr int PS = 4 + 2 * D;
+  const int bh = b * p.H + h;
   float cta_m = -INFINITY;
 #pragma unroll
-  for (int w = 0; w < kDecWarps; ++w) cta_m = fmaxf(cta_m, sm_m[w]);
+  for (int w = 0; w < kConsumerWarps; ++w) cta_m = fmaxf(cta_m, sh.m[w]);
   float cta_l = 0.f, part_acc = 0.f, part_y = 0.f;
   const int d = tid;
 #pragma unroll
-  for (int w = 0; w < kDecWarps; ++w) {
-    const float wgt = (sm_m[w] == -INFINITY) ? 0.f : exp2f(sm_m[w] - cta_m);
-    cta_l += sm_l[w] * wgt;
+  for (int w = 0; w < kConsumerWarps; ++w) {
+    const float wgt = (sh.m[w] == -INFINITY) ? 0.f : exp2f(sh.m[w] - cta_m);
+    cta_l += sh.l[w] * wgt;
     if (d < D) part_acc += sm_acc[w][d] * wgt;
   }
   if (d < D) {
@@ -201,11 +170,34 @@ decode_kernel(const DecodeParams p) {
     for (int rr = 0; rr < RSUB; ++rr) part_y += sm_y[rr][d];
   }
 
-  float fin_acc, fin_l, fin_y, fin_m;
+  float fin_acc, fin_l, fin_y;
   if (p.split_k == 1) {
-    fin_acc = part_acc; fin_l = cta_l; fin_y = part_y; fin_m = cta_m;
+    fin_acc = part_acc; fin_l = cta_l; fin_y = part_y;
+  } else if constexpr (CLUSTER) {
+    if (tid == 0) { sm_part[0] = cta_m; sm_part[1] = cta_l; }
+    if (d < D) { sm_part[4 + d] = part_acc; sm_part[4 + D + d] = part_y; }
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    const bool leader = cluster.block_rank() == 0;
+    if (leader) {
+      float M = -INFINITY;
+      for (int q = 0; q < p.split_k; ++q) M = fmaxf(M, *cluster.map_shared_rank(sm_part, q));
+      fin_acc = 0.f; fin_l = 0.f; fin_y = 0.f;
+#pragma unroll 4
+      for (int q = 0; q < p.split_k; ++q) {
+        const float* peer = cluster.map_shared_rank(sm_part, q);
+        const float mq = peer[0];
+        const float wgt = (mq == -INFINITY) ? 0.f : exp2f(mq - M);
+        fin_l += peer[1] * wgt;
+        if (d < D) {
+          fin_acc += peer[4 + d] * wgt;
+          fin_y += peer[4 + D + d];
+        }
+      }
+    }
+    cluster.sync();  // peers keep their shared memory alive until the leader has read it
+    if (!leader) return;
   } else {
-    const int PS = 4 + 2 * D;
     float* part = p.ws_part + ((int64_t)bh * p.split_k + s) * PS;
     if (tid == 0) { part[0] = cta_m; part[1] = cta_l; }
     if (d < D) { part[4 + d] = part_acc; part[4 + D + d] = part_y; }
@@ -213,15 +205,17 @@ decode_kernel(const DecodeParams p) {
     __syncthreads();
     if (tid == 0) {
       const int prev = atomicAdd(p.ws_count + bh, 1);
-      sm_last = (prev == p.split_k - 1);
+      sh.last = (prev == p.split_k - 1);
     }
     __syncthreads();
-    if (!sm_last) return;
+    if (!sh.last) return;
     __threadfence();
     const float* all = p.ws_part + (int64_t)bh * p.split_k * PS;
     float M = -INFINITY;
+#pragma unroll 8
     for (int q = 0; q < p.split_k; ++q) M = fmaxf(M, __ldcg(all + q * PS));
-    fin_acc = 0.f; fin_l = 0.f; fin_y = 0.f; fin_m = M;
+    fin_acc = 0.f; fin_l = 0.f; fin_y = 0.f;
+#pragma unroll 8
     for (int q = 0; q < p.split_k; ++q) {
       const float mq = __ldcg(all + q * PS);
       const float wgt = (mq == -INFINITY) ? 0.f : exp2f(mq - M);
@@ -233,16 +227,13 @@ decode_kernel(const DecodeParams p) {
     }
     if (tid == 0) p.ws_count[bh] = 0;  // re-arm the ticket for the next launch
   }
-  (void)fin_m;
 
-  // ---------------- RMSNorm(y_I) * gla_scale, blend, store ---------------
   float sq = (d < D) ? fin_y * fin_y : 0.f;
   sq = warp_sum(sq);
-  if (lane == 0) sm_red[warp] = sq;
+  if (lane == 0) sh.red[warp] = sq;
   __syncthreads();
   float ss = 0.f;
-#pragma unroll
-  for (int w = 0; w < kDecWarps; ++w) ss += sm_red[w];
+  for (int w = 0; w < nwarps; ++w) ss += sh.red[w];
   if (d < D) {
     const float rs = rsqrtf(ss / (float)D + p.eps);
     const float nw = ld_any(p.norm_w, p.dt_nw, h * p.snw[0] + d * p.snw[1]);
@@ -253,36 +244,278 @@ decode_kernel(const DecodeParams p) {
   }
 }
 
+__device__ __forceinline__ int resolve_seq_len(const DecodeParams& p, int s, int tid) {
+  int seq_len = p.seq_len;
+  if (p.seq_len_dev != nullptr) {
+    seq_len = *p.seq_len_dev;
+    if (seq_len < 1 || seq_len > p.L) {
+      if (s == 0 && tid == 0) atomicOr(p.ws_status, 1);
+      seq_len = seq_len < 1 ? 1 : p.L;
+    }
+  }
+  return p.R == 0 ? 0 : seq_len;
+}
+
 template <typename T, int D>
-cudaError_t launch_d(const DecodeParams& p, bool vec, bool alpha, cudaStream_t st) {
-  dim3 grid(p.split_k, p.H, p.B);
-  if (vec) {
-    if (alpha) decode_kernel<T, D, true, true><<<grid, kDecThreads, 0, st>>>(p);
-    else decode_kernel<T, D, true, false><<<grid, kDecThreads, 0, st>>>(p);
+__device__ __forceinline__ void load_q(const DecodeParams& p, int b, int h, int tid, float* sm_q) {
+  if (tid < D) {
+    sm_q[tid] = (tid < p.R) ? to_f(reinterpret_cast<const T*>(p.q)[b * p.sq[0] + h * p.sq[1] + tid * p.sq[2]]) *
+                                  p.qk_scale_log2
+                            : 0.f;
+  }
+}
+
+// ============================================================================
+// Register-load variant (any strides).
+// ============================================================================
+template <typename T, int D, bool VEC, bool ALPHA>
+__global__ void __launch_bounds__(kConsumers)
+decode_reg_kernel(const DecodeParams p) {
+  constexpr int G = D / 8, TS = 32 / G, VI = 32 / TS;
+  constexpr int RSUB = kConsumers / (D / 4);
+  const int s = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int R = p.R;
+
+  __shared__ DecShared sh;
+  __shared__ __align__(16) float sm_acc[kConsumerWarps][D];
+  __shared__ __align__(16) float sm_y[RSUB][D];
+  __shared__ __align__(16) float sm_q[D];
+
+  const int seq_len = resolve_seq_len(p, s, tid);
+  int tps = (seq_len + p.split_k - 1) / p.split_k;
+  tps = (tps + kChunk - 1) & ~(kChunk - 1);
+  const int t_begin = s * tps;
+  const int t_end = min(seq_len, t_begin + tps);
+  load_q<T, D>(p, b, h, tid, sm_q);
+  __syncthreads();
+
+  const int cg = lane % G, ts = lane / G;
+  float m_run = -INFINITY, l_run = 0.f;
+  float acc[8];
+#pragma unroll
+  for (int c = 0; c < 8; ++c) acc[c] = 0.f;
+  const T* kb = reinterpret_cast<const T*>(p.cache_k) + b * p.sck[0] + h * p.sck[1];
+  const T* vb = reinterpret_cast<const T*>(p.cache_v) + b * p.scv[0] + h * p.scv[1];
+
+  for (int t0 = t_begin + warp * kChunk; t0 < t_end; t0 += kConsumerWarps * kChunk) {
+    const int t = t0 + lane;
+    Vec8<T> vr[VI];
+#pragma unroll
+    for (int i = 0; i < VI; ++i) {
+      const int tv = t0 + i * TS + ts;
+      if (tv < t_end) {
+        if constexpr (VEC) vr[i] = ld_vec8<T>(vb + (int64_t)tv * p.scv[2] + cg * 8);
+        else vr[i] = ld_strided8<T>(vb + (int64_t)tv * p.scv[2] + (int64_t)cg * 8 * p.scv[3], p.scv[3]);
+      } else {
+        vr[i] = zero_vec8<T>();
+      }
+    }
+    float sc = -INFINITY;
+    if (t < t_end) {
+      float dot = 0.f;
+      if constexpr (VEC) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          if (g * 8 < R) {
+            float f[8];
+            vec8_to_f(ld_vec8<T>(kb + (int64_t)t * p.sck[2] + g * 8), f);
+#pragma unroll
+            for (int c = 0; c < 8; ++c) dot = fmaf(sm_q[g * 8 + c], f[c], dot);
+          }
+        }
+      } else {
+        for (int c = 0; c < R; ++c) dot = fmaf(sm_q[c], to_f(kb[(int64_t)t * p.sck[2] + (int64_t)c * p.sck[3]]), dot);
+      }
+      sc = dot;
+    }
+    tile_update<T, D>(sc, vr, m_run, l_run, acc, ts);
+  }
+  warp_flush<D>(m_run, l_run, acc, lane, warp, sh, sm_acc);
+  gla_rows<T, D, ALPHA>(p, s, b, h, tid, sm_y);
+  __syncthreads();
+  finish<T, D, false>(p, s, b, h, tid, lane, warp, kConsumerWarps, sh, sm_acc, sm_y, nullptr);
+}
+
+// ============================================================================
+// TMA-bulk variant (cache rows contiguous: row stride R for K, D for V).
+// ============================================================================
+constexpr int kBulkChunk = 64;  // tokens per bulk chunk (two warp tiles)
+template <typename T>
+constexpr int bulk_stages() { return sizeof(T) == 4 ? 4 : 8; }
+
+template <typename T, int D, bool ALPHA, bool CLUSTER>
+__global__ void __launch_bounds__(kConsumers + 32)
+decode_bulk_kernel(const DecodeParams p) {
+  constexpr int G = D / 8, TS = 32 / G, VI = 32 / TS;
+  constexpr int RSUB = kConsumers / (D / 4);
+  constexpr int NST = bulk_stages<T>();
+  const int s = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int R = p.R;
+
+  __shared__ DecShared sh;
+  __shared__ __align__(16) float sm_acc[kConsumerWarps][D];
+  __shared__ __align__(16) float sm_y[RSUB][D];
+  __shared__ __align__(16) float sm_q[D];
+  __shared__ __align__(16) float sm_part[4 + 2 * D];
+  __shared__ __align__(8) uint64_t full_bar[NST], empty_bar[NST];
+  __shared__ int sm_err;
+  extern __shared__ __align__(128) unsigned char ring[];  // [NST][chunk*R] K, then [NST][chunk*D] V
+  T* sK = reinterpret_cast<T*>(ring);
+  T* sV = reinterpret_cast<T*>(ring + (size_t)NST * kBulkChunk * R * sizeof(T));
+
+  const int seq_len = resolve_seq_len(p, s, tid);
+  int tps = (seq_len + p.split_k - 1) / p.split_k;
+  tps = (tps + kBulkChunk - 1) & ~(kBulkChunk - 1);
+  const int t_begin = s * tps;
+  const int t_end = min(seq_len, t_begin + tps);
+  const int nchunks = t_end > t_begin ? (t_end - t_begin + kBulkChunk - 1) / kBulkChunk : 0;
+
+  if (tid == 0) {
+    for (int i = 0; i < NST; ++i) {
+      sm100::mbar_init(&full_bar[i], 1);
+      sm100::mbar_init(&empty_bar[i], 1);
+    }
+    sm_err = 0;
+    sm100::fence_mbar_init();
+  }
+  load_q<T, D>(p, b, h, tid, sm_q);
+  __syncthreads();
+
+  float m_run = -INFINITY, l_run = 0.f;
+  float acc[8];
+#pragma unroll
+  for (int c = 0; c < 8; ++c) acc[c] = 0.f;
+
+  if (warp == kConsumerWarps) {
+    // ---------------- producer: stream chunks into the ring ----------------
+    if (lane == 0) {
+      const char* kg = reinterpret_cast<const char*>(p.cache_k) + (b * p.sck[0] + h * p.sck[1]) * sizeof(T);
+      const char* vg = reinterpret_cast<const char*>(p.cache_v) + (b * p.scv[0] + h * p.scv[1]) * sizeof(T);
+      for (int c = 0; c < nchunks; ++c) {
+        const int st = c % NST;
+        if (c >= NST && !sm_err && !sm100::mbar_wait(&empty_bar[st], ((c / NST) - 1) & 1)) atomicOr(&sm_err, 1);
+        if (sm_err) break;
+        const int t0 = t_begin + c * kBulkChunk;
+        const int n = min(kBulkChunk, t_end - t0);
+        const uint32_t kbytes = (uint32_t)(n * R * sizeof(T)), vbytes = (uint32_t)(n * D * sizeof(T));
+        sm100::mbar_arrive_expect_tx(&full_bar[st], kbytes + vbytes);
+        sm100::bulk_g2s(sK + (size_t)st * kBulkChunk * R, kg + (size_t)t0 * R * sizeof(T), kbytes, &full_bar[st]);
+        sm100::bulk_g2s(sV + (size_t)st * kBulkChunk * D, vg + (size_t)t0 * D * sizeof(T), vbytes, &full_bar[st]);
+      }
+    }
   } else {
-    if (alpha) decode_kernel<T, D, false, true><<<grid, kDecThreads, 0, st>>>(p);
-    else decode_kernel<T, D, false, false><<<grid, kDecThreads, 0, st>>>(p);
+    // ---------------- consumers: GLA rows first (overlaps the first copies) -
+    gla_rows<T, D, ALPHA>(p, s, b, h, tid, sm_y);
+    const int cg_ = lane % G, ts = lane / G;
+    volatile int* verr = &sm_err;
+    for (int c = warp; c < nchunks; c += kConsumerWarps) {
+      const int st = c % NST;
+      if (!*verr && !sm100::mbar_wait(&full_bar[st], (c / NST) & 1)) atomicOr(&sm_err, 2);
+      const int t0 = t_begin + c * kBulkChunk;
+      const int n = min(kBulkChunk, t_end - t0);
+      const T* kc = sK + (size_t)st * kBulkChunk * R;
+      const T* vc = sV + (size_t)st * kBulkChunk * D;
+#pragma unroll
+      for (int sub = 0; sub < kBulkChunk / kChunk; ++sub) {
+        const int base = sub * kChunk;
+        Vec8<T> vr[VI];
+#pragma unroll
+        for (int i = 0; i < VI; ++i) {
+          const int tl = base + i * TS + ts;
+          vr[i] = tl < n ? *reinterpret_cast<const Vec8<T>*>(vc + tl * D + cg_ * 8) : zero_vec8<T>();
+        }
+        float sc = -INFINITY;
+        if (base + lane < n) {
+          float dot = 0.f;
+#pragma unroll
+          for (int g = 0; g < G; ++g) {
+            if (g * 8 < R) {
+              float f[8];
+              vec8_to_f(*reinterpret_cast<const Vec8<T>*>(kc + (base + lane) * R + g * 8), f);
+#pragma unroll
+              for (int cc = 0; cc < 8; ++cc) dot = fmaf(sm_q[g * 8 + cc], f[cc], dot);
+            }
+          }
+          sc = dot;
+        }
+        if (base < n) tile_update<T, D>(sc, vr, m_run, l_run, acc, ts);  // consumes every value read
+      }
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(&empty_bar[st]);
+    }
+    warp_flush<D>(m_run, l_run, acc, lane, warp, sh, sm_acc);
+  }
+  __syncthreads();
+  if (tid == 0 && sm_err) atomicOr(p.ws_status, 4 * sm_err);
+  finish<T, D, CLUSTER>(p, s, b, h, tid, lane, warp, kConsumerWarps + 1, sh, sm_acc, sm_y, sm_part);
+}
+
+template <typename T, int D, bool ALPHA, bool CLUSTER>
+cudaError_t launch_bulk(const DecodeParams& p, cudaStream_t st) {
+  const size_t smem = (size_t)bulk_stages<T>() * kBulkChunk * (p.R + D) * sizeof(T);
+  auto k = decode_bulk_kernel<T, D, ALPHA, CLUSTER>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(p.split_k, p.H, p.B);
+  cfg.blockDim = dim3(kConsumers + 32);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  if (CLUSTER) {
+    if (p.split_k > 8) {
+      e = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+      if (e != cudaSuccess) return e;
+    }
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = p.split_k;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+  }
+  e = cudaLaunchKernelEx(&cfg, k, p);
+  if (e != cudaSuccess) return e;
+  return cudaGetLastError();
+}
+
+template <typename T, int D>
+cudaError_t launch_d(const DecodeParams& p, int path, bool alpha, cudaStream_t st) {
+  dim3 grid(p.split_k, p.H, p.B);
+  if (path == 2) {
+    const bool cluster = p.split_k > 1 && p.split_k <= kMaxClusterSplit;
+    if (cluster) return alpha ? launch_bulk<T, D, true, true>(p, st) : launch_bulk<T, D, false, true>(p, st);
+    return alpha ? launch_bulk<T, D, true, false>(p, st) : launch_bulk<T, D, false, false>(p, st);
+  } else if (path == 1) {
+    if (alpha) decode_reg_kernel<T, D, true, true><<<grid, kConsumers, 0, st>>>(p);
+    else decode_reg_kernel<T, D, true, false><<<grid, kConsumers, 0, st>>>(p);
+  } else {
+    if (alpha) decode_reg_kernel<T, D, false, true><<<grid, kConsumers, 0, st>>>(p);
+    else decode_reg_kernel<T, D, false, false><<<grid, kConsumers, 0, st>>>(p);
   }
   return cudaGetLastError();
 }
 
 template <typename T>
-cudaError_t launch_t(const DecodeParams& p, bool vec, bool alpha, cudaStream_t st) {
+cudaError_t launch_t(const DecodeParams& p, int path, bool alpha, cudaStream_t st) {
   switch (p.D) {
-    case 32: return launch_d<T, 32>(p, vec, alpha, st);
-    case 64: return launch_d<T, 64>(p, vec, alpha, st);
-    case 128: return launch_d<T, 128>(p, vec, alpha, st);
+    case 32: return launch_d<T, 32>(p, path, alpha, st);
+    case 64: return launch_d<T, 64>(p, path, alpha, st);
+    case 128: return launch_d<T, 128>(p, path, alpha, st);
     default: return cudaErrorInvalidValue;
   }
 }
 
 }  // namespace
 
-cudaError_t launch_decode(const DecodeParams& p, int dtype, bool vec, bool alpha, cudaStream_t st) {
+// path: 0 = strided register loads, 1 = 16-byte register loads, 2 = TMA bulk ring
+cudaError_t launch_decode(const DecodeParams& p, int dtype, int path, bool alpha, cudaStream_t st) {
   switch (dtype) {
-    case HOFA_DTYPE_BF16: return launch_t<__nv_bfloat16>(p, vec, alpha, st);
-    case HOFA_DTYPE_F16: return launch_t<__half>(p, vec, alpha, st);
-    default: return launch_t<float>(p, vec, alpha, st);
+    case HOFA_DTYPE_BF16: return launch_t<__nv_bfloat16>(p, path, alpha, st);
+    case HOFA_DTYPE_F16: return launch_t<__half>(p, path, alpha, st);
+    default: return launch_t<float>(p, path, alpha, st);
   }
 }
 

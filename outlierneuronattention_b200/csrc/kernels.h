@@ -32,7 +32,8 @@ struct DecodeParams {
   int* ws_status;
 };
 
-cudaError_t launch_decode(const DecodeParams& p, int dtype, bool vec, bool alpha, cudaStream_t st);
+// path: 0 = strided register loads, 1 = 16-byte register loads, 2 = TMA bulk ring
+cudaError_t launch_decode(const DecodeParams& p, int dtype, int path, bool alpha, cudaStream_t st);
 
 struct GlaParams {
   const void* q; const void* k; const void* v;

@@ -155,3 +155,39 @@ def test_config2_full_size_sampled_heads():
             ref = outlier_attention_core(qs, sl(k), sl(v), r, 2.0, sl(mix)[:, :, q0:q0 + 128],
                                          out=sl(Y_gla)[:, :, q0:q0 + 128], q_offset=q0)
             assert maxabs(sl(Y)[:, :, q0:q0 + 128], ref) <= 2e-2
+
+
+def _prefill_status():
+    import ctypes
+    from outlierneuronattention_b200 import _capi
+    v = ctypes.c_int32(0)
+    assert _capi.lib().hofa_prefill_read_status(_capi.stream_handle(torch.device("cuda")), ctypes.byref(v)) == 0
+    return v.value
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("B,H,T,D,r,qoff", [(1, 1, 128, 64, 16, 0), (2, 3, 1000, 64, 16, 0), (1, 2, 129, 64, 16, 0),
+                                            (1, 2, 300, 128, 32, 0), (1, 2, 256, 64, 64, 0), (1, 2, 200, 64, 16, 77),
+                                            (2, 2, 257, 128, 16, 0)])
+def test_outlier_tensor_core_path(monkeypatch, dtype, B, H, T, D, r, qoff):
+    """The tcgen05 kernel (bf16/f16, D in {64,128}, r in {16,32,64}) and the
+    CUDA-core kernel agree with the oracle on the same inputs; the tensor-core
+    kernel's bounded waits never ran out."""
+    from outlierneuronattention_b200 import exact_attention_triton
+    q, k, v, _, mix, _ = rand_qkv(B, H, T, D, dtype, seed=T + D + r, scale=1.0)
+    qs, ms = q[:, :, qoff:], mix[:, :, qoff:]
+    base = (torch.randn(B, H, T - qoff, D) * 0.1).to(dtype)
+    ref = outlier_attention_core(qs, k, v, r, math.sqrt(D / r), ms, out=base, q_offset=qoff)
+    assert _prefill_status() == 0
+    outs = {}
+    for path in ("tc", "cuda_core"):
+        if path == "cuda_core":
+            monkeypatch.setenv("HOFA_OUTLIER_NO_TC", "1")
+        out = base.cuda().clone()
+        exact_attention_triton(qs.cuda(), k.cuda(), v.cuda(), r, math.sqrt(D / r), ms.cuda(), out=out, q_offset=qoff)
+        torch.cuda.synchronize()
+        outs[path] = out
+        assert maxabs(out, ref) <= 2e-2, path
+    monkeypatch.delenv("HOFA_OUTLIER_NO_TC")
+    assert _prefill_status() == 0
+    assert maxabs(outs["tc"], outs["cuda_core"].cpu()) <= 2e-2
