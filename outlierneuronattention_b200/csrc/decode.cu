@@ -39,14 +39,16 @@ namespace hofa {
 
 namespace {
 
-constexpr int kConsumerWarps = 4;
-constexpr int kConsumers = kConsumerWarps * 32;
+constexpr int kConsumerWarps = 4;              // warps of the register-load kernel; the GLA-row
+constexpr int kConsumers = kConsumerWarps * 32;  // mapping always uses the first 128 threads
+constexpr int kMaxWarps = 8;                     // consumer warps of the bulk kernel (4 or 8)
+constexpr int kMaxStages = 16;
 constexpr int kChunk = 32;           // tokens per warp tile
 constexpr int kMaxClusterSplit = 16;  // splits combined through a thread-block cluster
 
 struct DecShared {
-  float m[kConsumerWarps], l[kConsumerWarps];
-  float red[8];
+  float m[kMaxWarps], l[kMaxWarps];
+  float red[kMaxWarps + 2];
   int last;
 };
 
@@ -147,7 +149,7 @@ __device__ __forceinline__ void gla_rows(const DecodeParams& p, int s, int b, in
 //            trip, no fences, no atomics), or
 //   workspace: partials go to global memory and the last CTA to take a
 //            ticket combines them (any split count).
-template <typename T, int D, bool CLUSTER>
+template <typename T, int D, bool CLUSTER, int NW>
 __device__ __forceinline__ void finish(const DecodeParams& p, int s, int b, int h, int tid, int lane, int warp,
                                        int nwarps, DecShared& sh, float (*sm_acc)[D], float (*sm_y)[D],
                                        float* sm_part) {
@@ -156,11 +158,11 @@ __device__ __forceinline__ void finish(const DecodeParams& p, int s, int b, int 
   const int bh = b * p.H + h;
   float cta_m = -INFINITY;
 #pragma unroll
-  for (int w = 0; w < kConsumerWarps; ++w) cta_m = fmaxf(cta_m, sh.m[w]);
+  for (int w = 0; w < NW; ++w) cta_m = fmaxf(cta_m, sh.m[w]);
   float cta_l = 0.f, part_acc = 0.f, part_y = 0.f;
   const int d = tid;
 #pragma unroll
-  for (int w = 0; w < kConsumerWarps; ++w) {
+  for (int w = 0; w < NW; ++w) {
     const float wgt = (sh.m[w] == -INFINITY) ? 0.f : exp2f(sh.m[w] - cta_m);
     cta_l += sh.l[w] * wgt;
     if (d < D) part_acc += sm_acc[w][d] * wgt;
@@ -334,32 +336,29 @@ decode_reg_kernel(const DecodeParams p) {
   warp_flush<D>(m_run, l_run, acc, lane, warp, sh, sm_acc);
   gla_rows<T, D, ALPHA>(p, s, b, h, tid, sm_y);
   __syncthreads();
-  finish<T, D, false>(p, s, b, h, tid, lane, warp, kConsumerWarps, sh, sm_acc, sm_y, nullptr);
+  finish<T, D, false, kConsumerWarps>(p, s, b, h, tid, lane, warp, kConsumerWarps, sh, sm_acc, sm_y, nullptr);
 }
 
 // ============================================================================
 // TMA-bulk variant (cache rows contiguous: row stride R for K, D for V).
 // ============================================================================
 constexpr int kBulkChunk = 64;  // tokens per bulk chunk (two warp tiles)
-template <typename T>
-constexpr int bulk_stages() { return sizeof(T) == 4 ? 4 : 8; }
-
-template <typename T, int D, bool ALPHA, bool CLUSTER>
-__global__ void __launch_bounds__(kConsumers + 32)
+template <typename T, int D, bool ALPHA, bool CLUSTER, int NW>
+__global__ void __launch_bounds__(NW * 32 + 32)
 decode_bulk_kernel(const DecodeParams p) {
   constexpr int G = D / 8, TS = 32 / G, VI = 32 / TS;
   constexpr int RSUB = kConsumers / (D / 4);
-  constexpr int NST = bulk_stages<T>();
+  const int NST = p.stages;
   const int s = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int R = p.R;
 
   __shared__ DecShared sh;
-  __shared__ __align__(16) float sm_acc[kConsumerWarps][D];
+  __shared__ __align__(16) float sm_acc[NW][D];
   __shared__ __align__(16) float sm_y[RSUB][D];
   __shared__ __align__(16) float sm_q[D];
   __shared__ __align__(16) float sm_part[4 + 2 * D];
-  __shared__ __align__(8) uint64_t full_bar[NST], empty_bar[NST];
+  __shared__ __align__(8) uint64_t full_bar[kMaxStages], empty_bar[kMaxStages];
   __shared__ int sm_err;
   extern __shared__ __align__(128) unsigned char ring[];  // [NST][chunk*R] K, then [NST][chunk*D] V
   T* sK = reinterpret_cast<T*>(ring);
@@ -388,7 +387,7 @@ decode_bulk_kernel(const DecodeParams p) {
 #pragma unroll
   for (int c = 0; c < 8; ++c) acc[c] = 0.f;
 
-  if (warp == kConsumerWarps) {
+  if (warp == NW) {
     // ---------------- producer: stream chunks into the ring ----------------
     if (lane == 0) {
       const char* kg = reinterpret_cast<const char*>(p.cache_k) + (b * p.sck[0] + h * p.sck[1]) * sizeof(T);
@@ -407,10 +406,10 @@ decode_bulk_kernel(const DecodeParams p) {
     }
   } else {
     // ---------------- consumers: GLA rows first (overlaps the first copies) -
-    gla_rows<T, D, ALPHA>(p, s, b, h, tid, sm_y);
+    if (tid < kConsumers) gla_rows<T, D, ALPHA>(p, s, b, h, tid, sm_y);
     const int cg_ = lane % G, ts = lane / G;
     volatile int* verr = &sm_err;
-    for (int c = warp; c < nchunks; c += kConsumerWarps) {
+    for (int c = warp; c < nchunks; c += NW) {
       const int st = c % NST;
       if (!*verr && !sm100::mbar_wait(&full_bar[st], (c / NST) & 1)) atomicOr(&sm_err, 2);
       const int t0 = t_begin + c * kBulkChunk;
@@ -449,18 +448,18 @@ decode_bulk_kernel(const DecodeParams p) {
   }
   __syncthreads();
   if (tid == 0 && sm_err) atomicOr(p.ws_status, 4 * sm_err);
-  finish<T, D, CLUSTER>(p, s, b, h, tid, lane, warp, kConsumerWarps + 1, sh, sm_acc, sm_y, sm_part);
+  finish<T, D, CLUSTER, NW>(p, s, b, h, tid, lane, warp, NW + 1, sh, sm_acc, sm_y, sm_part);
 }
 
-template <typename T, int D, bool ALPHA, bool CLUSTER>
+template <typename T, int D, bool ALPHA, bool CLUSTER, int NW>
 cudaError_t launch_bulk(const DecodeParams& p, cudaStream_t st) {
-  const size_t smem = (size_t)bulk_stages<T>() * kBulkChunk * (p.R + D) * sizeof(T);
-  auto k = decode_bulk_kernel<T, D, ALPHA, CLUSTER>;
+  const size_t smem = (size_t)p.stages * kBulkChunk * (p.R + D) * sizeof(T);
+  auto k = decode_bulk_kernel<T, D, ALPHA, CLUSTER, NW>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.split_k, p.H, p.B);
-  cfg.blockDim = dim3(kConsumers + 32);
+  cfg.blockDim = dim3(NW * 32 + 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
@@ -486,8 +485,12 @@ cudaError_t launch_d(const DecodeParams& p, int path, bool alpha, cudaStream_t s
   dim3 grid(p.split_k, p.H, p.B);
   if (path == 2) {
     const bool cluster = p.split_k > 1 && p.split_k <= kMaxClusterSplit;
-    if (cluster) return alpha ? launch_bulk<T, D, true, true>(p, st) : launch_bulk<T, D, false, true>(p, st);
-    return alpha ? launch_bulk<T, D, true, false>(p, st) : launch_bulk<T, D, false, false>(p, st);
+    if (p.consumer_warps == 8) {
+      if (cluster) return alpha ? launch_bulk<T, D, true, true, 8>(p, st) : launch_bulk<T, D, false, true, 8>(p, st);
+      return alpha ? launch_bulk<T, D, true, false, 8>(p, st) : launch_bulk<T, D, false, false, 8>(p, st);
+    }
+    if (cluster) return alpha ? launch_bulk<T, D, true, true, 4>(p, st) : launch_bulk<T, D, false, true, 4>(p, st);
+    return alpha ? launch_bulk<T, D, true, false, 4>(p, st) : launch_bulk<T, D, false, false, 4>(p, st);
   } else if (path == 1) {
     if (alpha) decode_reg_kernel<T, D, true, true><<<grid, kConsumers, 0, st>>>(p);
     else decode_reg_kernel<T, D, true, false><<<grid, kConsumers, 0, st>>>(p);

@@ -30,6 +30,8 @@ struct DecodeParams {
   float* ws_part;
   int* ws_count;
   int* ws_status;
+  int stages;                 // bulk ring depth (64-token chunks)
+  int consumer_warps;         // bulk kernel consumer warps: 4 or 8
 };
 
 // path: 0 = strided register loads, 1 = 16-byte register loads, 2 = TMA bulk ring

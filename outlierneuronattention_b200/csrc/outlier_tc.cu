@@ -180,21 +180,22 @@ outlier_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
       }
     }
     const float mts = mt * scale;
-    if (mts > m_used + 8.f) {
-      const float factor = exp2f(m_used - mts);  // 0 on the first tile
-      l_sum *= factor;
-      if (j > 0) {
+    const bool raise = mts > m_used + 8.f;
+    const float factor = raise ? exp2f(m_used - mts) : 1.f;  // 0 on the first tile
+    l_sum *= factor;
+    if (raise) m_used = mts;
+    // TMEM loads/stores are warp-collective: the whole warp rescales its rows
+    // of O when any of them raised its max (the others multiply by 1)
+    if (j > 0 && __any_sync(0xffffffffu, raise)) {
 #pragma unroll
-        for (int c = 0; c < D; c += 32) {
-          uint32_t r[32];
-          sm100::tmem_ld32(tO + lane_off + c, r);
-          sm100::tc_wait_ld();
+      for (int c = 0; c < D; c += 32) {
+        uint32_t r[32];
+        sm100::tmem_ld32(tO + lane_off + c, r);
+        sm100::tc_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * factor);
-          sm100::tmem_st32(tO + lane_off + c, r);
-        }
+        for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * factor);
+        sm100::tmem_st32(tO + lane_off + c, r);
       }
-      m_used = mts;
     }
     // ---- pass 2: P = exp2(s*scale - m) as 16-bit pairs over columns [0, 64)
 #pragma unroll

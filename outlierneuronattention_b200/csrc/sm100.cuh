@@ -1,9 +1,9 @@
 // Thin inline-PTX wrappers for sm_100a: mbarriers, bulk / tensor copies
 // (TMA, never with cluster multicast) and tcgen05 (TMEM + 5th-gen MMA).
 //
-// Every wait is bounded: mbar_wait() gives up after `max_iter` polls and
-// returns false, so a kernel can record an error and leave instead of
-// spinning forever.
+// Every wait is bounded: mbar_wait() gives up after a wall-time deadline
+// (%globaltimer) and returns false, so a kernel can record an error and leave
+// instead of spinning forever.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -41,11 +41,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait for the phase with the given parity to complete.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t max_iter = (1u << 24)) {
-  for (uint32_t i = 0; i < max_iter; ++i)
-    if (mbar_try_wait(bar, parity)) return true;
-  return false;
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+// Wait for the phase with the given parity to complete, giving up after
+// `timeout_ns` of wall time (default 200 ms; a healthy phase completes in
+// microseconds).  Returns false on timeout.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, uint64_t timeout_ns = 200000000ull) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    for (int i = 0; i < 32; ++i)
+      if (mbar_try_wait(bar, parity)) return true;
+    if (globaltimer_ns() - t0 > timeout_ns) return false;
+  }
 }
 
 // ---- bulk copies (TMA engine) ----------------------------------------------
