@@ -281,13 +281,21 @@ int hofa_decode_fwd(const hofa_decode_args* a, void* stream) {
   // TMA bulk path: additionally, every (b,h) slab of cache rows is contiguous
   const bool bulk = vec && a->cache_k.stride[2] == R && a->cache_v.stride[2] == D && !getenv_flag("HOFA_DECODE_NO_BULK");
   const int path = bulk ? 2 : (vec ? 1 : 0);
+  // bulk ring: 64-token slots; a slot is always consumed by the same warp,
+  // which requires stages % consumer_warps == 0
+  p.consumer_warps = 4;
   p.stages = es == 4 ? 4 : 8;
-  p.consumer_warps = 8;
+  if (const char* v = getenv("HOFA_DECODE_WARPS")) p.consumer_warps = atoi(v) == 8 ? 8 : 4;
   if (const char* v = getenv("HOFA_DECODE_STAGES")) {
     const int n = atoi(v);
-    if (n >= 2 && n <= 16 && (size_t)n * 64 * (R + D) * es <= 200 * 1024) p.stages = n;
+    if (n >= 2 && n <= 16) p.stages = n;
   }
-  if (const char* v = getenv("HOFA_DECODE_WARPS")) p.consumer_warps = atoi(v) == 4 ? 4 : 8;
+  p.stages = ((p.stages + p.consumer_warps - 1) / p.consumer_warps) * p.consumer_warps;
+  while (p.stages > p.consumer_warps && (size_t)p.stages * 64 * (R + D) * es > 200 * 1024) p.stages -= p.consumer_warps;
+  if (p.stages > 16 || (size_t)p.stages * 64 * (R + D) * es > 200 * 1024) {
+    p.consumer_warps = 4;
+    p.stages = 4;
+  }
   cudaError_t e = hofa::launch_decode(p, dt, path, alpha, reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "hofa_decode_fwd launch");
   return HOFA_OK;

@@ -371,6 +371,14 @@ decode_bulk_kernel(const DecodeParams p) {
   const int t_end = min(seq_len, t_begin + tps);
   const int nchunks = t_end > t_begin ? (t_end - t_begin + kBulkChunk - 1) / kBulkChunk : 0;
 
+  // Slot st of the ring holds chunks st, st+NST, ... and is consumed by warp
+  // st % NW only when NST % NW == 0; otherwise a warp could wait on a phase
+  // two completions ahead (mbarrier parity waits alias).  The host guarantees
+  // the divisibility; a violation is reported and the CTA produces nothing.
+  if (NST % NW != 0 || NST > kMaxStages) {
+    if (tid == 0) atomicOr(p.ws_status, 16);
+    return;
+  }
   if (tid == 0) {
     for (int i = 0; i < NST; ++i) {
       sm100::mbar_init(&full_bar[i], 1);
@@ -379,8 +387,7 @@ decode_bulk_kernel(const DecodeParams p) {
     sm_err = 0;
     sm100::fence_mbar_init();
   }
-  load_q<T, D>(p, b, h, tid, sm_q);
-  __syncthreads();
+  __syncthreads();  // barriers initialised; the producer starts streaming at once
 
   float m_run = -INFINITY, l_run = 0.f;
   float acc[8];
@@ -405,7 +412,9 @@ decode_bulk_kernel(const DecodeParams p) {
       }
     }
   } else {
-    // ---------------- consumers: GLA rows first (overlaps the first copies) -
+    // ---------------- consumers: q, then GLA rows (overlap the first copies)
+    load_q<T, D>(p, b, h, tid, sm_q);
+    asm volatile("bar.sync 1, %0;" ::"n"(NW * 32) : "memory");  // consumers only
     if (tid < kConsumers) gla_rows<T, D, ALPHA>(p, s, b, h, tid, sm_y);
     const int cg_ = lane % G, ts = lane / G;
     volatile int* verr = &sm_err;
