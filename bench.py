@@ -329,6 +329,8 @@ def run_ours(args):
            "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                    "d2h_bytes_per_step": d2h, "api": "outlierneuronattention_b200.fused_hofa_decode"},
            "gpu_launches": args.steps, "clocks": clocks}
+    if not args.no_prefill:
+        out["prefill"] = measure_prefill(dev)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(B, args.cpu_seconds)
     if world > 1:
@@ -336,6 +338,69 @@ def run_ours(args):
         dist.destroy_process_group()
     if rank == 0:
         print(json.dumps(out), flush=True)
+
+
+# ----------------------------------------------------------------------------- prefill
+def measure_prefill(dev, B=4, T=8192, steps=5, warmup=3):
+    """BASELINE config 2 prefill of the attention core (bf16, B=4, T=8192,
+    H=16, d_h=64, r=16): gates + RoPE + cache export (hofa_prep_fwd), the
+    chunked GLA (hofa_prefill_gla_fwd) and the tcgen05 outlier attention
+    (hofa_prefill_outlier_fwd), on projections already in HBM.  Inputs
+    (3 x 64 MiB) exceed L2.  Per-kernel device times come from CUDA events."""
+    from outlierneuronattention_b200.chunk_gla_inlier import gla_forward
+    from outlierneuronattention_b200.exact_attention import exact_attention_triton
+    from outlierneuronattention_b200.modules import RotaryEmbedding
+    from outlierneuronattention_b200.prep import prep
+    g = torch.Generator(device=dev).manual_seed(3)
+    x3 = torch.randn(B, T, 3, H, D, device=dev, generator=g).to(torch.bfloat16)
+    q0, k0, v = (x3[:, :, i].transpose(1, 2) for i in range(3))  # [B,H,T,D] views, as the layer's projections
+    gate_w = torch.randn(H, 2 * D, device=dev, generator=g) * 0.1
+    gate_b = torch.full((H,), -1.0, device=dev)
+    mix_w = torch.randn(H, 2 * D, device=dev, generator=g) * 0.1
+    mix_b = torch.zeros(H, device=dev)
+    rope = RotaryEmbedding(R).to(dev)
+    gs = torch.ones(1, H, 1, D, device=dev)
+    q, k = q0.clone(), k0.clone()
+    lg = torch.empty(B, H, T, device=dev)
+    mix = torch.empty(B, H, T, device=dev, dtype=torch.bfloat16)
+    ck = torch.empty(B, H, T, R, device=dev, dtype=torch.bfloat16)
+    cv = torch.empty(B, H, T, D, device=dev, dtype=torch.bfloat16)
+    y = torch.empty(B, H, T, D, device=dev, dtype=torch.bfloat16)
+    st = torch.empty(B, H, J, D, device=dev)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+    times = {"prep": [], "gla": [], "outlier": []}
+    for it in range(warmup + steps):
+        q.copy_(q0)
+        k.copy_(k0)
+        torch.cuda.synchronize()
+        ev[0].record()
+        prep(q, k, v, gate_w, gate_b, lg, mix_w=mix_w, mix_b=mix_b, mix_out=mix, cos=rope.cos_cached,
+             sin=rope.sin_cached, R=R, pos0=0, cache_k=ck, cache_v=cv)
+        ev[1].record()
+        gla_forward(q, k, v, lg, R, mix_g=mix, gla_scale=gs, y=y, state_out=st)
+        ev[2].record()
+        exact_attention_triton(q, k, v, R, 2.0, mix, out=y)
+        ev[3].record()
+        torch.cuda.synchronize()
+        if it >= warmup:
+            times["prep"].append(ev[0].elapsed_time(ev[1]))
+            times["gla"].append(ev[1].elapsed_time(ev[2]))
+            times["outlier"].append(ev[2].elapsed_time(ev[3]))
+    ms = {k_: statistics.median(v_) for k_, v_ in times.items()}
+    total = sum(ms.values())
+    attn_flops = B * H * (R + D) * T * T            # causal QK^T + PV, 2 flops per MAC
+    gla_flops = 6 * B * H * J * D * T
+    bf16_peak = 1647.9
+    pk = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(pk):
+        bf16_peak = float(json.load(open(pk))["bf16_tflops"])
+    ach = attn_flops / (ms["outlier"] / 1e3) / 1e12
+    return {"workload": f"config2-prefill-B{B}-T{T}", "tokens_per_s": round(B * T / (total / 1e3), 1),
+            "ms": round(total, 4), "ms_by_kernel": {k_: round(v_, 4) for k_, v_ in ms.items()},
+            "algorithmic_flops": attn_flops + gla_flops, "exps": B * H * T * T // 2,
+            "roofline_outlier_kernel": {"bound": "tensor", "achieved": round(ach, 2), "peak": bf16_peak,
+                                        "unit": "TFLOP/s", "frac": round(ach / bf16_peak, 4),
+                                        "peak_source": "measured bf16_tflops (burst)"}}
 
 
 # ----------------------------------------------------------------------------- CPU arm
@@ -393,6 +458,9 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-prefill", action="store_true", help="skip the config-2 prefill measurement")
+    ap.add_argument("--profile-prefill", action="store_true",
+                    help="only the config-2 prefill kernels (for ncu captures); prints no bench line")
     ap.add_argument("--profile", action="store_true",
                     help="only warm-up + timed decode launches (for ncu captures); prints no bench line")
     args = ap.parse_args()
@@ -400,6 +468,10 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.profile_prefill:
+        # small, self-contained command for ncu: one warm-up and one timed prefill
+        torch.cuda.set_device(0)
+        print(json.dumps(measure_prefill(torch.device("cuda", 0), steps=1, warmup=1)))
     else:
         run_ours(args)
 

@@ -133,7 +133,7 @@ bool getenv_flag(const char* name) {
 bool supported_d(int64_t D) { return D == 32 || D == 64 || D == 128; }
 
 constexpr int kMaxSplit = 64;
-constexpr int kAutoSplitMax = 16;
+constexpr int kAutoClusterMax = 16;
 constexpr int kMaxSegments = 64;
 
 size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -151,14 +151,20 @@ int32_t hofa_abi_version(void) { return HOFA_ABI_VERSION; }
 int32_t hofa_decode_choose_split(int32_t B, int32_t H, int32_t seq_len, int32_t sms) {
   if (B <= 0 || H <= 0) return 1;
   if (sms <= 0) sms = 148;
-  // one wave of the cache-streaming kernel (two CTAs per SM), at most 16
-  // splits (one thread-block cluster per head), at least 256 tokens a split
+  // about four resident CTAs of the cache-streaming kernel per SM, at least
+  // 256 tokens a split; up to 16 splits run as one thread-block cluster per
+  // head (a power of two), more splits combine through the workspace
   const int64_t heads = (int64_t)B * H;
-  int64_t s = (2 * (int64_t)sms) / heads;
+  int64_t s = (4 * (int64_t)sms) / heads;
   const int64_t by_len = seq_len / 256 > 1 ? seq_len / 256 : 1;
   if (s > by_len) s = by_len;
-  if (s > kAutoSplitMax) s = kAutoSplitMax;
+  if (s > kMaxSplit) s = kMaxSplit;
   if (s < 1) s = 1;
+  if (s <= kAutoClusterMax) {
+    int64_t p2 = 1;
+    while (p2 * 2 <= s) p2 *= 2;
+    s = p2;
+  }
   return (int32_t)s;
 }
 
@@ -284,7 +290,7 @@ int hofa_decode_fwd(const hofa_decode_args* a, void* stream) {
   // bulk ring: 64-token slots; a slot is always consumed by the same warp,
   // which requires stages % consumer_warps == 0
   p.consumer_warps = 4;
-  p.stages = es == 4 ? 4 : 8;
+  p.stages = 4;
   if (const char* v = getenv("HOFA_DECODE_WARPS")) p.consumer_warps = atoi(v) == 8 ? 8 : 4;
   if (const char* v = getenv("HOFA_DECODE_STAGES")) {
     const int n = atoi(v);

@@ -117,6 +117,7 @@ __device__ __forceinline__ void gla_rows(const DecodeParams& p, int s, int b, in
     const float gam_h = expf(lg);
     const float* sin_ = p.state_in + b * p.sst[0] + h * p.sst[1];
     float* sout = p.state_out + b * p.sso[0] + h * p.sso[1];
+#pragma unroll 2
     for (int row = r0 + rsub; row < r1; row += RSUB) {
       const float kr = to_f(kp[(int64_t)(R + row) * p.sk[2]]);
       const float qr = to_f(qp[(int64_t)(R + row) * p.sq[2]]);
@@ -387,6 +388,12 @@ decode_bulk_kernel(const DecodeParams p) {
     sm_err = 0;
     sm100::fence_mbar_init();
   }
+  // Programmatic dependent launch: this grid may have been scheduled while the
+  // previous kernel of the stream was still running; wait for it to complete
+  // (and its writes to be visible) before touching global memory, then let
+  // the next kernel start scheduling.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __syncthreads();  // barriers initialised; the producer starts streaming at once
 
   float m_run = -INFINITY, l_run = 0.f;
@@ -412,10 +419,10 @@ decode_bulk_kernel(const DecodeParams p) {
       }
     }
   } else {
-    // ---------------- consumers: q, then GLA rows (overlap the first copies)
+    // ---------------- consumers: GLA rows and q (overlap the first copies) -
+    if (tid < kConsumers) gla_rows<T, D, ALPHA>(p, s, b, h, tid, sm_y);
     load_q<T, D>(p, b, h, tid, sm_q);
     asm volatile("bar.sync 1, %0;" ::"n"(NW * 32) : "memory");  // consumers only
-    if (tid < kConsumers) gla_rows<T, D, ALPHA>(p, s, b, h, tid, sm_y);
     const int cg_ = lane % G, ts = lane / G;
     volatile int* verr = &sm_err;
     for (int c = warp; c < nchunks; c += NW) {
@@ -471,18 +478,21 @@ cudaError_t launch_bulk(const DecodeParams& p, cudaStream_t st) {
   cfg.blockDim = dim3(NW * 32 + 32);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
   if (CLUSTER) {
     if (p.split_k > 8) {
       e = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
       if (e != cudaSuccess) return e;
     }
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = p.split_k;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = p.split_k;
+    attr[1].val.clusterDim.y = 1;
+    attr[1].val.clusterDim.z = 1;
+    cfg.numAttrs = 2;
   }
   e = cudaLaunchKernelEx(&cfg, k, p);
   if (e != cudaSuccess) return e;
