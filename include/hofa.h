@@ -100,6 +100,20 @@ int32_t hofa_decode_choose_split(int32_t B, int32_t H, int32_t seq_len, int32_t 
  * Synchronises `stream`; not for use inside graph capture. */
 int hofa_decode_read_status(void* workspace, void* stream, int32_t* status_out);
 
+/* Same decode step as hofa_decode_fwd for callers that cannot allocate
+ * device memory (a host runtime that owns all allocations, a real-time loop
+ * that must not enter the driver's allocator, glue holding only borrowed
+ * pointers).  No counterpart in the reference.  args->workspace and
+ * args->workspace_bytes are ignored: the scratch is a 2 MiB array built into
+ * the library (held on every GPU that loads it until exit), and calls needing
+ * more (hofa_decode_workspace_size of their B, H, D and split count) fail with
+ * HOFA_ERR_WORKSPACE.  All calls share that array, so calls that overlap on the
+ * GPU race and must be serialised by the caller.  The first call on a device
+ * looks up the array's address; make it before any stream capture.  Each call
+ * clears the array's ticket and status words on `stream` before the kernel;
+ * it never allocates. */
+int hofa_decode_fwd_noalloc(const hofa_decode_args* args, void* stream);
+
 /* ------------------------------------------------------------------------ */
 /* Prefill, inlier path: chunked gated linear attention.                      */
 /* ------------------------------------------------------------------------ */

@@ -140,6 +140,15 @@ size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
 
 }  // namespace
 
+namespace hofa {
+// Records `message` as the calling thread's last error and returns `code`
+// (for entry points defined outside this file).
+int set_last_error(int code, const char* message) {
+  g_err = message;
+  return code;
+}
+}  // namespace hofa
+
 extern "C" {
 
 const char* hofa_last_error(void) { return g_err.c_str(); }
