@@ -160,11 +160,11 @@ int32_t hofa_abi_version(void) { return HOFA_ABI_VERSION; }
 int32_t hofa_decode_choose_split(int32_t B, int32_t H, int32_t seq_len, int32_t sms) {
   if (B <= 0 || H <= 0) return 1;
   if (sms <= 0) sms = 148;
-  // about four resident CTAs of the cache-streaming kernel per SM, at least
+  // about two resident CTAs of the cache-streaming kernel per SM, at least
   // 256 tokens a split; up to 16 splits run as one thread-block cluster per
   // head (a power of two), more splits combine through the workspace
   const int64_t heads = (int64_t)B * H;
-  int64_t s = (4 * (int64_t)sms) / heads;
+  int64_t s = (2 * (int64_t)sms) / heads;
   const int64_t by_len = seq_len / 256 > 1 ? seq_len / 256 : 1;
   if (s > by_len) s = by_len;
   if (s > kMaxSplit) s = kMaxSplit;

@@ -396,10 +396,12 @@ decode_bulk_kernel(const DecodeParams p) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __syncthreads();  // barriers initialised; the producer starts streaming at once
 
-  float m_run = -INFINITY, l_run = 0.f;
-  float acc[8];
+  // two independent online-softmax states per warp (one per half of a
+  // 64-token chunk) so that their dependency chains interleave
+  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
+  float acc[2][8];
 #pragma unroll
-  for (int c = 0; c < 8; ++c) acc[c] = 0.f;
+  for (int c = 0; c < 8; ++c) acc[0][c] = acc[1][c] = 0.f;
 
   if (warp == NW) {
     // ---------------- producer: stream chunks into the ring ----------------
@@ -455,12 +457,19 @@ decode_bulk_kernel(const DecodeParams p) {
           }
           sc = dot;
         }
-        if (base < n) tile_update<T, D>(sc, vr, m_run, l_run, acc, ts);  // consumes every value read
+        if (base < n) tile_update<T, D>(sc, vr, m_run[sub], l_run[sub], acc[sub], ts);  // consumes every value read
       }
       __syncwarp();
       if (lane == 0) sm100::mbar_arrive(&empty_bar[st]);
     }
-    warp_flush<D>(m_run, l_run, acc, lane, warp, sh, sm_acc);
+    // merge the two states (both are warp-uniform in m)
+    const float mm = fmaxf(m_run[0], m_run[1]);
+    const float w0 = m_run[0] == -INFINITY ? 0.f : exp2f(m_run[0] - mm);
+    const float w1 = m_run[1] == -INFINITY ? 0.f : exp2f(m_run[1] - mm);
+    float accm[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) accm[c] = acc[0][c] * w0 + acc[1][c] * w1;
+    warp_flush<D>(mm, l_run[0] * w0 + l_run[1] * w1, accm, lane, warp, sh, sm_acc);
   }
   __syncthreads();
   if (tid == 0 && sm_err) atomicOr(p.ws_status, 4 * sm_err);
