@@ -135,7 +135,11 @@ typedef struct hofa_gla_args {
 } hofa_gla_args;
 
 /* Replaces chunk_gla_inlier_fwd (src/chunk_gla_inlier.py:153-237) and
- * chunk_gla_fwd_kernel (:5-150). */
+ * chunk_gla_fwd_kernel (:5-150).  bf16/f16 inputs with D = 64, R % 8 == 0 and
+ * no log_alpha run three chunk-parallel tcgen05 kernels (per-chunk state
+ * contributions, a scan over chunks, per-chunk outputs) when the workspace
+ * holds hofa_gla_workspace_size() bytes; other cases run a segment-parallel
+ * CUDA-core kernel. */
 int hofa_prefill_gla_fwd(const hofa_gla_args* args, void* stream);
 size_t hofa_gla_workspace_size(int32_t B, int32_t H, int32_t T, int32_t D, int32_t R,
                                int32_t chunk_size, int32_t num_segments);
@@ -161,9 +165,10 @@ typedef struct hofa_outlier_args {
  * accumulators); other shapes and float32 inputs on a CUDA-core kernel. */
 int hofa_prefill_outlier_fwd(const hofa_outlier_args* args, void* stream);
 
-/* Device status of the tensor-core outlier kernel since the last read (0 = no
- * fault; 1 = a bounded wait for a copy or an MMA ran out and the affected
- * tile rows were not written), then clears it.  Synchronises `stream`. */
+/* Device status of the tensor-core prefill kernels since the last read (0 = no
+ * fault; bit 0: outlier attention, bit 1: GLA -- a bounded wait for a copy or
+ * an MMA ran out and the affected rows were not written), then clears it.
+ * Synchronises `stream`. */
 int hofa_prefill_read_status(void* stream, int32_t* status_out);
 
 /* ------------------------------------------------------------------------ */

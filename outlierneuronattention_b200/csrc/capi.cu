@@ -17,6 +17,11 @@
 
 namespace hofa {
 int gla_internal_chunk(int D);
+size_t gla_tc_workspace_bytes(int64_t B, int64_t H, int64_t T, int64_t J);
+bool gla_tc_eligible(const GlaParams& p, int dtype);
+cudaError_t launch_gla_tc(const GlaParams& p, int dtype, cudaStream_t st, bool* taken);
+int gla_tc_chunk();
+cudaError_t read_gla_tc_status(int* out, cudaStream_t st);
 cudaError_t read_outlier_tc_status(int* out, cudaStream_t st);
 cudaError_t launch_outlier_generic(const OutlierParams& p, int dtype, cudaStream_t st);
 cudaError_t launch_outlier_tc(const OutlierParams& p, int dtype, cudaStream_t st, bool* taken);
@@ -134,6 +139,7 @@ bool supported_d(int64_t D) { return D == 32 || D == 64 || D == 128; }
 
 constexpr int kMaxSplit = 64;
 constexpr int kAutoClusterMax = 16;
+constexpr int kAutoClusterCap = 8;
 constexpr int kMaxSegments = 64;
 
 size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
@@ -172,7 +178,7 @@ int32_t hofa_decode_choose_split(int32_t B, int32_t H, int32_t seq_len, int32_t 
   if (s <= kAutoClusterMax) {
     int64_t p2 = 1;
     while (p2 * 2 <= s) p2 *= 2;
-    s = p2;
+    s = p2 < kAutoClusterCap ? p2 : kAutoClusterCap;  // clusters above 8 CTAs schedule poorly
   }
   return (int32_t)s;
 }
@@ -299,7 +305,7 @@ int hofa_decode_fwd(const hofa_decode_args* a, void* stream) {
   // bulk ring: 64-token slots; a slot is always consumed by the same warp,
   // which requires stages % consumer_warps == 0
   p.consumer_warps = 4;
-  p.stages = 4;
+  p.stages = es == 4 ? 4 : 8;
   if (const char* v = getenv("HOFA_DECODE_WARPS")) p.consumer_warps = atoi(v) == 8 ? 8 : 4;
   if (const char* v = getenv("HOFA_DECODE_STAGES")) {
     const int n = atoi(v);
@@ -345,7 +351,9 @@ size_t hofa_gla_workspace_size(int32_t B, int32_t H, int32_t T, int32_t D, int32
   const int64_t nchunks = (T + C - 1) / C;
   if (nseg > nchunks) nseg = nchunks;
   const int64_t J = D - R;
-  return (size_t)B * H * nseg * (J * D + J) * sizeof(float) + 256;
+  const size_t cuda_core = (size_t)B * H * nseg * (J * D + J) * sizeof(float) + 256;
+  const size_t tensor_core = hofa::gla_tc_workspace_bytes(B, H, T, J);
+  return cuda_core > tensor_core ? cuda_core : tensor_core;
 }
 
 int hofa_prefill_gla_fwd(const hofa_gla_args* a, void* stream) {
@@ -390,6 +398,43 @@ int hofa_prefill_gla_fwd(const hofa_gla_args* a, void* stream) {
     if (a->state_out.dtype != HOFA_DTYPE_F32) return fail(HOFA_ERR_INVALID_ARGUMENT, "state_out must be float32");
   }
   if (T == 0) return HOFA_OK;
+  // tensor-core path: chunk-parallel tcgen05 kernels (bf16/f16, head dim 64, scalar decay)
+  {
+    hofa::GlaParams tp;
+    memset(&tp, 0, sizeof(tp));
+    tp.D = (int)D; tp.R = R; tp.log_alpha = alpha ? a->log_alpha.data : nullptr;
+    const size_t need_tc = hofa::gla_tc_workspace_bytes(B, H, T, J);
+    if (hofa::gla_tc_eligible(tp, dt) && a->workspace != nullptr && a->workspace_bytes >= need_tc &&
+        ((reinterpret_cast<uintptr_t>(a->workspace) & 15u) == 0)) {
+      tp = p;  // side-tensor strides filled above
+      tp.q = a->q.data; tp.k = a->k.data; tp.v = a->v.data;
+      tp.log_gamma = a->log_gamma.data;
+      tp.mix_g = p.fuse ? a->mix_g.data : nullptr;
+      tp.gla_scale = p.fuse ? a->gla_scale.data : nullptr;
+      tp.state_init = present(a->state_init) ? (const float*)a->state_init.data : nullptr;
+      tp.y = a->y.data;
+      tp.state_out = present(a->state_out) ? (float*)a->state_out.data : nullptr;
+      tp.B = (int)B; tp.H = (int)H; tp.T = (int)T; tp.D = (int)D; tp.R = R; tp.J = (int)J;
+      tp.chunk = hofa::gla_tc_chunk();
+      tp.nseg = (int)((T + tp.chunk - 1) / tp.chunk);
+      tp.seg_len = tp.chunk;
+      tp.eps = a->eps;
+      for (int i = 0; i < 4; ++i) {
+        tp.sq[i] = a->q.stride[i]; tp.sk[i] = a->k.stride[i]; tp.sv[i] = a->v.stride[i]; tp.sy[i] = a->y.stride[i];
+      }
+      if (tp.state_init) for (int i = 0; i < 3; ++i) tp.ssi[i] = a->state_init.stride[i];
+      if (tp.state_out) for (int i = 0; i < 4; ++i) tp.sso[i] = a->state_out.stride[i];
+      tp.dt_lg = a->log_gamma.dtype;
+      tp.dt_mg = p.fuse ? a->mix_g.dtype : 0;
+      tp.dt_gs = p.fuse ? a->gla_scale.dtype : 0;
+      tp.ws_state = reinterpret_cast<float*>(a->workspace);
+      tp.ws_decay = tp.ws_state + (size_t)B * H * tp.nseg * J * 64;
+      bool taken = false;
+      cudaError_t e = hofa::launch_gla_tc(tp, dt, reinterpret_cast<cudaStream_t>(stream), &taken);
+      if (e != cudaSuccess) return cuda_fail(e, "hofa_prefill_gla_fwd launch (tensor cores)");
+      if (taken) return HOFA_OK;
+    }
+  }
   int nseg, seg_len, C;
   gla_geometry(B, H, T, D, a->num_segments, num_sms(), &nseg, &seg_len, &C);
   const size_t need = (size_t)B * H * nseg * (J * D + J) * sizeof(float);
@@ -468,10 +513,11 @@ int hofa_prefill_outlier_fwd(const hofa_outlier_args* a, void* stream) {
 
 int hofa_prefill_read_status(void* stream, int32_t* status_out) {
   if (status_out == nullptr) return fail(HOFA_ERR_INVALID_ARGUMENT, "NULL argument");
-  int v = 0;
+  int v = 0, w = 0;
   cudaError_t e = hofa::read_outlier_tc_status(&v, reinterpret_cast<cudaStream_t>(stream));
+  if (e == cudaSuccess) e = hofa::read_gla_tc_status(&w, reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "hofa_prefill_read_status");
-  *status_out = v;
+  *status_out = v | (w << 1);
   return HOFA_OK;
 }
 

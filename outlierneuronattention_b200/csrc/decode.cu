@@ -141,92 +141,6 @@ __device__ __forceinline__ void gla_rows(const DecodeParams& p, int s, int b, in
   for (int c = 0; c < 4; ++c) sm_y[rsub][4 * c4 + c] = ya[c];
 }
 
-// The same GLA-row work split in two: gla_prefetch() issues every load of a
-// thread's rows (up to kPrefetchRows; the rest are handled by gla_rows-style
-// loads at compute time) so that they are in flight while the cache streams,
-// gla_compute() does the arithmetic and the stores afterwards.
-constexpr int kPrefetchRows = 6;
-template <int D>
-struct GlaPrefetch {
-  float4 s4[kPrefetchRows];
-  float kr[kPrefetchRows], qr[kPrefetchRows], la[kPrefetchRows];
-  float v4[4];
-  float lg;
-};
-
-template <typename T, int D, bool ALPHA>
-__device__ __forceinline__ void gla_prefetch(const DecodeParams& p, int s, int b, int h, int tid, GlaPrefetch<D>& f) {
-  constexpr int D4 = D / 4;
-  constexpr int RSUB = kConsumers / D4;
-  const int R = p.R, J = D - p.R;
-  const int rows_per = (J + p.split_k - 1) / p.split_k;
-  const int r0 = s * rows_per, r1 = min(J, r0 + rows_per);
-  const int c4 = tid % D4, rsub = tid / D4;
-  if (r0 >= r1) return;
-  const T* qp = reinterpret_cast<const T*>(p.q) + b * p.sq[0] + h * p.sq[1];
-  const T* kp = reinterpret_cast<const T*>(p.k) + b * p.sk[0] + h * p.sk[1];
-  const T* vp = reinterpret_cast<const T*>(p.v) + b * p.sv[0] + h * p.sv[1];
-#pragma unroll
-  for (int c = 0; c < 4; ++c) f.v4[c] = to_f(vp[(int64_t)(4 * c4 + c) * p.sv[2]]);
-  f.lg = ld_any(p.log_gamma, p.dt_lg, b * p.slg[0] + h * p.slg[1]);
-  const float* sin_ = p.state_in + b * p.sst[0] + h * p.sst[1];
-#pragma unroll
-  for (int i = 0; i < kPrefetchRows; ++i) {
-    const int row = r0 + rsub + i * RSUB;
-    if (row < r1) {
-      f.s4[i] = __ldg(reinterpret_cast<const float4*>(sin_ + (int64_t)row * p.sst[2] + 4 * c4));
-      f.kr[i] = to_f(kp[(int64_t)(R + row) * p.sk[2]]);
-      f.qr[i] = to_f(qp[(int64_t)(R + row) * p.sq[2]]);
-      if constexpr (ALPHA) f.la[i] = ld_any(p.log_alpha, p.dt_la, b * p.sla[0] + h * p.sla[1] + row * p.sla[2]);
-    }
-  }
-}
-
-template <typename T, int D, bool ALPHA>
-__device__ __forceinline__ void gla_compute(const DecodeParams& p, int s, int b, int h, int tid, const GlaPrefetch<D>& f,
-                                            float (*sm_y)[D]) {
-  constexpr int D4 = D / 4;
-  constexpr int RSUB = kConsumers / D4;
-  const int R = p.R, J = D - p.R;
-  const int rows_per = (J + p.split_k - 1) / p.split_k;
-  const int r0 = s * rows_per, r1 = min(J, r0 + rows_per);
-  const int c4 = tid % D4, rsub = tid / D4;
-  float ya[4] = {0.f, 0.f, 0.f, 0.f};
-  if (r0 < r1) {
-    float* sout = p.state_out + b * p.sso[0] + h * p.sso[1];
-    const float gam_h = expf(f.lg);
-    auto apply = [&](int row, float4 s4, float kr, float qr, float la) {
-      const float gam = ALPHA ? expf(f.lg * expf(la)) : gam_h;
-      float4 n4;
-      n4.x = fmaf(gam, s4.x, kr * f.v4[0]);
-      n4.y = fmaf(gam, s4.y, kr * f.v4[1]);
-      n4.z = fmaf(gam, s4.z, kr * f.v4[2]);
-      n4.w = fmaf(gam, s4.w, kr * f.v4[3]);
-      *reinterpret_cast<float4*>(sout + (int64_t)row * p.sso[2] + 4 * c4) = n4;
-      ya[0] = fmaf(qr, n4.x, ya[0]);
-      ya[1] = fmaf(qr, n4.y, ya[1]);
-      ya[2] = fmaf(qr, n4.z, ya[2]);
-      ya[3] = fmaf(qr, n4.w, ya[3]);
-    };
-#pragma unroll
-    for (int i = 0; i < kPrefetchRows; ++i) {
-      const int row = r0 + rsub + i * RSUB;
-      if (row < r1) apply(row, f.s4[i], f.kr[i], f.qr[i], f.la[i]);
-    }
-    // rows beyond the prefetch window (head dim 128 with few splits)
-    const T* qp = reinterpret_cast<const T*>(p.q) + b * p.sq[0] + h * p.sq[1];
-    const T* kp = reinterpret_cast<const T*>(p.k) + b * p.sk[0] + h * p.sk[1];
-    const float* sin_ = p.state_in + b * p.sst[0] + h * p.sst[1];
-    for (int row = r0 + rsub + kPrefetchRows * RSUB; row < r1; row += RSUB) {
-      const float la = ALPHA ? ld_any(p.log_alpha, p.dt_la, b * p.sla[0] + h * p.sla[1] + row * p.sla[2]) : 0.f;
-      apply(row, __ldg(reinterpret_cast<const float4*>(sin_ + (int64_t)row * p.sst[2] + 4 * c4)),
-            to_f(kp[(int64_t)(R + row) * p.sk[2]]), to_f(qp[(int64_t)(R + row) * p.sq[2]]), la);
-    }
-  }
-#pragma unroll
-  for (int c = 0; c < 4; ++c) sm_y[rsub][4 * c4 + c] = ya[c];
-}
-
 // CTA partial (m, l, acc[D], y_I[D]), cross-split combine, RMSNorm, blend,
 // store.  Called by every thread of the CTA after a __syncthreads() that
 // publishes sh / sm_acc / sm_y.  The splits of one (b,h) combine either
@@ -482,12 +396,10 @@ decode_bulk_kernel(const DecodeParams p) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   __syncthreads();  // barriers initialised; the producer starts streaming at once
 
-  // two independent online-softmax states per warp (one per half of a
-  // 64-token chunk) so that their dependency chains interleave
-  float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
-  float acc[2][8];
+  float m_run = -INFINITY, l_run = 0.f;
+  float acc[8];
 #pragma unroll
-  for (int c = 0; c < 8; ++c) acc[0][c] = acc[1][c] = 0.f;
+  for (int c = 0; c < 8; ++c) acc[c] = 0.f;
 
   if (warp == NW) {
     // ---------------- producer: stream chunks into the ring ----------------
@@ -507,10 +419,8 @@ decode_bulk_kernel(const DecodeParams p) {
       }
     }
   } else {
-    // ---------------- consumers: issue the GLA-row loads and q, stream the
-    // cache, then finish the GLA rows from registers
-    GlaPrefetch<D> gpf;
-    if (tid < kConsumers) gla_prefetch<T, D, ALPHA>(p, s, b, h, tid, gpf);
+    // ---------------- consumers: GLA rows and q (overlap the first copies) -
+    if (tid < kConsumers) gla_rows<T, D, ALPHA>(p, s, b, h, tid, sm_y);
     load_q<T, D>(p, b, h, tid, sm_q);
     asm volatile("bar.sync 1, %0;" ::"n"(NW * 32) : "memory");  // consumers only
     const int cg_ = lane % G, ts = lane / G;
@@ -545,20 +455,12 @@ decode_bulk_kernel(const DecodeParams p) {
           }
           sc = dot;
         }
-        if (base < n) tile_update<T, D>(sc, vr, m_run[sub], l_run[sub], acc[sub], ts);  // consumes every value read
+        if (base < n) tile_update<T, D>(sc, vr, m_run, l_run, acc, ts);  // consumes every value read
       }
       __syncwarp();
       if (lane == 0) sm100::mbar_arrive(&empty_bar[st]);
     }
-    // merge the two states (both are warp-uniform in m)
-    const float mm = fmaxf(m_run[0], m_run[1]);
-    const float w0 = m_run[0] == -INFINITY ? 0.f : exp2f(m_run[0] - mm);
-    const float w1 = m_run[1] == -INFINITY ? 0.f : exp2f(m_run[1] - mm);
-    float accm[8];
-#pragma unroll
-    for (int c = 0; c < 8; ++c) accm[c] = acc[0][c] * w0 + acc[1][c] * w1;
-    warp_flush<D>(mm, l_run[0] * w0 + l_run[1] * w1, accm, lane, warp, sh, sm_acc);
-    if (tid < kConsumers) gla_compute<T, D, ALPHA>(p, s, b, h, tid, gpf, sm_y);
+    warp_flush<D>(m_run, l_run, acc, lane, warp, sh, sm_acc);
   }
   __syncthreads();
   if (tid == 0 && sm_err) atomicOr(p.ws_status, 4 * sm_err);

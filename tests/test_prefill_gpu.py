@@ -191,3 +191,35 @@ def test_outlier_tensor_core_path(monkeypatch, dtype, B, H, T, D, r, qoff):
     monkeypatch.delenv("HOFA_OUTLIER_NO_TC")
     assert _prefill_status() == 0
     assert maxabs(outs["tc"], outs["cuda_core"].cpu()) <= 2e-2
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("B,H,T,r,fuse,init", [(1, 1, 128, 16, True, False), (2, 3, 1000, 16, True, True),
+                                               (1, 2, 129, 16, False, False), (1, 2, 300, 0, True, False),
+                                               (2, 2, 257, 32, True, True), (1, 1, 64, 8, False, True)])
+def test_gla_tensor_core_path(monkeypatch, dtype, B, H, T, r, fuse, init):
+    """The chunk-parallel tcgen05 GLA (bf16/f16, d_h = 64, scalar decay) and the
+    CUDA-core GLA agree with the oracle on the same inputs, including a seeded
+    initial state; the tensor-core kernels' bounded waits never ran out."""
+    from outlierneuronattention_b200.chunk_gla_inlier import gla_forward
+    D = 64
+    q, k, v, lg, mix, gs = rand_qkv(B, H, T, D, dtype, seed=T + r)
+    s0 = torch.randn(B, H, D - r, D) * 0.3 if init else None
+    Yr, Sr = chunk_gla_core(q, k, v, lg, r, 64, mix_g=mix if fuse else None, gla_scale=gs if fuse else None,
+                            eps=1e-5, state_init=s0)
+    assert _prefill_status() == 0
+    outs = {}
+    for path in ("tc", "cuda_core"):
+        if path == "cuda_core":
+            monkeypatch.setenv("HOFA_GLA_NO_TC", "1")
+        st = torch.empty(B, H, D - r, D, device="cuda")
+        Y = gla_forward(q.cuda(), k.cuda(), v.cuda(), lg.cuda(), r, mix_g=mix.cuda() if fuse else None,
+                        gla_scale=gs.cuda() if fuse else None, state_out=st,
+                        initial_state=None if s0 is None else s0.cuda())
+        torch.cuda.synchronize()
+        outs[path] = (Y, st)
+        scale = 1.0 if fuse else max(1.0, Yr.abs().max().item())
+        assert maxabs(Y, Yr) <= 2e-2 * scale, path
+        assert (st.double().cpu() - Sr).abs().max().item() <= 2e-3 * max(1.0, Sr.abs().max().item()), path
+    monkeypatch.delenv("HOFA_GLA_NO_TC")
+    assert _prefill_status() == 0
