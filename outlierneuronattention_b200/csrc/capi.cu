@@ -609,6 +609,19 @@ int hofa_prep_fwd(const hofa_prep_args* a, void* stream) {
   p.dt_mw = p.mix_w ? a->mix_w.dtype : 0; p.dt_mb = p.mix_b ? a->mix_b.dtype : 0;
   p.dt_fm = p.fixed_mix ? a->fixed_mix.dtype : 0;
   p.dt_lg = a->log_gamma.dtype; p.dt_mo = p.mix_out ? a->mix_out.dtype : 0;
+  // 16-byte row path: unit channel stride and 16-byte aligned rows for q, k (and v / caches when written)
+  {
+    auto rows16 = [](const hofa_tensor& t) {
+      if (t.stride[3] != 1 || !aligned16(t.data)) return false;
+      for (int i = 0; i < 3; ++i)
+        if ((t.stride[i] * 2) % 16 != 0 && t.shape[i] != 1) return false;
+      return true;
+    };
+    bool vec = dt != HOFA_DTYPE_F32 && R % 8 == 0 && rows16(a->q) && rows16(a->k);
+    if (p.cache_k) vec = vec && rows16(a->cache_k);
+    if (p.cache_v) vec = vec && rows16(a->cache_v) && rows16(a->v);
+    p.vec = vec;
+  }
   cudaError_t e = hofa::launch_prep(p, dt, reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "hofa_prep_fwd launch");
   return HOFA_OK;

@@ -93,6 +93,7 @@ struct PrepParams {
   int64_t slg[3], smo[3];
   int64_t sck[4], scv[4];
   int dt_gw, dt_gb, dt_mw, dt_mb, dt_fm, dt_cs, dt_lg, dt_mo;
+  bool vec;                    // unit channel strides and 16-byte aligned rows everywhere
 };
 
 cudaError_t launch_prep(const PrepParams& p, int dtype, cudaStream_t st);

@@ -3,7 +3,9 @@
 // Replaces the reference's Triton kernel _fwd_kernel (src/exact_attention.py:
 // 45-161): out += mix * softmax(sm_scale * q_r k_r^T, causal) v with r = R
 // query/key channels and D value channels.  One CTA of 128 threads owns 128
-// query rows of one (b,h); thread i owns row i, which is TMEM lane i.
+// query rows of one (b,h); thread i owns row i, which is TMEM lane i.  Keys
+// come in tiles of 64, so S/P (64 columns) and O (64 columns at head dim 64)
+// fit in 128 TMEM columns and three to four CTAs share an SM.
 //
 //   TMA (4-D tiled maps over [B,H,T,channels], no multicast) brings the Q
 //   tile once and K/V tiles of 128 keys into a two-stage shared-memory ring.
@@ -11,13 +13,13 @@
 //   with 128-byte swizzled rows (as stored in memory), so no transposition.
 //   Per key tile:
 //     S   = Q K^T            tcgen05.mma kind::f16, A/B from shared memory,
-//                             fp32 accumulator in TMEM columns [0, 128)
-//     P   = exp2(S*c - m)    every thread reads its row of S from TMEM
-//                             (two passes: row max, then exponentials), writes
-//                             P as bf16/f16 pairs over columns [0, 64)
+//                             fp32 accumulator in TMEM columns [0, 64)
+//     P   = exp2(S*c - m)    every thread reads its row of S from TMEM in one
+//                             round trip (row max, then exponentials), writes
+//                             P as bf16/f16 pairs over columns [0, 32)
 //     O  += P V              tcgen05.mma with A = P from TMEM, B = V from
 //                             shared memory, fp32 accumulator in TMEM
-//                             columns [128, 128 + D)
+//                             columns [64, 64 + D)
 //   The running max is only raised when a row's max grows by more than 2^8
 //   (then the row of O is rescaled in TMEM); otherwise P is formed against the
 //   stale max, which changes nothing but the common factor removed at the end.
@@ -39,17 +41,20 @@ __device__ int g_outlier_tc_status;
 
 namespace {
 
-constexpr int kTile = 128;        // query rows per CTA = keys per tile
+constexpr int kRows = 128;        // query rows per CTA (TMEM lanes)
+constexpr int kKeys = 64;         // keys per tile
 constexpr int kThreads = 128;
-constexpr uint32_t kTmemCols = 256;
-constexpr uint32_t kColO = 128;   // first TMEM column of O
-constexpr size_t kSmemFloor = 80 * 1024;  // keeps <= 2 CTAs (2 x 256 TMEM columns) per SM
+
+// TMEM columns: S / P in [0, kKeys), O in [kKeys, kKeys + D), rounded up to a power of two
+template <int D>
+constexpr uint32_t tmem_cols() { return kKeys + D <= 128 ? 128 : 256; }
 
 template <int D, int R>
 constexpr size_t smem_bytes() {
-  constexpr size_t qk_slot = ((size_t)kTile * R * 2 + 1023) & ~size_t(1023);
-  constexpr size_t need = 1024 + 3 * qk_slot + 2 * (size_t)kTile * D * 2 + 64;
-  return need > kSmemFloor ? need : kSmemFloor;
+  constexpr size_t q = ((size_t)kRows * R * 2 + 1023) & ~size_t(1023);
+  constexpr size_t k = ((size_t)kKeys * R * 2 + 1023) & ~size_t(1023);
+  constexpr size_t v = (size_t)kKeys * D * 2;
+  return 1024 + q + 2 * k + 2 * v + 64;
 }
 
 constexpr uint32_t swizzle_mode(int row_bytes) {
@@ -66,24 +71,27 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, bool bf16) {
 }
 
 template <typename T, int D, int R>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, 3)
 outlier_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                   const __grid_constant__ CUtensorMap tv, const OutlierParams p) {
   constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr int RB = R * 2;                       // bytes per Q/K row
-  constexpr uint32_t QK_BYTES = kTile * RB;
-  constexpr uint32_t V_BYTES = kTile * D * 2;
-  constexpr uint32_t QK_SLOT = (QK_BYTES + 1023) & ~1023u;
+  constexpr uint32_t Q_BYTES = kRows * RB;
+  constexpr uint32_t K_BYTES = kKeys * RB;
+  constexpr uint32_t V_BYTES = kKeys * D * 2;
+  constexpr uint32_t Q_SLOT = (Q_BYTES + 1023) & ~1023u;
+  constexpr uint32_t K_SLOT = (K_BYTES + 1023) & ~1023u;
   constexpr uint32_t SWZ = swizzle_mode(RB);
-  constexpr uint32_t IDESC_S = sm100::idesc_f16(BF16, false, false, kTile, kTile);
-  constexpr uint32_t IDESC_O = sm100::idesc_f16(BF16, false, true, kTile, D);
+  constexpr uint32_t IDESC_S = sm100::idesc_f16(BF16, false, false, kRows, kKeys);
+  constexpr uint32_t IDESC_O = sm100::idesc_f16(BF16, false, true, kRows, D);
+  constexpr uint32_t NCOLS = tmem_cols<D>();
 
   extern __shared__ unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* sQ = base;
-  unsigned char* sK[2] = {base + QK_SLOT, base + 2 * QK_SLOT};
-  unsigned char* sV[2] = {base + 3 * QK_SLOT, base + 3 * QK_SLOT + V_BYTES};
-  uint64_t* bars = reinterpret_cast<uint64_t*>(base + 3 * QK_SLOT + 2 * V_BYTES);
+  unsigned char* sK[2] = {base + Q_SLOT, base + Q_SLOT + K_SLOT};
+  unsigned char* sV[2] = {base + Q_SLOT + 2 * K_SLOT, base + Q_SLOT + 2 * K_SLOT + V_BYTES};
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + Q_SLOT + 2 * K_SLOT + 2 * V_BYTES);
   uint64_t* bar_q = bars + 0;
   uint64_t* bar_kv = bars + 1;  // [2]
   uint64_t* bar_s = bars + 3;
@@ -92,12 +100,12 @@ outlier_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
   int* err_flag = reinterpret_cast<int*>(bars + 7);
 
   const int tid = threadIdx.x, warp = tid >> 5;
-  const int nqb = (p.Tq + kTile - 1) / kTile;
+  const int nqb = (p.Tq + kRows - 1) / kRows;
   const int qb = nqb - 1 - (int)blockIdx.x;     // long causal rows first
   const int h = blockIdx.y, b = blockIdx.z;
-  const int q0 = qb * kTile;
-  const int last_key = min(p.Tk - 1, q0 + kTile - 1 + p.q_offset);
-  const int ntiles = last_key / kTile + 1;
+  const int q0 = qb * kRows;
+  const int last_key = min(p.Tk - 1, q0 + kRows - 1 + p.q_offset);
+  const int ntiles = last_key / kKeys + 1;
 
   if (tid == 0) {
     sm100::mbar_init(bar_q, 1);
@@ -112,25 +120,25 @@ outlier_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
     sm100::prefetch_tmap(&tv);
   }
   if (warp == 0) {
-    sm100::tmem_alloc(tmem_slot, kTmemCols);
+    sm100::tmem_alloc(tmem_slot, NCOLS);
     sm100::tmem_relinquish();
   }
   sm100::tc_fence_before();
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tO = tmem + kColO;
+  const uint32_t tS = tmem, tO = tmem + kKeys;
   const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
 
   auto load_kv = [&](int j, int st) {
-    sm100::mbar_arrive_expect_tx(&bar_kv[st], QK_BYTES + V_BYTES);
-    sm100::tma_load_4d(sK[st], &tk, 0, j * kTile, h, b, &bar_kv[st]);
+    sm100::mbar_arrive_expect_tx(&bar_kv[st], K_BYTES + V_BYTES);
+    sm100::tma_load_4d(sK[st], &tk, 0, j * kKeys, h, b, &bar_kv[st]);
 #pragma unroll
     for (int g = 0; g < D / 64; ++g)
-      sm100::tma_load_4d(sV[st] + g * kTile * 128, &tv, g * 64, j * kTile, h, b, &bar_kv[st]);
+      sm100::tma_load_4d(sV[st] + g * kKeys * 128, &tv, g * 64, j * kKeys, h, b, &bar_kv[st]);
   };
   if (tid == 0) {
-    sm100::mbar_arrive_expect_tx(bar_q, QK_BYTES);
+    sm100::mbar_arrive_expect_tx(bar_q, Q_BYTES);
     sm100::tma_load_4d(sQ, &tq, 0, q0, h, b, bar_q);
     load_kv(0, 0);
   }
@@ -164,21 +172,23 @@ outlier_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
     wait(bar_s, j & 1);
     sm100::tc_fence_after();
 
-    // ---- pass 1: row max of this tile -------------------------------------
-    const int k0 = j * kTile;
-    const bool masked = k0 + kTile - 1 > q0 + p.q_offset || k0 + kTile > p.Tk;
-    float mt = -INFINITY;
-#pragma unroll
-    for (int c = 0; c < kTile; c += 32) {
-      uint32_t r[32];
-      sm100::tmem_ld32(tS + lane_off + c, r);
-      sm100::tc_wait_ld();
+    // ---- the row's 64 scores of this tile, one TMEM round trip ------------
+    uint32_t r0[32], r1[32];
+    sm100::tmem_ld32(tS + lane_off, r0);
+    sm100::tmem_ld32(tS + lane_off + 32, r1);
+    sm100::tc_wait_ld();
+    const int k0 = j * kKeys;
+    const bool masked = k0 + kKeys - 1 > q0 + p.q_offset || k0 + kKeys > p.Tk;
+    if (masked) {
 #pragma unroll
       for (int i = 0; i < 32; ++i) {
-        const float s = __uint_as_float(r[i]);
-        mt = (masked && k0 + c + i > limit) ? mt : fmaxf(mt, s);
+        if (k0 + i > limit) r0[i] = __float_as_uint(-INFINITY);
+        if (k0 + 32 + i > limit) r1[i] = __float_as_uint(-INFINITY);
       }
     }
+    float mt = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) mt = fmaxf(mt, fmaxf(__uint_as_float(r0[i]), __uint_as_float(r1[i])));
     const float mts = mt * scale;
     const bool raise = mts > m_used + 8.f;
     const float factor = raise ? exp2f(m_used - mts) : 1.f;  // 0 on the first tile
@@ -197,36 +207,29 @@ outlier_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
         sm100::tmem_st32(tO + lane_off + c, r);
       }
     }
-    // ---- pass 2: P = exp2(s*scale - m) as 16-bit pairs over columns [0, 64)
+    // ---- P = exp2(s*scale - m) as 16-bit pairs over columns [0, 32) --------
+    uint32_t pk[32];
+    float ls = 0.f;
 #pragma unroll
-    for (int c = 0; c < kTile; c += 64) {
-      uint32_t r0[32], r1[32], pk[32];
-      sm100::tmem_ld32(tS + lane_off + c, r0);
-      sm100::tmem_ld32(tS + lane_off + c + 32, r1);
-      sm100::tc_wait_ld();
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        float e[4];
-        const uint32_t src[4] = {r0[2 * i], r0[2 * i + 1], r1[2 * i], r1[2 * i + 1]};
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const int key = k0 + c + (u < 2 ? 2 * i + u : 32 + 2 * i + (u - 2));
-          e[u] = (masked && key > limit) ? 0.f : exp2f(fmaf(__uint_as_float(src[u]), scale, -m_used));
-          l_sum += e[u];
-        }
-        pk[i] = pack2(e[0], e[1], BF16);
-        pk[16 + i] = pack2(e[2], e[3], BF16);
-      }
-      sm100::tmem_st32(tS + lane_off + c / 2, pk);
+    for (int i = 0; i < 16; ++i) {
+      const float e0 = exp2f(fmaf(__uint_as_float(r0[2 * i]), scale, -m_used));
+      const float e1 = exp2f(fmaf(__uint_as_float(r0[2 * i + 1]), scale, -m_used));
+      const float e2 = exp2f(fmaf(__uint_as_float(r1[2 * i]), scale, -m_used));
+      const float e3 = exp2f(fmaf(__uint_as_float(r1[2 * i + 1]), scale, -m_used));
+      ls += (e0 + e1) + (e2 + e3);
+      pk[i] = pack2(e0, e1, BF16);
+      pk[16 + i] = pack2(e2, e3, BF16);
     }
+    l_sum += ls;
+    sm100::tmem_st32(tS + lane_off, pk);
     sm100::tc_wait_st();
     sm100::tc_fence_before();
     __syncthreads();
     if (tid == 0 && !*verr) {
       sm100::tc_fence_after();
-      const uint64_t vdesc = sm100::smem_desc(sV[st], kTile * 128, 1024, sm100::kSwizzle128);
+      const uint64_t vdesc = sm100::smem_desc(sV[st], kKeys * 128, 1024, sm100::kSwizzle128);
 #pragma unroll
-      for (int kk = 0; kk < kTile / 16; ++kk)
+      for (int kk = 0; kk < kKeys / 16; ++kk)
         sm100::mma_ts(tO, tS + kk * 8, vdesc + (uint64_t)(kk * 2048 >> 4), IDESC_O, j > 0 || kk > 0);
       sm100::mma_commit(bar_o);
     }
@@ -257,7 +260,7 @@ outlier_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
   sm100::tc_fence_before();
   __syncthreads();
   if (*err_flag && tid == 0) atomicOr(&g_outlier_tc_status, 1);
-  if (warp == 0) sm100::tmem_dealloc(tmem, kTmemCols);
+  if (warp == 0) sm100::tmem_dealloc(tmem, NCOLS);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -277,12 +280,12 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 // 4-D map over [B, H, T, C] (dims innermost first: channels, T, H, B) with a
 // (box_c x 128 x 1 x 1) box.
 bool make_map(CUtensorMap* m, const void* ptr, bool bf16, int64_t C, int64_t T, int64_t H, int64_t B,
-              const int64_t* stride, int box_c, CUtensorMapSwizzle swz) {
+              const int64_t* stride, int box_c, int box_rows, CUtensorMapSwizzle swz) {
   auto fn = encode_fn();
   if (fn == nullptr) return false;
   cuuint64_t dims[4] = {(cuuint64_t)C, (cuuint64_t)T, (cuuint64_t)H, (cuuint64_t)B};
   cuuint64_t strides[3] = {(cuuint64_t)(stride[2] * 2), (cuuint64_t)(stride[1] * 2), (cuuint64_t)(stride[0] * 2)};
-  cuuint32_t box[4] = {(cuuint32_t)box_c, (cuuint32_t)kTile, 1, 1};
+  cuuint32_t box[4] = {(cuuint32_t)box_c, (cuuint32_t)box_rows, 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
   CUresult r = fn(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4,
                   const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
@@ -309,15 +312,15 @@ cudaError_t launch_dr(const OutlierParams& p, cudaStream_t st, bool* taken) {
   CUtensorMap mq, mk, mv;
   const CUtensorMapSwizzle qk_swz = R == 16 ? CU_TENSOR_MAP_SWIZZLE_32B
                                             : (R == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
-  if (!make_map(&mq, p.q, bf16, R, p.Tq, p.H, p.B, sq, R, qk_swz)) return cudaSuccess;
-  if (!make_map(&mk, p.k, bf16, R, p.Tk, p.H, p.B, sk, R, qk_swz)) return cudaSuccess;
-  if (!make_map(&mv, p.v, bf16, D, p.Tk, p.H, p.B, sv, 64, CU_TENSOR_MAP_SWIZZLE_128B)) return cudaSuccess;
+  if (!make_map(&mq, p.q, bf16, R, p.Tq, p.H, p.B, sq, R, kRows, qk_swz)) return cudaSuccess;
+  if (!make_map(&mk, p.k, bf16, R, p.Tk, p.H, p.B, sk, R, kKeys, qk_swz)) return cudaSuccess;
+  if (!make_map(&mv, p.v, bf16, D, p.Tk, p.H, p.B, sv, 64, kKeys, CU_TENSOR_MAP_SWIZZLE_128B)) return cudaSuccess;
   auto k = outlier_tc_kernel<T, D, R>;
   constexpr size_t smem = smem_bytes<D, R>();
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   *taken = true;
-  dim3 grid((p.Tq + kTile - 1) / kTile, p.H, p.B);
+  dim3 grid((p.Tq + kRows - 1) / kRows, p.H, p.B);
   k<<<grid, kThreads, smem, st>>>(mq, mk, mv, p);
   return cudaGetLastError();
 }

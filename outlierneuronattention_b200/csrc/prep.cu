@@ -1,4 +1,5 @@
-// Gates + RoPE + cache export for one (b, h, token) per warp.
+// Gates + RoPE + cache export: one thread per (token, head) with 16-byte row
+// accesses (prep_vec_kernel), or one warp per (token, head) for any strides.
 //
 // Replaces the layer's elementwise glue around the attention core
 // (src/HybridOutlierFactorizedAttention.py):
@@ -110,8 +111,111 @@ prep_kernel(const PrepParams p) {
   }
 }
 
+// Vector variant: one thread per (token, head), 16-byte loads/stores of whole
+// rows, the head's gate / mix weights staged in shared memory.  Needs unit
+// channel stride, 16-byte aligned rows and R % 8 == 0.
+constexpr int kVecThreads = 128;
+
+template <typename T, int D, int RMAX>  // RMAX == R (compile-time, so RoPE stays in registers)
+__global__ void __launch_bounds__(kVecThreads)
+prep_vec_kernel(const PrepParams p) {
+  constexpr int G = D / 8;  // 16-byte groups of 8 channels (2-byte types)
+  __shared__ float w_gate[2 * D], w_mix[2 * D];
+  const int h = blockIdx.y, b = blockIdx.z;
+  const int n = blockIdx.x * kVecThreads + threadIdx.x;
+  const bool has_mix = p.mix_w != nullptr;
+  for (int i = threadIdx.x; i < 2 * D; i += kVecThreads) {
+    w_gate[i] = ld_any(p.gate_w, p.dt_gw, h * p.sgw[0] + i * p.sgw[1]);
+    w_mix[i] = has_mix ? ld_any(p.mix_w, p.dt_mw, h * p.smw[0] + i * p.smw[1]) : 0.f;
+  }
+  __syncthreads();
+  if (n >= p.N) return;
+  T* qp = reinterpret_cast<T*>(p.q) + b * p.sq[0] + h * p.sq[1] + (int64_t)n * p.sq[2];
+  T* kp = reinterpret_cast<T*>(p.k) + b * p.sk[0] + h * p.sk[1] + (int64_t)n * p.sk[2];
+  float qo[RMAX > 0 ? RMAX : 1], ko[RMAX > 0 ? RMAX : 1];
+  float g = 0.f, ml = 0.f;
+#pragma unroll
+  for (int c = 0; c < G; ++c) {
+    float fq[8], fk[8];
+    vec8_to_f(*reinterpret_cast<const Vec8<T>*>(qp + 8 * c), fq);
+    vec8_to_f(*reinterpret_cast<const Vec8<T>*>(kp + 8 * c), fk);
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      g = fmaf(fq[e], w_gate[8 * c + e], g);
+      g = fmaf(fk[e], w_gate[D + 8 * c + e], g);
+      ml = fmaf(fq[e], w_mix[8 * c + e], ml);
+      ml = fmaf(fk[e], w_mix[D + 8 * c + e], ml);
+      if (8 * c + e < RMAX) { qo[8 * c + e] = fq[e]; ko[8 * c + e] = fk[e]; }
+    }
+  }
+  g += ld_any(p.gate_b, p.dt_gb, h * p.sgb);
+  st_any(p.log_gamma, p.dt_lg, b * p.slg[0] + h * p.slg[1] + (int64_t)n * p.slg[2],
+         -(fmaxf(g, 0.f) + log1pf(expf(-fabsf(g)))));
+  if (p.mix_out != nullptr) {
+    const float mlog = has_mix ? ml + ld_any(p.mix_b, p.dt_mb, h * p.smb) : ld_any(p.fixed_mix, p.dt_fm, h * p.sfm);
+    st_any(p.mix_out, p.dt_mo, b * p.smo[0] + h * p.smo[1] + (int64_t)n * p.smo[2], 1.f / (1.f + expf(-mlog)));
+  }
+  const int pos = (p.pos0_dev != nullptr ? *p.pos0_dev : p.pos0) + n;
+  if (RMAX > 0 && p.rope) {
+    constexpr int half = RMAX / 2;
+    const int prow = pos < 0 ? 0 : (pos < p.P ? pos : p.P - 1);
+    float qr[RMAX > 0 ? RMAX : 1], kr[RMAX > 0 ? RMAX : 1];
+#pragma unroll
+    for (int c = 0; c < RMAX; ++c) {
+      const float cs = ld_any(p.cos, p.dt_cs, (int64_t)prow * p.scos[0] + c * p.scos[1]);
+      const float sn = ld_any(p.sin, p.dt_cs, (int64_t)prow * p.ssin[0] + c * p.ssin[1]);
+      const float qh = c < half ? -qo[c + half] : qo[c - half];
+      const float kh = c < half ? -ko[c + half] : ko[c - half];
+      qr[c] = qo[c] * cs + qh * sn;
+      kr[c] = ko[c] * cs + kh * sn;
+    }
+#pragma unroll
+    for (int c = 0; c < RMAX / 8; ++c) {
+      T tq[8], tk[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) { tq[e] = from_f<T>(qr[8 * c + e]); tk[e] = from_f<T>(kr[8 * c + e]); }
+      *reinterpret_cast<uint4*>(qp + 8 * c) = *reinterpret_cast<const uint4*>(tq);
+      *reinterpret_cast<uint4*>(kp + 8 * c) = *reinterpret_cast<const uint4*>(tk);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) ko[8 * c + e] = kr[8 * c + e];
+    }
+  }
+  if (RMAX > 0 && p.cache_k != nullptr && pos >= 0 && pos < p.L) {
+    T* ck = reinterpret_cast<T*>(p.cache_k) + b * p.sck[0] + h * p.sck[1] + (int64_t)pos * p.sck[2];
+#pragma unroll
+    for (int c = 0; c < RMAX / 8; ++c) {
+      T tk[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) tk[e] = from_f<T>(ko[8 * c + e]);
+      *reinterpret_cast<uint4*>(ck + 8 * c) = *reinterpret_cast<const uint4*>(tk);
+    }
+  }
+  if (p.cache_v != nullptr && pos >= 0 && pos < p.L) {
+    const T* vp = reinterpret_cast<const T*>(p.v) + b * p.sv[0] + h * p.sv[1] + (int64_t)n * p.sv[2];
+    T* cv = reinterpret_cast<T*>(p.cache_v) + b * p.scv[0] + h * p.scv[1] + (int64_t)pos * p.scv[2];
+#pragma unroll
+    for (int c = 0; c < G; ++c) *reinterpret_cast<uint4*>(cv + 8 * c) = *reinterpret_cast<const uint4*>(vp + 8 * c);
+  }
+}
+
 template <typename T>
 cudaError_t launch_t(const PrepParams& p, cudaStream_t st) {
+  if constexpr (sizeof(T) == 2) {
+    if (p.vec) {
+      const dim3 grid((unsigned)((p.N + kVecThreads - 1) / kVecThreads), p.H, p.B);
+      const int r = p.rope ? p.R : 0;
+      bool launched = true;
+#define HOFA_PREP_VEC(DD, RR) \
+  else if (p.D == DD && r == RR) prep_vec_kernel<T, DD, RR><<<grid, kVecThreads, 0, st>>>(p);
+      if (false) {}
+      HOFA_PREP_VEC(64, 0) HOFA_PREP_VEC(64, 8) HOFA_PREP_VEC(64, 16) HOFA_PREP_VEC(64, 32)
+      HOFA_PREP_VEC(128, 0) HOFA_PREP_VEC(128, 16) HOFA_PREP_VEC(128, 32) HOFA_PREP_VEC(128, 64)
+      HOFA_PREP_VEC(32, 0) HOFA_PREP_VEC(32, 8) HOFA_PREP_VEC(32, 16)
+      else launched = false;
+#undef HOFA_PREP_VEC
+      if (launched) return cudaGetLastError();
+    }
+  }
   const int64_t total = (int64_t)p.B * p.H * p.N;
   const dim3 grid((unsigned)((total + kPrepWarps - 1) / kPrepWarps));
   switch (p.D) {

@@ -1,0 +1,63 @@
+"""hofa_prep_fwd (gates, logsigmoid, RoPE in place, cache rows) against the
+reference's formulas (src/HybridOutlierFactorizedAttention.py:67-95, 176-198,
+365-384; src/modules/modules.py:33-45) evaluated in float64 on the same inputs.
+Both kernels are covered: the 16-byte-row kernel (bf16 views of a
+projection output) and the warp-per-token kernel (strided / float32)."""
+import pytest
+import torch
+import torch.nn.functional as F
+
+from oracle.hofa_oracle import apply_rope, rope_cos_sin
+
+pytestmark = pytest.mark.gpu
+
+
+def reference(q, k, v, gw, gb, mw, mb, r, pos0, base=10000.0):
+    q, k, v = q.double(), k.double(), v.double()
+    D = q.shape[-1]
+    logits = torch.einsum("bhnf,hf->bhn", q, gw[:, :D].double()) + torch.einsum("bhnf,hf->bhn", k, gw[:, D:].double()) + gb.double().view(1, -1, 1)
+    ml = torch.einsum("bhnf,hf->bhn", q, mw[:, :D].double()) + torch.einsum("bhnf,hf->bhn", k, mw[:, D:].double()) + mb.double().view(1, -1, 1)
+    N = q.shape[2]
+    cos, sin = rope_cos_sin(r, pos0 + N, base)
+    cos, sin = cos[pos0:], sin[pos0:]
+    qr, kr = q.clone(), k.clone()
+    if r:
+        qr[..., :r] = apply_rope(q[..., :r], cos, sin)
+        kr[..., :r] = apply_rope(k[..., :r], cos, sin)
+    return F.logsigmoid(-logits), torch.sigmoid(ml), qr, kr
+
+
+@pytest.mark.parametrize("dtype,strided", [(torch.bfloat16, False), (torch.float16, False), (torch.float32, False),
+                                           (torch.bfloat16, True)])
+@pytest.mark.parametrize("D,r", [(64, 16), (64, 32), (128, 32), (64, 0)])
+def test_prep_matches_reference_formulas(dtype, strided, D, r):
+    from outlierneuronattention_b200.modules import RotaryEmbedding
+    from outlierneuronattention_b200.prep import prep
+    g = torch.Generator().manual_seed(D + r)
+    B, H, N, L, pos0 = 2, 3, 150, 300, 17
+    x = torch.randn(B, N, 3, H, D, generator=g)
+    if strided:  # channel stride 2: the warp-per-token kernel
+        x = torch.randn(B, N, 3, H, D, 2, generator=g)[..., 0]
+    xq, xk, xv = (x[:, :, i].transpose(1, 2) for i in range(3))  # [B,H,N,D] views
+    gw, mw = torch.randn(H, 2 * D, generator=g) * 0.3, torch.randn(H, 2 * D, generator=g) * 0.3
+    gb, mb = torch.randn(H, generator=g), torch.randn(H, generator=g)
+    qd, kd, vd = (t.to(dtype).cuda() for t in (xq, xk, xv))
+    ref_lg, ref_mix, ref_q, ref_k = reference(qd.cpu(), kd.cpu(), vd.cpu(), gw, gb, mw, mb, r, pos0)
+    lg = torch.empty(B, H, N, device="cuda")
+    mix = torch.empty(B, H, N, device="cuda", dtype=dtype)
+    ck = torch.zeros(B, H, L, max(r, 8), device="cuda", dtype=dtype)
+    cv = torch.zeros(B, H, L, D, device="cuda", dtype=dtype)
+    rope = RotaryEmbedding(max(r, 2)).cuda()
+    prep(qd, kd, vd, gw.cuda(), gb.cuda(), lg, mix_w=mw.cuda(), mix_b=mb.cuda(), mix_out=mix,
+         cos=rope.cos_cached, sin=rope.sin_cached, R=r, pos0=pos0, cache_k=ck if r else None, cache_v=cv,
+         use_rope=r > 0)
+    torch.cuda.synchronize()
+    tol = 1e-4 if dtype == torch.float32 else 2e-2
+    assert (lg.double().cpu() - ref_lg).abs().max().item() <= tol
+    assert (mix.double().cpu() - ref_mix).abs().max().item() <= tol
+    assert (qd.double().cpu() - ref_q).abs().max().item() <= tol * 4
+    assert (kd.double().cpu() - ref_k).abs().max().item() <= tol * 4
+    if r:
+        assert (ck[:, :, pos0:pos0 + N, :r].double().cpu() - ref_k[..., :r]).abs().max().item() <= tol * 4
+        assert ck[:, :, :pos0].abs().max().item() == 0 and ck[:, :, pos0 + N:].abs().max().item() == 0
+    assert torch.equal(cv[:, :, pos0:pos0 + N].cpu(), vd.cpu())
