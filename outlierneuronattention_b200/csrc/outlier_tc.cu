@@ -71,7 +71,7 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, bool bf16) {
 }
 
 template <typename T, int D, int R>
-__global__ void __launch_bounds__(kThreads, 3)
+__global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2)
 outlier_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                   const __grid_constant__ CUtensorMap tv, const OutlierParams p) {
   constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
@@ -89,8 +89,8 @@ outlier_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
   extern __shared__ unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* sQ = base;
-  unsigned char* sK[2] = {base + Q_SLOT, base + Q_SLOT + K_SLOT};
-  unsigned char* sV[2] = {base + Q_SLOT + 2 * K_SLOT, base + Q_SLOT + 2 * K_SLOT + V_BYTES};
+  unsigned char* const sK0 = base + Q_SLOT;                  // slot st at sK0 + st * K_SLOT
+  unsigned char* const sV0 = base + Q_SLOT + 2 * K_SLOT;     // slot st at sV0 + st * V_BYTES
   uint64_t* bars = reinterpret_cast<uint64_t*>(base + Q_SLOT + 2 * K_SLOT + 2 * V_BYTES);
   uint64_t* bar_q = bars + 0;
   uint64_t* bar_kv = bars + 1;  // [2]
@@ -132,10 +132,10 @@ outlier_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
 
   auto load_kv = [&](int j, int st) {
     sm100::mbar_arrive_expect_tx(&bar_kv[st], K_BYTES + V_BYTES);
-    sm100::tma_load_4d(sK[st], &tk, 0, j * kKeys, h, b, &bar_kv[st]);
+    sm100::tma_load_4d(sK0 + st * K_SLOT, &tk, 0, j * kKeys, h, b, &bar_kv[st]);
 #pragma unroll
     for (int g = 0; g < D / 64; ++g)
-      sm100::tma_load_4d(sV[st] + g * kKeys * 128, &tv, g * 64, j * kKeys, h, b, &bar_kv[st]);
+      sm100::tma_load_4d(sV0 + st * V_BYTES + g * kKeys * 128, &tv, g * 64, j * kKeys, h, b, &bar_kv[st]);
   };
   if (tid == 0) {
     sm100::mbar_arrive_expect_tx(bar_q, Q_BYTES);
@@ -164,7 +164,7 @@ outlier_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
     wait(&bar_kv[st], (j >> 1) & 1);
     if (tid == 0 && !*verr) {
       sm100::tc_fence_after();
-      const uint64_t kdesc = sm100::smem_desc(sK[st], 16, 8 * RB, SWZ);
+      const uint64_t kdesc = sm100::smem_desc(sK0 + st * K_SLOT, 16, 8 * RB, SWZ);
 #pragma unroll
       for (int ks = 0; ks < R / 16; ++ks) sm100::mma_ss(tS, qdesc + 2 * ks, kdesc + 2 * ks, IDESC_S, ks > 0);
       sm100::mma_commit(bar_s);
@@ -198,36 +198,47 @@ outlier_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
     // of O when any of them raised its max (the others multiply by 1)
     if (j > 0 && __any_sync(0xffffffffu, raise)) {
 #pragma unroll
-      for (int c = 0; c < D; c += 32) {
-        uint32_t r[32];
-        sm100::tmem_ld32(tO + lane_off + c, r);
+      for (int c = 0; c < D; c += 16) {
+        uint32_t r[16];
+        sm100::tmem_ld16(tO + lane_off + c, r);
         sm100::tc_wait_ld();
 #pragma unroll
-        for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * factor);
-        sm100::tmem_st32(tO + lane_off + c, r);
+        for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * factor);
+        sm100::tmem_st16(tO + lane_off + c, r);
       }
     }
-    // ---- P = exp2(s*scale - m) as 16-bit pairs over columns [0, 32) --------
-    uint32_t pk[32];
+    // ---- P = exp2(s*scale - m) as 16-bit pairs over columns [0, 32), written
+    // in two halves of 16 columns to keep the register count low
     float ls = 0.f;
+    {
+      uint32_t pk[16];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const float e0 = exp2f(fmaf(__uint_as_float(r0[2 * i]), scale, -m_used));
-      const float e1 = exp2f(fmaf(__uint_as_float(r0[2 * i + 1]), scale, -m_used));
-      const float e2 = exp2f(fmaf(__uint_as_float(r1[2 * i]), scale, -m_used));
-      const float e3 = exp2f(fmaf(__uint_as_float(r1[2 * i + 1]), scale, -m_used));
-      ls += (e0 + e1) + (e2 + e3);
-      pk[i] = pack2(e0, e1, BF16);
-      pk[16 + i] = pack2(e2, e3, BF16);
+      for (int i = 0; i < 16; ++i) {
+        const float e0 = exp2f(fmaf(__uint_as_float(r0[2 * i]), scale, -m_used));
+        const float e1 = exp2f(fmaf(__uint_as_float(r0[2 * i + 1]), scale, -m_used));
+        ls += e0 + e1;
+        pk[i] = pack2(e0, e1, BF16);
+      }
+      sm100::tmem_st16(tS + lane_off, pk);
+    }
+    {
+      uint32_t pk[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const float e2 = exp2f(fmaf(__uint_as_float(r1[2 * i]), scale, -m_used));
+        const float e3 = exp2f(fmaf(__uint_as_float(r1[2 * i + 1]), scale, -m_used));
+        ls += e2 + e3;
+        pk[i] = pack2(e2, e3, BF16);
+      }
+      sm100::tmem_st16(tS + lane_off + 16, pk);
     }
     l_sum += ls;
-    sm100::tmem_st32(tS + lane_off, pk);
     sm100::tc_wait_st();
     sm100::tc_fence_before();
     __syncthreads();
     if (tid == 0 && !*verr) {
       sm100::tc_fence_after();
-      const uint64_t vdesc = sm100::smem_desc(sV[st], kKeys * 128, 1024, sm100::kSwizzle128);
+      const uint64_t vdesc = sm100::smem_desc(sV0 + st * V_BYTES, kKeys * 128, 1024, sm100::kSwizzle128);
 #pragma unroll
       for (int kk = 0; kk < kKeys / 16; ++kk)
         sm100::mma_ts(tO, tS + kk * 8, vdesc + (uint64_t)(kk * 2048 >> 4), IDESC_O, j > 0 || kk > 0);
@@ -243,13 +254,13 @@ outlier_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
   const float inv = l_sum > 0.f ? mix / l_sum : 0.f;
   T* og = reinterpret_cast<T*>(p.out) + b * p.so[0] + h * p.so[1] + (int64_t)(store ? row : 0) * p.so[2];
 #pragma unroll
-  for (int c = 0; c < D; c += 32) {
-    uint32_t r[32];
-    sm100::tmem_ld32(tO + lane_off + c, r);  // warp-collective: every lane executes it
+  for (int c = 0; c < D; c += 16) {
+    uint32_t r[16];
+    sm100::tmem_ld16(tO + lane_off + c, r);  // warp-collective: every lane executes it
     sm100::tc_wait_ld();
     if (store) {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
+      for (int i = 0; i < 16; ++i) {
         const int64_t off = (int64_t)(c + i) * p.so[3];
         float o = __uint_as_float(r[i]) * inv;
         if (p.accumulate) o += to_f(og[off]);
@@ -536,8 +547,9 @@ cudaError_t launch_dr(const OutlierParams& p, cudaStream_t st, bool* taken) {
   if (!make_map(&mk, p.k, bf16, R, p.Tk, p.H, p.B, sk, R, kKeys, qk_swz)) return cudaSuccess;
   if (!make_map(&mv, p.v, bf16, D, p.Tk, p.H, p.B, sv, 64, kKeys, CU_TENSOR_MAP_SWIZZLE_128B)) return cudaSuccess;
   dim3 grid((p.Tq + kRows - 1) / kRows, p.H, p.B);
-  const char* nopipe = getenv("HOFA_OUTLIER_NO_PIPE");
-  if (D == 64 && !(nopipe != nullptr && nopipe[0] != '\0' && nopipe[0] != '0')) {
+  // the pipelined variant (two CTAs per SM) is opt-in: the four-CTA kernel below is faster at r=16
+  const char* pipe = getenv("HOFA_OUTLIER_PIPE");
+  if (D == 64 && pipe != nullptr && pipe[0] != '\0' && pipe[0] != '0') {
     auto k = outlier_tc_pipe_kernel<T, R>;
     constexpr size_t smem = pipe_smem_bytes<R>();
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
