@@ -2,27 +2,33 @@
 //
 // Replaces the reference's Triton kernel _fwd_kernel (src/exact_attention.py:
 // 45-161): out += mix * softmax(sm_scale * q_r k_r^T, causal) v with r = R
-// query/key channels and D value channels.  One CTA of 128 threads owns 128
-// query rows of one (b,h); thread i owns row i, which is TMEM lane i.  Keys
-// come in tiles of 64, so S/P (64 columns) and O (64 columns at head dim 64)
-// fit in 128 TMEM columns and three to four CTAs share an SM.
+// query/key channels and D value channels.  One CTA owns 128 query rows of
+// one (b,h): warps 0-3 run the softmax (thread i owns row i, which is TMEM
+// lane i) and warp 4 issues every TMA copy and MMA.  Keys come in tiles of 32.
 //
-//   TMA (4-D tiled maps over [B,H,T,channels], no multicast) brings the Q
-//   tile once and K/V tiles of 128 keys into a two-stage shared-memory ring.
-//   Q/K tiles are K-major with R*2-byte swizzled rows; V tiles are MN-major
-//   with 128-byte swizzled rows (as stored in memory), so no transposition.
-//   Per key tile:
-//     S   = Q K^T            tcgen05.mma kind::f16, A/B from shared memory,
-//                             fp32 accumulator in TMEM columns [0, 64)
-//     P   = exp2(S*c - m)    every thread reads its row of S from TMEM in one
-//                             round trip (row max, then exponentials), writes
-//                             P as bf16/f16 pairs over columns [0, 32)
-//     O  += P V              tcgen05.mma with A = P from TMEM, B = V from
-//                             shared memory, fp32 accumulator in TMEM
-//                             columns [64, 64 + D)
-//   The running max is only raised when a row's max grows by more than 2^8
-//   (then the row of O is rescaled in TMEM); otherwise P is formed against the
-//   stale max, which changes nothing but the common factor removed at the end.
+//   TMEM: two S/P buffers of 32 fp32 columns and O (D fp32 columns); 128
+//   columns in all at head dim 64, so four CTAs share an SM.
+//   Shared memory: the Q tile and 4-stage K and V rings filled by TMA (4-D
+//   tiled maps over [B,H,T,channels], no multicast).
+//
+//   Issuer, step t:  S_t = Q K_t^T into buffer t%2 (once O += P_{t-2} V_{t-2},
+//                    the buffer's last reader, is done), then
+//                    O += P_{t-1} V_{t-1} once P_{t-1} is complete
+//                    (tcgen05.mma kind::f16; P from TMEM, V from shared memory)
+//   Softmax, tile t: load the row of S_t from TMEM, row max, P = exp2(S*c - m)
+//                    as 16-bit pairs written back over the first 16 columns of
+//                    the same buffer, arrive on the buffer's P barrier.
+//   S_{t+1} is computed while the softmax of tile t runs, and the softmax
+//   never waits for a P V product except to rescale O.
+//
+// The running max is raised only when a row's max grows by more than 2^64
+// (bf16; 2^8 for f16, whose largest value is 65504) -- then the row of O is
+// rescaled in TMEM; otherwise P is formed against the stale max, which
+// changes nothing but the common factor removed at the end.
+//
+// Exponentials: a share of the exp2 evaluations of each full (unmasked) tile
+// runs on the FMA pipe as a cubic polynomial (exp2_pair_poly), the rest on the
+// MUFU unit, so that neither unit alone bounds the softmax.
 //
 // Every mbarrier wait is bounded; on a timeout the CTA records an error in
 // g_outlier_tc_status, skips the rest of its work, frees its TMEM and exits.
@@ -41,21 +47,32 @@ __device__ int g_outlier_tc_status;
 
 namespace {
 
-constexpr int kRows = 128;        // query rows per CTA (TMEM lanes)
-constexpr int kKeys = 64;         // keys per tile
-constexpr int kThreads = 128;
+constexpr int kRows = 128;         // query rows per CTA (TMEM lanes)
+constexpr int kKeys = 32;          // keys per tile
+constexpr int kSoftmaxWarps = 4;
+constexpr int kThreads = 32 * (kSoftmaxWarps + 1);
+constexpr int kStages = 4;         // K and V ring depth
+constexpr int kEmuDefault = 0;     // of every 8 exp2 pairs of a full tile, this many run on the FMA pipe
 
-// TMEM columns: S / P in [0, kKeys), O in [kKeys, kKeys + D), rounded up to a power of two
+// TMEM columns: S/P buffers in [0, 2*kKeys), O in [2*kKeys, 2*kKeys + D), rounded up to a power of two
 template <int D>
-constexpr uint32_t tmem_cols() { return kKeys + D <= 128 ? 128 : 256; }
+constexpr uint32_t tmem_cols() { return 2 * kKeys + D <= 128 ? 128 : 256; }
+
+constexpr uint32_t round1k(uint32_t b) { return (b + 1023u) & ~1023u; }
 
 template <int D, int R>
-constexpr size_t smem_bytes() {
-  constexpr size_t q = ((size_t)kRows * R * 2 + 1023) & ~size_t(1023);
-  constexpr size_t k = ((size_t)kKeys * R * 2 + 1023) & ~size_t(1023);
-  constexpr size_t v = (size_t)kKeys * D * 2;
-  return 1024 + q + 2 * k + 2 * v + 64;
-}
+struct Smem {
+  static constexpr uint32_t RB = R * 2;                       // bytes per Q/K row
+  static constexpr uint32_t Q_BYTES = kRows * RB;
+  static constexpr uint32_t K_BYTES = kKeys * RB;
+  static constexpr uint32_t V_BYTES = kKeys * D * 2;
+  static constexpr uint32_t K_SLOT = round1k(K_BYTES);
+  static constexpr uint32_t V_SLOT = round1k(V_BYTES);
+  static constexpr uint32_t OFF_K = round1k(Q_BYTES);
+  static constexpr uint32_t OFF_V = OFF_K + kStages * K_SLOT;
+  static constexpr uint32_t OFF_BAR = OFF_V + kStages * V_SLOT;
+  static constexpr size_t BYTES = 1024 + OFF_BAR + 256;       // + alignment slack, barriers
+};
 
 constexpr uint32_t swizzle_mode(int row_bytes) {
   return row_bytes == 32 ? sm100::kSwizzle32 : (row_bytes == 64 ? sm100::kSwizzle64 : sm100::kSwizzle128);
@@ -70,255 +87,102 @@ __device__ __forceinline__ uint32_t pack2(float a, float b, bool bf16) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-template <typename T, int D, int R>
+// 2^x for two fp32 lanes without the MUFU unit (packed f32x2 FMA-pipe math).
+// Range reduction 2^x = 2^n * 2^f with n = floor(x) and f = x - n in [0, 1):
+// adding 1.5*2^23 with round-toward-minus-infinity leaves n in the low
+// mantissa bits of t, so t - 1.5*2^23 = n exactly and (bits(t) << 23) is n
+// shifted into the exponent field.  2^f is a cubic fitted to minimise the
+// maximum relative error over [0, 1) (a linear programme over 4001 points):
+// max relative error 7.5e-5, below the 2^-9 rounding of the 16-bit P that the
+// P V product consumes.  x is clamped at -126 so that the exponent field never
+// underflows into the sign bit (2^-126 is zero for every later use).
+__device__ __forceinline__ void exp2_pair_poly(uint64_t x2, float& e0, float& e1) {
+  constexpr float kMagic = 12582912.0f;  // 1.5 * 2^23
+  constexpr float kC0 = 0.99992525577545166f, kC1 = 0.69583284854888916f;
+  constexpr float kC2 = 0.22606939077377319f, kC3 = 0.078023009002208710f;
+  float x0, x1;
+  sm100::f2_unpack(x2, x0, x1);
+  const uint64_t x = sm100::f2_pack(fmaxf(x0, -126.f), fmaxf(x1, -126.f));
+  const uint64_t magic = sm100::f2_pack(kMagic, kMagic);
+  const uint64_t t = sm100::f2_add_rm(x, magic);
+  const uint64_t f = sm100::f2_sub(x, sm100::f2_sub(t, magic));
+  uint64_t p = sm100::f2_fma(sm100::f2_pack(kC3, kC3), f, sm100::f2_pack(kC2, kC2));
+  p = sm100::f2_fma(p, f, sm100::f2_pack(kC1, kC1));
+  p = sm100::f2_fma(p, f, sm100::f2_pack(kC0, kC0));
+  float p0, p1, t0, t1;
+  sm100::f2_unpack(p, p0, p1);
+  sm100::f2_unpack(t, t0, t1);
+  e0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
+  e1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
+}
+
+// Row of 32 scores -> 32 probabilities packed as 16-bit pairs in pk[16]
+// (pair i = columns 2i, 2i+1); returns the row sum in fp32.  E of every 8
+// pairs use the polynomial, the rest the MUFU unit.
+template <bool BF16, int E>
+__device__ __forceinline__ float row_exp(const uint32_t (&r)[32], float scale, float m, uint32_t (&pk)[16]) {
+  const uint64_t sc2 = sm100::f2_pack(scale, scale);
+  const uint64_t nm2 = sm100::f2_pack(-m, -m);
+  uint64_t acc[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) acc[i] = sm100::f2_pack(0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < 16; ++i) {
+    const uint64_t x =
+        sm100::f2_fma(sm100::f2_pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), sc2, nm2);
+    float e0, e1;
+    if ((i & 7) < E) {
+      exp2_pair_poly(x, e0, e1);
+    } else {
+      float x0, x1;
+      sm100::f2_unpack(x, x0, x1);
+      e0 = sm100::ex2_approx(x0);
+      e1 = sm100::ex2_approx(x1);
+    }
+    acc[i & 3] = sm100::f2_add(acc[i & 3], sm100::f2_pack(e0, e1));
+    pk[i] = pack2(e0, e1, BF16);
+  }
+  const uint64_t t = sm100::f2_add(sm100::f2_add(acc[0], acc[1]), sm100::f2_add(acc[2], acc[3]));
+  float a, b;
+  sm100::f2_unpack(t, a, b);
+  return a + b;
+}
+
+template <typename T, int D, int R, int EMU>
 __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2)
 outlier_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                   const __grid_constant__ CUtensorMap tv, const OutlierParams p) {
+  using L = Smem<D, R>;
   constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
-  constexpr int RB = R * 2;                       // bytes per Q/K row
-  constexpr uint32_t Q_BYTES = kRows * RB;
-  constexpr uint32_t K_BYTES = kKeys * RB;
-  constexpr uint32_t V_BYTES = kKeys * D * 2;
-  constexpr uint32_t Q_SLOT = (Q_BYTES + 1023) & ~1023u;
-  constexpr uint32_t K_SLOT = (K_BYTES + 1023) & ~1023u;
-  constexpr uint32_t SWZ = swizzle_mode(RB);
+  constexpr uint32_t SWZ = swizzle_mode(L::RB);
   constexpr uint32_t IDESC_S = sm100::idesc_f16(BF16, false, false, kRows, kKeys);
   constexpr uint32_t IDESC_O = sm100::idesc_f16(BF16, false, true, kRows, D);
   constexpr uint32_t NCOLS = tmem_cols<D>();
+  // lazy rescale threshold (log2 units): P values stay below 2^kRaise.  bf16
+  // P and the fp32 row sums and O share fp32's exponent range, so 2^64 (and
+  // a row sum below 2^64 times the key count) is far from overflow; f16 P
+  // (largest value 65504) keeps a margin at 2^8
+  constexpr float kRaise = BF16 ? 64.f : 8.f;
 
   extern __shared__ unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  unsigned char* sQ = base;
-  unsigned char* const sK0 = base + Q_SLOT;                  // slot st at sK0 + st * K_SLOT
-  unsigned char* const sV0 = base + Q_SLOT + 2 * K_SLOT;     // slot st at sV0 + st * V_BYTES
-  uint64_t* bars = reinterpret_cast<uint64_t*>(base + Q_SLOT + 2 * K_SLOT + 2 * V_BYTES);
+  unsigned char* const sQ = base;
+  unsigned char* const sK0 = base + L::OFF_K;   // slot s at sK0 + s * K_SLOT
+  unsigned char* const sV0 = base + L::OFF_V;   // slot s at sV0 + s * V_SLOT
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + L::OFF_BAR);
   uint64_t* bar_q = bars + 0;
-  uint64_t* bar_kv = bars + 1;  // [2]
-  uint64_t* bar_s = bars + 3;
-  uint64_t* bar_o = bars + 4;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 6);
-  int* err_flag = reinterpret_cast<int*>(bars + 7);
-
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int nqb = (p.Tq + kRows - 1) / kRows;
-  const int qb = nqb - 1 - (int)blockIdx.x;     // long causal rows first
-  const int h = blockIdx.y, b = blockIdx.z;
-  const int q0 = qb * kRows;
-  const int last_key = min(p.Tk - 1, q0 + kRows - 1 + p.q_offset);
-  const int ntiles = last_key / kKeys + 1;
-
-  if (tid == 0) {
-    sm100::mbar_init(bar_q, 1);
-    sm100::mbar_init(&bar_kv[0], 1);
-    sm100::mbar_init(&bar_kv[1], 1);
-    sm100::mbar_init(bar_s, 1);
-    sm100::mbar_init(bar_o, 1);
-    *err_flag = 0;
-    sm100::fence_mbar_init();
-    sm100::prefetch_tmap(&tq);
-    sm100::prefetch_tmap(&tk);
-    sm100::prefetch_tmap(&tv);
-  }
-  if (warp == 0) {
-    sm100::tmem_alloc(tmem_slot, NCOLS);
-    sm100::tmem_relinquish();
-  }
-  sm100::tc_fence_before();
-  __syncthreads();
-  sm100::tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  const uint32_t tS = tmem, tO = tmem + kKeys;
-  const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-
-  auto load_kv = [&](int j, int st) {
-    sm100::mbar_arrive_expect_tx(&bar_kv[st], K_BYTES + V_BYTES);
-    sm100::tma_load_4d(sK0 + st * K_SLOT, &tk, 0, j * kKeys, h, b, &bar_kv[st]);
-#pragma unroll
-    for (int g = 0; g < D / 64; ++g)
-      sm100::tma_load_4d(sV0 + st * V_BYTES + g * kKeys * 128, &tv, g * 64, j * kKeys, h, b, &bar_kv[st]);
-  };
-  if (tid == 0) {
-    sm100::mbar_arrive_expect_tx(bar_q, Q_BYTES);
-    sm100::tma_load_4d(sQ, &tq, 0, q0, h, b, bar_q);
-    load_kv(0, 0);
-  }
-
-  const float scale = p.qk_scale_log2;
-  const int row = q0 + tid;
-  const int limit = min(row + p.q_offset, p.Tk - 1);   // last visible key of this row
-  float m_used = -INFINITY, l_sum = 0.f;
-  // Bounded waits; after the first timeout in the CTA every later wait and
-  // MMA / copy issue is skipped, while the loop keeps its uniform trip count
-  // so that barriers and warp-collective TMEM accesses stay convergent.
-  volatile int* verr = err_flag;
-  auto wait = [&](uint64_t* bar, uint32_t parity) {
-    if (*verr) return;
-    if (!sm100::mbar_wait(bar, parity)) atomicOr(err_flag, 1);
-  };
-  wait(bar_q, 0);
-
-  const uint64_t qdesc = sm100::smem_desc(sQ, 16, 8 * RB, SWZ);
-  for (int j = 0; j < ntiles; ++j) {
-    const int st = j & 1;
-    if (tid == 0 && j + 1 < ntiles && !*verr) load_kv(j + 1, st ^ 1);
-    wait(&bar_kv[st], (j >> 1) & 1);
-    if (tid == 0 && !*verr) {
-      sm100::tc_fence_after();
-      const uint64_t kdesc = sm100::smem_desc(sK0 + st * K_SLOT, 16, 8 * RB, SWZ);
-#pragma unroll
-      for (int ks = 0; ks < R / 16; ++ks) sm100::mma_ss(tS, qdesc + 2 * ks, kdesc + 2 * ks, IDESC_S, ks > 0);
-      sm100::mma_commit(bar_s);
-    }
-    wait(bar_s, j & 1);
-    sm100::tc_fence_after();
-
-    // ---- the row's 64 scores of this tile, one TMEM round trip ------------
-    uint32_t r0[32], r1[32];
-    sm100::tmem_ld32(tS + lane_off, r0);
-    sm100::tmem_ld32(tS + lane_off + 32, r1);
-    sm100::tc_wait_ld();
-    const int k0 = j * kKeys;
-    const bool masked = k0 + kKeys - 1 > q0 + p.q_offset || k0 + kKeys > p.Tk;
-    if (masked) {
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        if (k0 + i > limit) r0[i] = __float_as_uint(-INFINITY);
-        if (k0 + 32 + i > limit) r1[i] = __float_as_uint(-INFINITY);
-      }
-    }
-    float mt = -INFINITY;
-#pragma unroll
-    for (int i = 0; i < 32; ++i) mt = fmaxf(mt, fmaxf(__uint_as_float(r0[i]), __uint_as_float(r1[i])));
-    const float mts = mt * scale;
-    const bool raise = mts > m_used + 8.f;
-    const float factor = raise ? exp2f(m_used - mts) : 1.f;  // 0 on the first tile
-    l_sum *= factor;
-    if (raise) m_used = mts;
-    // TMEM loads/stores are warp-collective: the whole warp rescales its rows
-    // of O when any of them raised its max (the others multiply by 1)
-    if (j > 0 && __any_sync(0xffffffffu, raise)) {
-#pragma unroll
-      for (int c = 0; c < D; c += 16) {
-        uint32_t r[16];
-        sm100::tmem_ld16(tO + lane_off + c, r);
-        sm100::tc_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 16; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * factor);
-        sm100::tmem_st16(tO + lane_off + c, r);
-      }
-    }
-    // ---- P = exp2(s*scale - m) as 16-bit pairs over columns [0, 32), written
-    // in two halves of 16 columns to keep the register count low
-    float ls = 0.f;
-    {
-      uint32_t pk[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float e0 = exp2f(fmaf(__uint_as_float(r0[2 * i]), scale, -m_used));
-        const float e1 = exp2f(fmaf(__uint_as_float(r0[2 * i + 1]), scale, -m_used));
-        ls += e0 + e1;
-        pk[i] = pack2(e0, e1, BF16);
-      }
-      sm100::tmem_st16(tS + lane_off, pk);
-    }
-    {
-      uint32_t pk[16];
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const float e2 = exp2f(fmaf(__uint_as_float(r1[2 * i]), scale, -m_used));
-        const float e3 = exp2f(fmaf(__uint_as_float(r1[2 * i + 1]), scale, -m_used));
-        ls += e2 + e3;
-        pk[i] = pack2(e2, e3, BF16);
-      }
-      sm100::tmem_st16(tS + lane_off + 16, pk);
-    }
-    l_sum += ls;
-    sm100::tc_wait_st();
-    sm100::tc_fence_before();
-    __syncthreads();
-    if (tid == 0 && !*verr) {
-      sm100::tc_fence_after();
-      const uint64_t vdesc = sm100::smem_desc(sV0 + st * V_BYTES, kKeys * 128, 1024, sm100::kSwizzle128);
-#pragma unroll
-      for (int kk = 0; kk < kKeys / 16; ++kk)
-        sm100::mma_ts(tO, tS + kk * 8, vdesc + (uint64_t)(kk * 2048 >> 4), IDESC_O, j > 0 || kk > 0);
-      sm100::mma_commit(bar_o);
-    }
-    wait(bar_o, j & 1);
-    sm100::tc_fence_after();
-  }
-
-  // ---- epilogue: out = (accumulate ? out : 0) + mix * O / l ----------------
-  const bool store = row < p.Tq && !*verr;
-  const float mix = store ? ld_any(p.mix_g, p.dt_mg, b * p.smg[0] + h * p.smg[1] + (int64_t)row * p.smg[2]) : 0.f;
-  const float inv = l_sum > 0.f ? mix / l_sum : 0.f;
-  T* og = reinterpret_cast<T*>(p.out) + b * p.so[0] + h * p.so[1] + (int64_t)(store ? row : 0) * p.so[2];
-#pragma unroll
-  for (int c = 0; c < D; c += 16) {
-    uint32_t r[16];
-    sm100::tmem_ld16(tO + lane_off + c, r);  // warp-collective: every lane executes it
-    sm100::tc_wait_ld();
-    if (store) {
-#pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const int64_t off = (int64_t)(c + i) * p.so[3];
-        float o = __uint_as_float(r[i]) * inv;
-        if (p.accumulate) o += to_f(og[off]);
-        og[off] = from_f<T>(o);
-      }
-    }
-  }
-  sm100::tc_fence_before();
-  __syncthreads();
-  if (*err_flag && tid == 0) atomicOr(&g_outlier_tc_status, 1);
-  if (warp == 0) sm100::tmem_dealloc(tmem, NCOLS);
-}
-
-// ---------------------------------------------------------------------------
-// Pipelined variant for head dim 64: three S/P buffers in TMEM and a 4-deep
-// K/V ring let the tensor core run one tile ahead of the softmax:
-//   iteration j:  [issuer] S_{j+1} = Q K_{j+1}^T into buffer (j+1)%3
-//                 softmax of S_j -> P_j in buffer j%3
-//                 [issuer] O += P_j V_j; K/V of tile j+3 -> ring slot (j+3)%4
-// so neither MMA round trip sits on the softmax's critical path.  Every MMA
-// group commits to its own buffer's mbarrier, so a parity wait never spans
-// more than one phase.
-// ---------------------------------------------------------------------------
-template <typename T, int R>
-__global__ void __launch_bounds__(kThreads, 2)
-outlier_tc_pipe_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                       const __grid_constant__ CUtensorMap tv, const OutlierParams p) {
-  constexpr int D = 64;
-  constexpr int NKV = 4, NS = 3;
-  constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
-  constexpr int RB = R * 2;
-  constexpr uint32_t Q_BYTES = kRows * RB;
-  constexpr uint32_t K_BYTES = kKeys * RB;
-  constexpr uint32_t V_BYTES = kKeys * D * 2;
-  constexpr uint32_t Q_SLOT = (Q_BYTES + 1023) & ~1023u;
-  constexpr uint32_t K_SLOT = (K_BYTES + 1023) & ~1023u;
-  constexpr uint32_t SWZ = swizzle_mode(RB);
-  constexpr uint32_t IDESC_S = sm100::idesc_f16(BF16, false, false, kRows, kKeys);
-  constexpr uint32_t IDESC_O = sm100::idesc_f16(BF16, false, true, kRows, D);
-  constexpr uint32_t NCOLS = 256;
-  constexpr uint32_t COL_O = NS * kKeys;
-
-  extern __shared__ unsigned char smem_raw[];
-  unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  unsigned char* sQ = base;
-  unsigned char* sK0 = base + Q_SLOT;
-  unsigned char* sV0 = sK0 + NKV * K_SLOT;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sV0 + NKV * V_BYTES);
-  uint64_t* bar_q = bars;
-  uint64_t* bar_kv = bars + 1;            // [NKV]
-  uint64_t* bar_s = bar_kv + NKV;         // [NS]
-  uint64_t* bar_o = bar_s + NS;           // [NS]
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_o + NS);
+  uint64_t* bar_k = bars + 1;                 // [kStages] K_t landed
+  uint64_t* bar_v = bar_k + kStages;          // [kStages] V_t landed
+  uint64_t* bar_s = bar_v + kStages;          // [2] S_t complete in buffer t%2
+  uint64_t* bar_p = bar_s + 2;                // [2] every softmax warp wrote P_t
+  uint64_t* bar_o = bar_p + 2;                // one phase per O += P V
+  uint64_t* bar_fin = bar_o + 1;              // the last O += P V is done
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_fin + 1);
   int* err_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
-  const int tid = threadIdx.x, warp = tid >> 5;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nqb = (p.Tq + kRows - 1) / kRows;
-  const int qb = nqb - 1 - (int)blockIdx.x;
+  const int qb = nqb - 1 - (int)blockIdx.x;     // long causal rows first
   const int h = blockIdx.y, b = blockIdx.z;
   const int q0 = qb * kRows;
   const int last_key = min(p.Tk - 1, q0 + kRows - 1 + p.q_offset);
@@ -326,13 +190,18 @@ outlier_tc_pipe_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
 
   if (tid == 0) {
     sm100::mbar_init(bar_q, 1);
-    for (int i = 0; i < NKV; ++i) sm100::mbar_init(&bar_kv[i], 1);
-    for (int i = 0; i < NS; ++i) { sm100::mbar_init(&bar_s[i], 1); sm100::mbar_init(&bar_o[i], 1); }
+    for (int i = 0; i < kStages; ++i) {
+      sm100::mbar_init(&bar_k[i], 1);
+      sm100::mbar_init(&bar_v[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      sm100::mbar_init(&bar_s[i], 1);
+      sm100::mbar_init(&bar_p[i], kSoftmaxWarps);
+    }
+    sm100::mbar_init(bar_o, 1);
+    sm100::mbar_init(bar_fin, 1);
     *err_flag = 0;
     sm100::fence_mbar_init();
-    sm100::prefetch_tmap(&tq);
-    sm100::prefetch_tmap(&tk);
-    sm100::prefetch_tmap(&tv);
   }
   if (warp == 0) {
     sm100::tmem_alloc(tmem_slot, NCOLS);
@@ -342,142 +211,180 @@ outlier_tc_pipe_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tO = tmem + COL_O;
-  const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+  const uint32_t tO = tmem + 2 * kKeys;
+
+  // Bounded waits.  The CTA's error flag is only read when a phase is not
+  // already complete; after the first timeout every later wait and every
+  // MMA / copy issue is skipped, while the loops keep their trip counts so
+  // that warp-collective TMEM accesses stay convergent.
   volatile int* verr = err_flag;
   auto wait = [&](uint64_t* bar, uint32_t parity) {
+    if (sm100::mbar_try_wait(bar, parity)) return;
     if (*verr) return;
-    if (!sm100::mbar_wait(bar, parity)) atomicOr(err_flag, 1);
+    if (!sm100::mbar_wait_sleep(bar, parity)) atomicOr(err_flag, 1);
   };
-  auto load_kv = [&](int t) {
-    const int st = t % NKV;
-    sm100::mbar_arrive_expect_tx(&bar_kv[st], K_BYTES + V_BYTES);
-    sm100::tma_load_4d(sK0 + st * K_SLOT, &tk, 0, t * kKeys, h, b, &bar_kv[st]);
-    sm100::tma_load_4d(sV0 + st * V_BYTES, &tv, 0, t * kKeys, h, b, &bar_kv[st]);
-  };
-  const uint64_t qdesc = sm100::smem_desc(sQ, 16, 8 * RB, SWZ);
-  auto issue_s = [&](int t) {  // S_t -> buffer t % NS
-    const uint64_t kdesc = sm100::smem_desc(sK0 + (t % NKV) * K_SLOT, 16, 8 * RB, SWZ);
+
+  if (warp == kSoftmaxWarps) {
+    // ---------------------------- issuer ------------------------------------
+    if (lane == 0) {
+      sm100::prefetch_tmap(&tq);
+      sm100::prefetch_tmap(&tk);
+      sm100::prefetch_tmap(&tv);
+      auto load_kv = [&](int t) {
+        const int s = t % kStages;
+        sm100::mbar_arrive_expect_tx(&bar_k[s], L::K_BYTES);
+        sm100::tma_load_4d(sK0 + s * L::K_SLOT, &tk, 0, t * kKeys, h, b, &bar_k[s]);
+        sm100::mbar_arrive_expect_tx(&bar_v[s], L::V_BYTES);
 #pragma unroll
-    for (int ks = 0; ks < R / 16; ++ks)
-      sm100::mma_ss(tmem + (t % NS) * kKeys, qdesc + 2 * ks, kdesc + 2 * ks, IDESC_S, ks > 0);
-    sm100::mma_commit(&bar_s[t % NS]);
-  };
-  if (tid == 0) {
-    sm100::mbar_arrive_expect_tx(bar_q, Q_BYTES);
-    sm100::tma_load_4d(sQ, &tq, 0, q0, h, b, bar_q);
-    for (int t = 0; t < 3 && t < n; ++t) load_kv(t);
-    wait(bar_q, 0);
-    wait(&bar_kv[0], 0);
-    if (!*verr) {
-      sm100::tc_fence_after();
-      issue_s(0);
-    }
-  }
-
-  const float scale = p.qk_scale_log2;
-  const int row = q0 + tid;
-  const int limit = min(row + p.q_offset, p.Tk - 1);
-  float m_used = -INFINITY, l_sum = 0.f;
-
-  for (int j = 0; j < n; ++j) {
-    // ---- issuer: S_{j+1} into buffer (j+1)%3 (its last reader PV_{j-2} done) --
-    if (tid == 0 && j + 1 < n && !*verr) {
-      if (j >= 2) wait(&bar_o[(j - 2) % NS], ((j - 2) / NS) & 1);
-      wait(&bar_kv[(j + 1) % NKV], ((j + 1) / NKV) & 1);
-      if (!*verr) {
+        for (int g = 0; g < D / 64; ++g)
+          sm100::tma_load_4d(sV0 + s * L::V_SLOT + g * kKeys * 128, &tv, g * 64, t * kKeys, h, b, &bar_v[s]);
+      };
+      const uint64_t qdesc = sm100::smem_desc(sQ, 16, 8 * L::RB, SWZ);
+      auto issue_pv = [&](int u) {  // O += P_u V_u
+        wait(&bar_p[u & 1], (u >> 1) & 1);
+        wait(&bar_v[u % kStages], (u / kStages) & 1);
+        if (*verr) return;
         sm100::tc_fence_after();
-        issue_s(j + 1);
-      }
-    }
-    // ---- softmax of S_j ------------------------------------------------------
-    wait(&bar_s[j % NS], (j / NS) & 1);
-    sm100::tc_fence_after();
-    const uint32_t tS = tmem + (j % NS) * kKeys;
-    uint32_t r0[32], r1[32];
-    sm100::tmem_ld32(tS + lane_off, r0);
-    sm100::tmem_ld32(tS + lane_off + 32, r1);
-    sm100::tc_wait_ld();
-    const int k0 = j * kKeys;
-    const bool masked = k0 + kKeys - 1 > q0 + p.q_offset || k0 + kKeys > p.Tk;
-    if (masked) {
+        const uint64_t vdesc =
+            sm100::smem_desc(sV0 + (u % kStages) * L::V_SLOT, kKeys * 128, 1024, sm100::kSwizzle128);
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        if (k0 + i > limit) r0[i] = __float_as_uint(-INFINITY);
-        if (k0 + 32 + i > limit) r1[i] = __float_as_uint(-INFINITY);
-      }
-    }
-    float mt = -INFINITY;
+        for (int kk = 0; kk < kKeys / 16; ++kk)
+          sm100::mma_ts(tO, tmem + (u & 1) * kKeys + kk * 8, vdesc + (uint64_t)(kk * 2048 >> 4), IDESC_O,
+                        u > 0 || kk > 0);
+        sm100::mma_commit(bar_o);
+      };
+      sm100::mbar_arrive_expect_tx(bar_q, L::Q_BYTES);
+      sm100::tma_load_4d(sQ, &tq, 0, q0, h, b, bar_q);
+      for (int t = 0; t < kStages && t < n; ++t) load_kv(t);
+      wait(bar_q, 0);
+      for (int t = 0; t < n; ++t) {
+        if (t >= 2) {
+          // O += P_{t-2} V_{t-2} done: S/P buffer t%2 and the K/V slot of tile t-2 are free
+          wait(bar_o, (t - 2) & 1);
+          if (t + 2 < n && !*verr) load_kv(t + 2);
+        }
+        const int s = t % kStages;
+        wait(&bar_k[s], (t / kStages) & 1);
+        if (!*verr) {
+          sm100::tc_fence_after();
+          const uint64_t kdesc = sm100::smem_desc(sK0 + s * L::K_SLOT, 16, 8 * L::RB, SWZ);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) mt = fmaxf(mt, fmaxf(__uint_as_float(r0[i]), __uint_as_float(r1[i])));
-    const float mts = mt * scale;
-    const bool raise = mts > m_used + 8.f;
-    const float factor = raise ? exp2f(m_used - mts) : 1.f;
-    l_sum *= factor;
-    if (raise) m_used = mts;
-    if (j > 0 && __any_sync(0xffffffffu, raise)) {
-      wait(&bar_o[(j - 1) % NS], ((j - 1) / NS) & 1);  // O is stable once PV_{j-1} is done
+          for (int ks = 0; ks < R / 16; ++ks)
+            sm100::mma_ss(tmem + (t & 1) * kKeys, qdesc + 2 * ks, kdesc + 2 * ks, IDESC_S, ks > 0);
+          sm100::mma_commit(&bar_s[t & 1]);
+        }
+        if (t >= 1) issue_pv(t - 1);
+      }
+      issue_pv(n - 1);
+      sm100::mma_commit(bar_fin);
+    }
+  } else {
+    // ---------------------------- softmax -----------------------------------
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const float scale = p.qk_scale_log2;
+    const int row = q0 + tid;
+    const int limit = min(row + p.q_offset, p.Tk - 1);   // last visible key of this row
+    float m_used = -INFINITY, l_sum = 0.f;
+    for (int t = 0; t < n; ++t) {
+      const uint32_t tS = tmem + (t & 1) * kKeys + lane_off;
+      wait(&bar_s[t & 1], (t >> 1) & 1);
       sm100::tc_fence_after();
-#pragma unroll
-      for (int c = 0; c < D; c += 32) {
-        uint32_t r[32];
-        sm100::tmem_ld32(tO + lane_off + c, r);
-        sm100::tc_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * factor);
-        sm100::tmem_st32(tO + lane_off + c, r);
-      }
-    }
-    uint32_t pk[32];
-    float ls = 0.f;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const float e0 = exp2f(fmaf(__uint_as_float(r0[2 * i]), scale, -m_used));
-      const float e1 = exp2f(fmaf(__uint_as_float(r0[2 * i + 1]), scale, -m_used));
-      const float e2 = exp2f(fmaf(__uint_as_float(r1[2 * i]), scale, -m_used));
-      const float e3 = exp2f(fmaf(__uint_as_float(r1[2 * i + 1]), scale, -m_used));
-      ls += (e0 + e1) + (e2 + e3);
-      pk[i] = pack2(e0, e1, BF16);
-      pk[16 + i] = pack2(e2, e3, BF16);
-    }
-    l_sum += ls;
-    sm100::tmem_st32(tS + lane_off, pk);
-    sm100::tc_wait_st();
-    sm100::tc_fence_before();
-    __syncthreads();
-    // ---- issuer: O += P_j V_j; next K/V load into the slot PV_{j-1} freed ----
-    if (tid == 0 && !*verr) {
-      sm100::tc_fence_after();
-      const uint64_t vdesc = sm100::smem_desc(sV0 + (j % NKV) * V_BYTES, kKeys * 128, 1024, sm100::kSwizzle128);
-#pragma unroll
-      for (int kk = 0; kk < kKeys / 16; ++kk)
-        sm100::mma_ts(tO, tS + kk * 8, vdesc + (uint64_t)(kk * 2048 >> 4), IDESC_O, j > 0 || kk > 0);
-      sm100::mma_commit(&bar_o[j % NS]);
-      if (j + 3 < n) {
-        if (j >= 1) wait(&bar_o[(j - 1) % NS], ((j - 1) / NS) & 1);
-        if (!*verr) load_kv(j + 3);
-      }
-    }
-  }
-  wait(&bar_o[(n - 1) % NS], ((n - 1) / NS) & 1);
-  sm100::tc_fence_after();
+      uint32_t r[32];
+      sm100::tmem_ld32(tS, r);
+      sm100::tc_wait_ld();
 
-  const bool store = row < p.Tq && !*verr;
-  const float mix = store ? ld_any(p.mix_g, p.dt_mg, b * p.smg[0] + h * p.smg[1] + (int64_t)row * p.smg[2]) : 0.f;
-  const float inv = l_sum > 0.f ? mix / l_sum : 0.f;
-  T* og = reinterpret_cast<T*>(p.out) + b * p.so[0] + h * p.so[1] + (int64_t)(store ? row : 0) * p.so[2];
+      const int k0 = t * kKeys;
+      const bool masked = k0 + kKeys - 1 > q0 + p.q_offset || k0 + kKeys > p.Tk;
+      if (masked) {
 #pragma unroll
-  for (int c = 0; c < D; c += 32) {
-    uint32_t r[32];
-    sm100::tmem_ld32(tO + lane_off + c, r);
-    sm100::tc_wait_ld();
-    if (store) {
+        for (int i = 0; i < 32; ++i)
+          if (k0 + i > limit) r[i] = __float_as_uint(-INFINITY);
+      }
+      float mx[4];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        const int64_t off = (int64_t)(c + i) * p.so[3];
-        float o = __uint_as_float(r[i]) * inv;
-        if (p.accumulate) o += to_f(og[off]);
-        og[off] = from_f<T>(o);
+      for (int i = 0; i < 4; ++i)
+        mx[i] = sm100::fmax3(__uint_as_float(r[8 * i]), __uint_as_float(r[8 * i + 1]), __uint_as_float(r[8 * i + 2]));
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        mx[i] = sm100::fmax3(mx[i], __uint_as_float(r[8 * i + 3]), __uint_as_float(r[8 * i + 4]));
+        mx[i] = sm100::fmax3(mx[i], __uint_as_float(r[8 * i + 5]), __uint_as_float(r[8 * i + 6]));
+        mx[i] = fmaxf(mx[i], __uint_as_float(r[8 * i + 7]));
+      }
+      const float mts = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * scale;
+      const bool raise = mts > m_used + kRaise;
+      const float factor = raise ? sm100::ex2_approx(m_used - mts) : 1.f;  // 0 on the first tile
+      if (raise) m_used = mts;
+      // TMEM loads/stores are warp-collective: the whole warp rescales its rows
+      // of O when any of them raised its max (the others multiply by 1), once
+      // O += P_{t-1} V_{t-1} is done (O += P_{t-2} V_{t-2} completed before S_t
+      // was issued, so the parity wait sees the right phase)
+      if (t > 0 && __any_sync(0xffffffffu, raise)) {
+        wait(bar_o, (t - 1) & 1);
+        sm100::tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < D; c += 16) {
+          uint32_t o[16];
+          sm100::tmem_ld16(tO + lane_off + c, o);
+          sm100::tc_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
+          sm100::tmem_st16(tO + lane_off + c, o);
+        }
+      }
+      uint32_t pk[16];
+      const float ls = masked ? row_exp<BF16, 0>(r, scale, m_used, pk)   // exact zeros where masked
+                              : row_exp<BF16, EMU>(r, scale, m_used, pk);
+      l_sum = l_sum * factor + ls;
+      sm100::tmem_st16(tS, pk);   // P_t over the first 16 columns of this row's S_t
+      sm100::tc_wait_st();
+      sm100::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) sm100::mbar_arrive(&bar_p[t & 1]);
+    }
+    wait(bar_fin, 0);
+    sm100::tc_fence_after();
+
+    // ---- epilogue: out = (accumulate ? out : 0) + mix * O / l --------------
+    const bool store = row < p.Tq && !*verr;
+    const float mix = store ? ld_any(p.mix_g, p.dt_mg, b * p.smg[0] + h * p.smg[1] + (int64_t)row * p.smg[2]) : 0.f;
+    const float inv = l_sum > 0.f ? mix / l_sum : 0.f;
+    T* og = reinterpret_cast<T*>(p.out) + b * p.so[0] + h * p.so[1] + (int64_t)(store ? row : 0) * p.so[2];
+    const bool vec = p.so[3] == 1 && (reinterpret_cast<uintptr_t>(og) & 15u) == 0;
+#pragma unroll
+    for (int c = 0; c < D; c += 16) {
+      uint32_t o[16];
+      sm100::tmem_ld16(tO + lane_off + c, o);  // warp-collective: every lane executes it
+      sm100::tc_wait_ld();
+      if (store && vec) {
+        uint4* dst = reinterpret_cast<uint4*>(og + c);
+        uint32_t w[8];
+        uint4 old[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
+        if (p.accumulate) {
+          old[0] = dst[0];
+          old[1] = dst[1];
+        }
+        const uint32_t* ow = reinterpret_cast<const uint32_t*>(old);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float a = __uint_as_float(o[2 * i]) * inv, bb = __uint_as_float(o[2 * i + 1]) * inv;
+          if (p.accumulate) {
+            float oa, ob;
+            if (BF16) bf16x2_to_f(ow[i], oa, ob); else f16x2_to_f(ow[i], oa, ob);
+            a += oa;
+            bb += ob;
+          }
+          w[i] = pack2(a, bb, BF16);
+        }
+        dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+        dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+      } else if (store) {
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int64_t off = (int64_t)(c + i) * p.so[3];
+          float v = __uint_as_float(o[i]) * inv;
+          if (p.accumulate) v += to_f(og[off]);
+          og[off] = from_f<T>(v);
+        }
       }
     }
   }
@@ -485,13 +392,6 @@ outlier_tc_pipe_kernel(const __grid_constant__ CUtensorMap tq, const __grid_cons
   __syncthreads();
   if (*err_flag && tid == 0) atomicOr(&g_outlier_tc_status, 1);
   if (warp == 0) sm100::tmem_dealloc(tmem, NCOLS);
-}
-
-template <int R>
-constexpr size_t pipe_smem_bytes() {
-  constexpr size_t q = ((size_t)kRows * R * 2 + 1023) & ~size_t(1023);
-  constexpr size_t k = ((size_t)kKeys * R * 2 + 1023) & ~size_t(1023);
-  return 1024 + q + 4 * k + 4 * (size_t)kKeys * 64 * 2 + 128;
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -532,6 +432,34 @@ bool tma_ok(const void* ptr, const int64_t* s, int64_t B, int64_t H) {
   return true;
 }
 
+// Dynamic shared memory per CTA: at least what the kernel uses, and enough
+// that no more CTAs are resident on an SM than its 512 TMEM columns serve (a
+// CTA beyond that would wait inside tcgen05.alloc for a neighbour to finish).
+size_t residency_smem(size_t need, uint32_t tmem_cols_per_cta) {
+  static int per_sm = -1, reserved = 0;
+  if (per_sm < 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) != cudaSuccess) per_sm = 0;
+    if (cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev) != cudaSuccess) reserved = 0;
+  }
+  const int fit = 512 / (int)tmem_cols_per_cta;                  // CTAs whose TMEM fits
+  const long cap = per_sm / (fit + 1) - reserved + 128;            // more than 1/(fit+1) of the SM each
+  return cap > (long)need ? (size_t)((cap + 127) & ~127L) : need;
+}
+
+template <typename T, int D, int R, int EMU>
+cudaError_t launch_kernel(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const OutlierParams& p,
+                          dim3 grid, cudaStream_t st, bool* taken) {
+  auto k = outlier_tc_kernel<T, D, R, EMU>;
+  const size_t smem = residency_smem(Smem<D, R>::BYTES, tmem_cols<D>());
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  *taken = true;
+  k<<<grid, kThreads, smem, st>>>(mq, mk, mv, p);
+  return cudaGetLastError();
+}
+
 template <typename T, int D, int R>
 cudaError_t launch_dr(const OutlierParams& p, cudaStream_t st, bool* taken) {
   const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
@@ -547,24 +475,16 @@ cudaError_t launch_dr(const OutlierParams& p, cudaStream_t st, bool* taken) {
   if (!make_map(&mk, p.k, bf16, R, p.Tk, p.H, p.B, sk, R, kKeys, qk_swz)) return cudaSuccess;
   if (!make_map(&mv, p.v, bf16, D, p.Tk, p.H, p.B, sv, 64, kKeys, CU_TENSOR_MAP_SWIZZLE_128B)) return cudaSuccess;
   dim3 grid((p.Tq + kRows - 1) / kRows, p.H, p.B);
-  // the pipelined variant (two CTAs per SM) is opt-in: the four-CTA kernel below is faster at r=16
-  const char* pipe = getenv("HOFA_OUTLIER_PIPE");
-  if (D == 64 && pipe != nullptr && pipe[0] != '\0' && pipe[0] != '0') {
-    auto k = outlier_tc_pipe_kernel<T, R>;
-    constexpr size_t smem = pipe_smem_bytes<R>();
-    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    *taken = true;
-    k<<<grid, kThreads, smem, st>>>(mq, mk, mv, p);
-    return cudaGetLastError();
+  // HOFA_OUTLIER_EMU (0, 2, 3) overrides how many of every 8 exp2 pairs of a
+  // full tile run as the FMA-pipe polynomial (bf16, head dim 64, r = 16)
+  if constexpr (std::is_same<T, __nv_bfloat16>::value && D == 64 && R == 16) {
+    const char* emu = getenv("HOFA_OUTLIER_EMU");
+    const int e = emu != nullptr && emu[0] != '\0' ? atoi(emu) : kEmuDefault;
+    if (e == 0) return launch_kernel<T, D, R, 0>(mq, mk, mv, p, grid, st, taken);
+    if (e == 3) return launch_kernel<T, D, R, 3>(mq, mk, mv, p, grid, st, taken);
+    if (e == 2) return launch_kernel<T, D, R, 2>(mq, mk, mv, p, grid, st, taken);
   }
-  auto k = outlier_tc_kernel<T, D, R>;
-  constexpr size_t smem = smem_bytes<D, R>();
-  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (e != cudaSuccess) return e;
-  *taken = true;
-  k<<<grid, kThreads, smem, st>>>(mq, mk, mv, p);
-  return cudaGetLastError();
+  return launch_kernel<T, D, R, kEmuDefault>(mq, mk, mv, p, grid, st, taken);
 }
 
 template <typename T, int D>
