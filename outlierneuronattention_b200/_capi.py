@@ -99,6 +99,10 @@ FORMATS = {cls: struct.Struct(_pack_format(cls)) for cls in (DecodeArgs, GlaArgs
 ABSENT = (0, 0, 0, 1, 1, 1, 1, 0, 0, 0, 0)
 
 
+_PAD_SHAPE = ((1, 1, 1, 1), (1, 1, 1), (1, 1), (1,), ())
+_PAD_STRIDE = ((0, 0, 0, 0), (0, 0, 0), (0, 0), (0,), ())
+
+
 def tview(t: Optional[torch.Tensor]):
     """The hofa_tensor fields of a CUDA tensor (or of an absent optional one)."""
     if t is None:
@@ -109,11 +113,11 @@ def tview(t: Optional[torch.Tensor]):
     if not t.is_cuda:
         raise ValueError("HOFA kernels take CUDA tensors only (this library has no CPU path)")
     nd = t.dim()
+    if nd == 4:
+        return (t.data_ptr(), code, 4, *t.shape, *t.stride())
     if nd > 4:
         raise ValueError(f"tensors of at most 4 dims, got {nd}")
-    shp = tuple(t.shape) + (1,) * (4 - nd)
-    std = tuple(t.stride()) + (0,) * (4 - nd)
-    return (t.data_ptr(), code, nd) + shp + std
+    return (t.data_ptr(), code, nd, *t.shape, *_PAD_SHAPE[nd], *t.stride(), *_PAD_STRIDE[nd])
 
 
 _lib = None
@@ -168,8 +172,8 @@ def flat(*items):
     """Flatten tensor views (tuples) and scalars into one value tuple."""
     out = []
     for it in items:
-        if isinstance(it, tuple):
-            out.extend(it)
+        if type(it) is tuple:
+            out += it
         else:
             out.append(it)
     return tuple(out)
