@@ -194,21 +194,24 @@ __global__ void __launch_bounds__(256) gla_tc_scan_kernel(const GlaParams p) {
   float* ws = p.ws_state + bh * p.nseg * p.J * 64 + e;
   const float* gc = p.ws_decay + bh * p.nseg;
   const int64_t cs = (int64_t)p.J * 64;
+  // 16 chunk contributions per round trip: their loads are independent, only
+  // the fmaf chain is sequential
+  constexpr int kU = 16;
   int c = 0;
-  for (; c + 4 <= p.nseg; c += 4) {
-    float dS[4], g[4];
+  for (; c + kU <= p.nseg; c += kU) {
+    float dS[kU], g[kU];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) { dS[u] = ws[(c + u) * cs]; g[u] = gc[c + u]; }
+    for (int u = 0; u < kU; ++u) { dS[u] = ws[(c + u) * cs]; g[u] = gc[c + u]; }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < kU; ++u) {
       ws[(c + u) * cs] = S;
-      S = fmaf(exp2f(g[u] * kLog2e), S, dS[u]);
+      S = fmaf(sm100::ex2_approx(g[u] * kLog2e), S, dS[u]);
     }
   }
   for (; c < p.nseg; ++c) {
     const float dS = ws[c * cs];
     ws[c * cs] = S;
-    S = fmaf(exp2f(gc[c] * kLog2e), S, dS);
+    S = fmaf(sm100::ex2_approx(gc[c] * kLog2e), S, dS);
   }
   if (p.state_out) p.state_out[b * p.sso[0] + h * p.sso[1] + j * p.sso[2] + d * p.sso[3]] = S;
 }
@@ -230,8 +233,9 @@ gla_tc_out_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
   unsigned char* sK = base + kTile;
   unsigned char* sV = base + 2 * kTile;
   unsigned char* sS = base + 3 * kTile;            // start state, [64 rows j][64 d] bf16, 8 KB
-  float* sG = reinterpret_cast<float*>(sS + 64 * 128);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sG + kC);
+  float* sG = reinterpret_cast<float*>(sS + 64 * 128);     // cumulative log2 decay per token
+  float* sGS = sG + kC;                                     // gla_scale[h, 0:64]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sGS + 64);
   float* sm_warp = reinterpret_cast<float*>(bars + 4);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm_warp + 4);
   int* err = reinterpret_cast<int*>(tmem_slot + 1);
@@ -282,8 +286,9 @@ gla_tc_out_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
   }
   const int t = t0 + tid;
   const float g = t < p.T ? ld_any(p.log_gamma, p.dt_lg, b * p.slg[0] + h * p.slg[1] + (int64_t)t * p.slg[2]) : 0.f;
-  const float G = block_scan128(g, sm_warp, tid);
+  const float G = block_scan128(g, sm_warp, tid) * kLog2e;   // log2 units from here on
   sG[tid] = G;
+  if (tid < 64) sGS[tid] = p.fuse ? ld_any(p.gla_scale, p.dt_gs, h * p.sgs[0] + tid * p.sgs[1]) : 1.f;
   float mix = 0.f;
   if (p.fuse && t < p.T) mix = ld_any(p.mix_g, p.dt_mg, b * p.smg[0] + h * p.smg[1] + (int64_t)t * p.smg[2]);
   fence_async_smem();
@@ -315,10 +320,10 @@ gla_tc_out_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
 #pragma unroll
     for (int u = 0; u < 16; ++u) {
       const int j0 = cc + 2 * u, j1 = cc + 32 + 2 * u;
-      const float a0 = j0 <= i ? __uint_as_float(r0[2 * u]) * exp2f((G - sG[j0]) * kLog2e) : 0.f;
-      const float a1 = j0 + 1 <= i ? __uint_as_float(r0[2 * u + 1]) * exp2f((G - sG[j0 + 1]) * kLog2e) : 0.f;
-      const float a2 = j1 <= i ? __uint_as_float(r1[2 * u]) * exp2f((G - sG[j1]) * kLog2e) : 0.f;
-      const float a3 = j1 + 1 <= i ? __uint_as_float(r1[2 * u + 1]) * exp2f((G - sG[j1 + 1]) * kLog2e) : 0.f;
+      const float a0 = j0 <= i ? __uint_as_float(r0[2 * u]) * sm100::ex2_approx(G - sG[j0]) : 0.f;
+      const float a1 = j0 + 1 <= i ? __uint_as_float(r0[2 * u + 1]) * sm100::ex2_approx(G - sG[j0 + 1]) : 0.f;
+      const float a2 = j1 <= i ? __uint_as_float(r1[2 * u]) * sm100::ex2_approx(G - sG[j1]) : 0.f;
+      const float a3 = j1 + 1 <= i ? __uint_as_float(r1[2 * u + 1]) * sm100::ex2_approx(G - sG[j1 + 1]) : 0.f;
       pk[u] = pack2(a0, a1, BF16);
       pk[16 + u] = pack2(a2, a3, BF16);
     }
@@ -340,7 +345,7 @@ gla_tc_out_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
 
   // epilogue: y = Y1 + exp(G_i) Y2, fused (1 - mix) * gla_scale * RMSNorm(y)
   float y[64];
-  const float eg = exp2f(G * kLog2e);
+  const float eg = sm100::ex2_approx(G);
 #pragma unroll
   for (int cc = 0; cc < 64; cc += 32) {
     uint32_t a[32], bb[32];
@@ -359,10 +364,19 @@ gla_tc_out_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
       scale = rsqrtf(ss / 64.f + p.eps) * (1.f - mix);
     }
     T* yp = reinterpret_cast<T*>(p.y) + b * p.sy[0] + h * p.sy[1] + (int64_t)t * p.sy[2];
+    if (p.sy[3] == 1 && (reinterpret_cast<uintptr_t>(yp) & 15u) == 0) {
 #pragma unroll
-    for (int d = 0; d < 64; ++d) {
-      const float gs = p.fuse ? ld_any(p.gla_scale, p.dt_gs, h * p.sgs[0] + d * p.sgs[1]) : 1.f;
-      yp[(int64_t)d * p.sy[3]] = from_f<T>(y[d] * scale * gs);
+      for (int d = 0; d < 64; d += 8) {
+        uint4 w;
+        w.x = pack2(y[d] * scale * sGS[d], y[d + 1] * scale * sGS[d + 1], BF16);
+        w.y = pack2(y[d + 2] * scale * sGS[d + 2], y[d + 3] * scale * sGS[d + 3], BF16);
+        w.z = pack2(y[d + 4] * scale * sGS[d + 4], y[d + 5] * scale * sGS[d + 5], BF16);
+        w.w = pack2(y[d + 6] * scale * sGS[d + 6], y[d + 7] * scale * sGS[d + 7], BF16);
+        *reinterpret_cast<uint4*>(yp + d) = w;
+      }
+    } else {
+#pragma unroll
+      for (int d = 0; d < 64; ++d) yp[(int64_t)d * p.sy[3]] = from_f<T>(y[d] * scale * sGS[d]);
     }
   }
   sm100::tc_fence_before();
