@@ -342,6 +342,8 @@ def run_ours(args):
            "gpu_launches": args.steps, "clocks": clocks}
     if not args.no_prefill:
         out["prefill"] = measure_prefill(dev)
+    if not args.no_config4 and world == 1:
+        out["config4"] = measure_config4(dev)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(B, args.cpu_seconds)
     if world > 1:
@@ -352,7 +354,7 @@ def run_ours(args):
 
 
 # ----------------------------------------------------------------------------- prefill
-def measure_prefill(dev, B=4, T=8192, steps=5, warmup=3):
+def measure_prefill(dev, B=4, T=8192, steps=5, warmup=3, name="config2"):
     """BASELINE config 2 prefill of the attention core (bf16, B=4, T=8192,
     H=16, d_h=64, r=16): gates + RoPE + cache export (hofa_prep_fwd), the
     chunked GLA (hofa_prefill_gla_fwd) and the tcgen05 outlier attention
@@ -406,12 +408,65 @@ def measure_prefill(dev, B=4, T=8192, steps=5, warmup=3):
     if os.path.exists(pk):
         bf16_peak = float(json.load(open(pk))["bf16_tflops"])
     ach = attn_flops / (ms["outlier"] / 1e3) / 1e12
-    return {"workload": f"config2-prefill-B{B}-T{T}", "tokens_per_s": round(B * T / (total / 1e3), 1),
+    return {"workload": f"{name}-prefill-B{B}-T{T}", "tokens_per_s": round(B * T / (total / 1e3), 1),
             "ms": round(total, 4), "ms_by_kernel": {k_: round(v_, 4) for k_, v_ in ms.items()},
             "algorithmic_flops": attn_flops + gla_flops, "exps": B * H * T * T // 2,
             "roofline_outlier_kernel": {"bound": "tensor", "achieved": round(ach, 2), "peak": bf16_peak,
                                         "unit": "TFLOP/s", "frac": round(ach / bf16_peak, 4),
                                         "peak_source": "measured bf16_tflops (burst)"}}
+
+
+def measure_config4(dev, steps=64, reps=3):
+    """BASELINE config 4 on one GPU: the attention core's prefill at B=1,
+    T=65536, and decode steps against a 65,600-token cache (B=1; two rotating
+    168 MB cache sets, so every step streams its cache from HBM; the steps are
+    replayed from a CUDA graph and timed with CUDA events)."""
+    from outlierneuronattention_b200 import _capi, fused_hofa_decode
+    out = {"workload": "config4-B1-T65536", "prefill": measure_prefill(dev, B=1, T=65536, steps=3, warmup=1,
+                                                                       name="config4")}
+    L4, B4 = 65600, 1
+    g = torch.Generator(device=dev).manual_seed(11)
+    sets = []
+    for _ in range(2):
+        ck = (torch.randn(B4, H, L4, R, device=dev, generator=g) * KEY_STD).to(torch.bfloat16)
+        cv = (torch.randn(B4, H, L4, D, device=dev, generator=g) * VAL_STD).to(torch.bfloat16)
+        sets.append((ck, cv))
+    inp = make_step_inputs(B4, "cpu", seed=4000)
+    q, k, v = (inp[n].to(dev) for n in ("q", "k", "v"))
+    lg, mix, nw = inp["log_gamma"].to(dev), inp["mix"].to(dev), inp["norm_w"].to(dev)
+    st = [torch.randn(B4, H, J, D, device=dev, generator=g) * 0.1, torch.empty(B4, H, J, D, device=dev)]
+
+    def launch(n):
+        for i in range(n):
+            ck, cv = sets[i % 2]
+            fused_hofa_decode(q, k, v, ck, cv, st[i % 2], st[(i + 1) % 2], lg, mix, nw, R, L4, 2.0)
+
+    stream = torch.cuda.Stream(dev)
+    with torch.cuda.stream(stream):
+        launch(4)
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            launch(steps)
+        graph.replay()
+        stream.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+        stream.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * steps)
+    del graph
+    nbytes = B4 * H * (L4 * (R + D) * 2 + J * D * 4 * 2)
+    peak, kind = peaks()
+    ach = nbytes / (us / 1e6) / 1e9
+    out["decode"] = {"batch": B4, "cache_len": L4, "us_per_step": round(us, 3),
+                     "tokens_per_s": round(B4 / (us / 1e6), 1), "algorithmic_bytes_per_step": nbytes,
+                     "split_k": int(_capi.lib().hofa_decode_choose_split(B4, H, L4, torch.cuda.get_device_properties(dev).multi_processor_count)),
+                     "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
+                                  "frac": round(ach / peak, 4), "peak_source": f"{kind} hbm_gbs"}}
+    return out
 
 
 # ----------------------------------------------------------------------------- CPU arm
@@ -470,6 +525,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-2 prefill measurement")
+    ap.add_argument("--no-config4", action="store_true",
+                    help="skip the config-4 (B=1, T=65536) prefill and long-cache decode measurement")
     ap.add_argument("--profile-prefill", action="store_true",
                     help="only the config-2 prefill kernels (for ncu captures); prints no bench line")
     ap.add_argument("--profile", action="store_true",
