@@ -344,6 +344,8 @@ def run_ours(args):
         out["prefill"] = measure_prefill(dev)
     if not args.no_config4 and world == 1:
         out["config4"] = measure_config4(dev)
+    if not args.no_config4 and world > 1:
+        out["config4_seqpar"] = measure_seqpar(dev, world)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(B, args.cpu_seconds)
     if world > 1:
@@ -467,6 +469,45 @@ def measure_config4(dev, steps=64, reps=3):
                      "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
                                   "frac": round(ach / peak, 4), "peak_source": f"{kind} hbm_gbs"}}
     return out
+
+
+def measure_seqpar(dev, world, steps=3, warmup=2):
+    """BASELINE config 4 prefill of the attention core (B=1, T=65536)
+    sequence-sharded over the ranks (zig-zag blocks; two GLA passes around
+    the block-state exchange, outlier attention against the all-gathered key
+    prefix).  Each rank draws its own tokens; the time per prefill is the max
+    over ranks of CUDA-event times around the whole sharded core, exchange
+    included."""
+    import torch.distributed as dist
+    from outlierneuronattention_b200 import seqpar
+    B4, T4 = 1, 65536
+    rank = dist.get_rank()
+    g = torch.Generator(device=dev).manual_seed(21 + rank)
+    Tl = T4 // world
+    x3 = torch.randn(B4, Tl, 3, H, D, device=dev, generator=g).to(torch.bfloat16)
+    q, k, v = (x3[:, :, i].transpose(1, 2) for i in range(3))
+    lg = torch.nn.functional.logsigmoid(torch.randn(B4, H, Tl, device=dev, generator=g)) / 16
+    mix = torch.sigmoid(torch.randn(B4, H, Tl, device=dev, generator=g)).to(torch.bfloat16)
+    gs = torch.ones(1, H, 1, D, device=dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    times = []
+    for it in range(warmup + steps):
+        dist.barrier()
+        torch.cuda.synchronize()
+        e0.record()
+        seqpar.sharded_attention_core(q, k, v, lg, mix, R, 2.0, gs, T4)
+        e1.record()
+        torch.cuda.synchronize()
+        if it >= warmup:
+            times.append(e0.elapsed_time(e1))
+    t = torch.tensor([statistics.median(times)], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = t.item()
+    return {"workload": f"config4-prefill-seqpar-B{B4}-T{T4}", "ranks": world, "ms": round(ms, 4),
+            "tokens_per_s": round(B4 * T4 / (ms / 1e3), 1),
+            "sharding": f"zig-zag: {2 * world} blocks of {T4 // (2 * world)} tokens, rank r owns r and {2 * world - 1}-r",
+            "exchange": "NCCL all_gather of K_O/V (async, overlaps the first GLA pass) and of GLA block states",
+            "timed": "gla (2 passes) + exchange + outlier attention, max over ranks"}
 
 
 # ----------------------------------------------------------------------------- CPU arm
