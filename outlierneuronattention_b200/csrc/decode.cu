@@ -96,15 +96,16 @@ __device__ __forceinline__ void warp_flush(float m_run, float l_run, float (&acc
 }
 
 // GLA rows [r0, r1) of (b,h): S' = gamma*S + k_I v^T -> state_out, and this
-// split's part of y_I = q_I S' -> sm_y (one row of partial sums per thread group).
-template <typename T, int D, bool ALPHA>
-__device__ __forceinline__ void gla_rows(const DecodeParams& p, int s, int b, int h, int tid, float (*sm_y)[D]) {
+// split's part of y_I = q_I S' -> sm_y (one row of partial sums per group of
+// D/4 threads).  Run by NT threads with indices t in [0, NT).
+template <typename T, int D, bool ALPHA, int NT>
+__device__ __forceinline__ void gla_rows(const DecodeParams& p, int s, int b, int h, int t, float (*sm_y)[D]) {
   constexpr int D4 = D / 4;
+  constexpr int RSUB = NT / D4;
   const int R = p.R, J = D - p.R;
   const int rows_per = (J + p.split_k - 1) / p.split_k;
   const int r0 = s * rows_per, r1 = min(J, r0 + rows_per);
-  const int c4 = tid % D4, rsub = tid / D4;
-  constexpr int RSUB = kConsumers / D4;
+  const int c4 = t % D4, rsub = t / D4;
   float ya[4] = {0.f, 0.f, 0.f, 0.f};
   if (r0 < r1) {
     const T* qp = reinterpret_cast<const T*>(p.q) + b * p.sq[0] + h * p.sq[1];
@@ -117,7 +118,7 @@ __device__ __forceinline__ void gla_rows(const DecodeParams& p, int s, int b, in
     const float gam_h = expf(lg);
     const float* sin_ = p.state_in + b * p.sst[0] + h * p.sst[1];
     float* sout = p.state_out + b * p.sso[0] + h * p.sso[1];
-#pragma unroll 2
+#pragma unroll 4
     for (int row = r0 + rsub; row < r1; row += RSUB) {
       const float kr = to_f(kp[(int64_t)(R + row) * p.sk[2]]);
       const float qr = to_f(qp[(int64_t)(R + row) * p.sq[2]]);
@@ -141,6 +142,21 @@ __device__ __forceinline__ void gla_rows(const DecodeParams& p, int s, int b, in
   for (int c = 0; c < 4; ++c) sm_y[rsub][4 * c4 + c] = ya[c];
 }
 
+// norm_w[h, d] and mix[b, h] for the epilogue, read at the start of a kernel
+// (after the grid dependency) so that the epilogue does no global round trip.
+struct EpiloguePrefetch {
+  float nw = 0.f, mix = 0.f;
+};
+template <int D>
+__device__ __forceinline__ EpiloguePrefetch prefetch_epilogue(const DecodeParams& p, int b, int h, int d) {
+  EpiloguePrefetch e;
+  if (d < D) {
+    e.nw = ld_any(p.norm_w, p.dt_nw, h * p.snw[0] + d * p.snw[1]);
+    e.mix = ld_any(p.mix_g, p.dt_mg, b * p.smg[0] + h * p.smg[1]);
+  }
+  return e;
+}
+
 // CTA partial (m, l, acc[D], y_I[D]), cross-split combine, RMSNorm, blend,
 // store.  Called by every thread of the CTA after a __syncthreads() that
 // publishes sh / sm_acc / sm_y.  The splits of one (b,h) combine either
@@ -150,11 +166,10 @@ __device__ __forceinline__ void gla_rows(const DecodeParams& p, int s, int b, in
 //            trip, no fences, no atomics), or
 //   workspace: partials go to global memory and the last CTA to take a
 //            ticket combines them (any split count).
-template <typename T, int D, bool CLUSTER, int NW>
+template <typename T, int D, bool CLUSTER, int NW, int RSUB>
 __device__ __forceinline__ void finish(const DecodeParams& p, int s, int b, int h, int tid, int lane, int warp,
                                        int nwarps, DecShared& sh, float (*sm_acc)[D], float (*sm_y)[D],
-                                       float* sm_part) {
-  constexpr int RSUB = kConsumers / (D / 4);
+                                       float* sm_part, EpiloguePrefetch ep) {
   constexpr int PS = 4 + 2 * D;
   const int bh = b * p.H + h;
   float cta_m = -INFINITY;
@@ -239,10 +254,8 @@ __device__ __forceinline__ void finish(const DecodeParams& p, int s, int b, int 
   for (int w = 0; w < nwarps; ++w) ss += sh.red[w];
   if (d < D) {
     const float rs = rsqrtf(ss / (float)D + p.eps);
-    const float nw = ld_any(p.norm_w, p.dt_nw, h * p.snw[0] + d * p.snw[1]);
-    const float mix = ld_any(p.mix_g, p.dt_mg, b * p.smg[0] + h * p.smg[1]);
     const float yo = fin_l > 0.f ? fin_acc / fin_l : 0.f;
-    const float out = mix * yo + (1.f - mix) * (fin_y * rs * nw);
+    const float out = ep.mix * yo + (1.f - ep.mix) * (fin_y * rs * ep.nw);
     reinterpret_cast<T*>(p.y)[b * p.sy[0] + h * p.sy[1] + d * p.sy[2]] = from_f<T>(out);
   }
 }
@@ -291,6 +304,7 @@ decode_reg_kernel(const DecodeParams p) {
   const int t_begin = s * tps;
   const int t_end = min(seq_len, t_begin + tps);
   load_q<T, D>(p, b, h, tid, sm_q);
+  const EpiloguePrefetch ep = prefetch_epilogue<D>(p, b, h, tid);
   __syncthreads();
 
   const int cg = lane % G, ts = lane / G;
@@ -335,20 +349,24 @@ decode_reg_kernel(const DecodeParams p) {
     tile_update<T, D>(sc, vr, m_run, l_run, acc, ts);
   }
   warp_flush<D>(m_run, l_run, acc, lane, warp, sh, sm_acc);
-  gla_rows<T, D, ALPHA>(p, s, b, h, tid, sm_y);
+  gla_rows<T, D, ALPHA, kConsumers>(p, s, b, h, tid, sm_y);
   __syncthreads();
-  finish<T, D, false, kConsumerWarps>(p, s, b, h, tid, lane, warp, kConsumerWarps, sh, sm_acc, sm_y, nullptr);
+  finish<T, D, false, kConsumerWarps, RSUB>(p, s, b, h, tid, lane, warp, kConsumerWarps, sh, sm_acc, sm_y, nullptr,
+                                            ep);
 }
 
 // ============================================================================
 // TMA-bulk variant (cache rows contiguous: row stride R for K, D for V).
 // ============================================================================
 constexpr int kBulkChunk = 64;  // tokens per bulk chunk (two warp tiles)
+// Warps: NW consumers, then the TMA producer (warp NW), then the GLA warp
+// (warp NW + 1), which updates this split's GLA state rows and its part of
+// y_I while the consumers stream the cache.
 template <typename T, int D, bool ALPHA, bool CLUSTER, int NW>
-__global__ void __launch_bounds__(NW * 32 + 32)
+__global__ void __launch_bounds__(NW * 32 + 64)
 decode_bulk_kernel(const DecodeParams p) {
   constexpr int G = D / 8, TS = 32 / G, VI = 32 / TS;
-  constexpr int RSUB = kConsumers / (D / 4);
+  constexpr int RSUB = 32 / (D / 4);   // rows of sm_y written by the GLA warp
   const int NST = p.stages;
   const int s = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -394,6 +412,7 @@ decode_bulk_kernel(const DecodeParams p) {
   // the next kernel start scheduling.
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const EpiloguePrefetch ep = prefetch_epilogue<D>(p, b, h, tid);
   __syncthreads();  // barriers initialised; the producer starts streaming at once
 
   float m_run = -INFINITY, l_run = 0.f;
@@ -418,9 +437,11 @@ decode_bulk_kernel(const DecodeParams p) {
         sm100::bulk_g2s(sV + (size_t)st * kBulkChunk * D, vg + (size_t)t0 * D * sizeof(T), vbytes, &full_bar[st]);
       }
     }
+  } else if (warp == NW + 1) {
+    // ---------------- GLA warp: state rows and y_I, beside the streaming ---
+    gla_rows<T, D, ALPHA, 32>(p, s, b, h, lane, sm_y);
   } else {
-    // ---------------- consumers: GLA rows and q (overlap the first copies) -
-    if (tid < kConsumers) gla_rows<T, D, ALPHA>(p, s, b, h, tid, sm_y);
+    // ---------------- consumers: q, then the cache stream ------------------
     load_q<T, D>(p, b, h, tid, sm_q);
     asm volatile("bar.sync 1, %0;" ::"n"(NW * 32) : "memory");  // consumers only
     const int cg_ = lane % G, ts = lane / G;
@@ -464,7 +485,7 @@ decode_bulk_kernel(const DecodeParams p) {
   }
   __syncthreads();
   if (tid == 0 && sm_err) atomicOr(p.ws_status, 4 * sm_err);
-  finish<T, D, CLUSTER, NW>(p, s, b, h, tid, lane, warp, NW + 1, sh, sm_acc, sm_y, sm_part);
+  finish<T, D, CLUSTER, NW, RSUB>(p, s, b, h, tid, lane, warp, NW + 2, sh, sm_acc, sm_y, sm_part, ep);
 }
 
 template <typename T, int D, bool ALPHA, bool CLUSTER, int NW>
@@ -475,7 +496,7 @@ cudaError_t launch_bulk(const DecodeParams& p, cudaStream_t st) {
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.split_k, p.H, p.B);
-  cfg.blockDim = dim3(NW * 32 + 32);
+  cfg.blockDim = dim3(NW * 32 + 64);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = st;
   cudaLaunchAttribute attr[2];
