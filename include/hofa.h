@@ -95,8 +95,11 @@ size_t hofa_decode_workspace_size(int32_t B, int32_t H, int32_t D, int32_t max_s
  * replaces the heuristic at src/hofa_decode_triton.py:374-383. */
 int32_t hofa_decode_choose_split(int32_t B, int32_t H, int32_t seq_len, int32_t num_sms);
 
-/* Status word the decode kernel leaves in its workspace (0 = no fault; 1 =
- * seq_len_dev held a value outside [1, L] and was clamped), then clears it.
+/* Status word the decode kernel leaves in its workspace, then clears it.
+ * 0 = no fault; bits: 1 = seq_len_dev held a value outside [1, L] and was
+ * clamped; 4 / 8 = a ring wait of the TMA-bulk kernel timed out (producer /
+ * consumer); 16 = invalid ring configuration; 64 = the cluster combine's wait
+ * for the other splits timed out.
  * Synchronises `stream`; not for use inside graph capture. */
 int hofa_decode_read_status(void* workspace, void* stream, int32_t* status_out);
 

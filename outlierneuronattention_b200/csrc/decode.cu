@@ -169,7 +169,7 @@ __device__ __forceinline__ EpiloguePrefetch prefetch_epilogue(const DecodeParams
 template <typename T, int D, bool CLUSTER, int NW, int RSUB>
 __device__ __forceinline__ void finish(const DecodeParams& p, int s, int b, int h, int tid, int lane, int warp,
                                        int nwarps, DecShared& sh, float (*sm_acc)[D], float (*sm_y)[D],
-                                       float* sm_part, EpiloguePrefetch ep) {
+                                       float (*sm_all)[4 + 2 * D], uint64_t* comb_bar, EpiloguePrefetch ep) {
   constexpr int PS = 4 + 2 * D;
   const int bh = b * p.H + h;
   float cta_m = -INFINITY;
@@ -192,29 +192,38 @@ __device__ __forceinline__ void finish(const DecodeParams& p, int s, int b, int 
   if (p.split_k == 1) {
     fin_acc = part_acc; fin_l = cta_l; fin_y = part_y;
   } else if constexpr (CLUSTER) {
-    if (tid == 0) { sm_part[0] = cta_m; sm_part[1] = cta_l; }
-    if (d < D) { sm_part[4 + d] = part_acc; sm_part[4 + D + d] = part_y; }
+    // every split CTA writes its partial into rank 0's sm_all[rank] through
+    // distributed shared memory and arrives (release, cluster scope) on rank
+    // 0's comb_bar, then exits; rank 0 waits once and combines locally.
     cg::cluster_group cluster = cg::this_cluster();
-    cluster.sync();
-    const bool leader = cluster.block_rank() == 0;
-    if (leader) {
-      float M = -INFINITY;
-      for (int q = 0; q < p.split_k; ++q) M = fmaxf(M, *cluster.map_shared_rank(sm_part, q));
-      fin_acc = 0.f; fin_l = 0.f; fin_y = 0.f;
+    const uint32_t rank = cluster.block_rank();
+    const bool leader = rank == 0;
+    sm100::cluster_wait();  // every CTA of the cluster has initialised comb_bar
+    float* slot = leader ? &sm_all[0][0] : cluster.map_shared_rank(&sm_all[rank][0], 0);
+    if (tid == 0) { slot[0] = cta_m; slot[1] = cta_l; }
+    if (d < D) { slot[4 + d] = part_acc; slot[4 + D + d] = part_y; }
+    __syncthreads();
+    if (!leader) {
+      if (tid == 0) {
+        sm100::fence_acq_rel_cluster();
+        sm100::mbar_arrive_remote(sm100::mapa_shared(comb_bar, 0));
+      }
+      return;
+    }
+    if (!sm100::mbar_wait_cluster(comb_bar, 0) && tid == 0) atomicOr(p.ws_status, 64);
+    float M = -INFINITY;
+    for (int q = 0; q < p.split_k; ++q) M = fmaxf(M, sm_all[q][0]);
+    fin_acc = 0.f; fin_l = 0.f; fin_y = 0.f;
 #pragma unroll 4
-      for (int q = 0; q < p.split_k; ++q) {
-        const float* peer = cluster.map_shared_rank(sm_part, q);
-        const float mq = peer[0];
-        const float wgt = (mq == -INFINITY) ? 0.f : exp2f(mq - M);
-        fin_l += peer[1] * wgt;
-        if (d < D) {
-          fin_acc += peer[4 + d] * wgt;
-          fin_y += peer[4 + D + d];
-        }
+    for (int q = 0; q < p.split_k; ++q) {
+      const float mq = sm_all[q][0];
+      const float wgt = (mq == -INFINITY) ? 0.f : exp2f(mq - M);
+      fin_l += sm_all[q][1] * wgt;
+      if (d < D) {
+        fin_acc += sm_all[q][4 + d] * wgt;
+        fin_y += sm_all[q][4 + D + d];
       }
     }
-    cluster.sync();  // peers keep their shared memory alive until the leader has read it
-    if (!leader) return;
   } else {
     float* part = p.ws_part + ((int64_t)bh * p.split_k + s) * PS;
     if (tid == 0) { part[0] = cta_m; part[1] = cta_l; }
@@ -352,7 +361,7 @@ decode_reg_kernel(const DecodeParams p) {
   gla_rows<T, D, ALPHA, kConsumers>(p, s, b, h, tid, sm_y);
   __syncthreads();
   finish<T, D, false, kConsumerWarps, RSUB>(p, s, b, h, tid, lane, warp, kConsumerWarps, sh, sm_acc, sm_y, nullptr,
-                                            ep);
+                                            nullptr, ep);
 }
 
 // ============================================================================
@@ -376,8 +385,9 @@ decode_bulk_kernel(const DecodeParams p) {
   __shared__ __align__(16) float sm_acc[NW][D];
   __shared__ __align__(16) float sm_y[RSUB][D];
   __shared__ __align__(16) float sm_q[D];
-  __shared__ __align__(16) float sm_part[4 + 2 * D];
+  __shared__ __align__(16) float sm_all[CLUSTER ? kMaxClusterSplit : 1][4 + 2 * D];  // split partials (rank 0's)
   __shared__ __align__(8) uint64_t full_bar[kMaxStages], empty_bar[kMaxStages];
+  __shared__ __align__(8) uint64_t comb_bar;
   __shared__ int sm_err;
   extern __shared__ __align__(128) unsigned char ring[];  // [NST][chunk*R] K, then [NST][chunk*D] V
   T* sK = reinterpret_cast<T*>(ring);
@@ -403,6 +413,7 @@ decode_bulk_kernel(const DecodeParams p) {
       sm100::mbar_init(&full_bar[i], 1);
       sm100::mbar_init(&empty_bar[i], 1);
     }
+    if (CLUSTER) sm100::mbar_init(&comb_bar, p.split_k > 1 ? p.split_k - 1 : 1);
     sm_err = 0;
     sm100::fence_mbar_init();
   }
@@ -414,6 +425,8 @@ decode_bulk_kernel(const DecodeParams p) {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const EpiloguePrefetch ep = prefetch_epilogue<D>(p, b, h, tid);
   __syncthreads();  // barriers initialised; the producer starts streaming at once
+  // cluster combine: arrive now, wait just before the first remote access
+  if (CLUSTER && p.split_k > 1) sm100::cluster_arrive_relaxed();
 
   float m_run = -INFINITY, l_run = 0.f;
   float acc[8];
@@ -485,7 +498,7 @@ decode_bulk_kernel(const DecodeParams p) {
   }
   __syncthreads();
   if (tid == 0 && sm_err) atomicOr(p.ws_status, 4 * sm_err);
-  finish<T, D, CLUSTER, NW, RSUB>(p, s, b, h, tid, lane, warp, NW + 2, sh, sm_acc, sm_y, sm_part, ep);
+  finish<T, D, CLUSTER, NW, RSUB>(p, s, b, h, tid, lane, warp, NW + 2, sh, sm_acc, sm_y, sm_all, &comb_bar, ep);
 }
 
 template <typename T, int D, bool ALPHA, bool CLUSTER, int NW>
