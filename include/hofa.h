@@ -202,6 +202,22 @@ typedef struct hofa_prep_args {
  * export / append (:196-198, :382-384). */
 int hofa_prep_fwd(const hofa_prep_args* args, void* stream);
 
+/* One decode step of the layer with the new token's prep fused in: the same
+ * result as hofa_prep_fwd(prep) followed by hofa_decode_fwd(decode) with
+ * decode.log_gamma = prep.log_gamma and decode.mix_g = prep.mix_out, where the
+ * new token's position is decode.seq_len - 1 (*decode.seq_len_dev - 1 when
+ * that is given; prep.pos0 / pos0_dev are ignored).  prep.q/k/v must be
+ * decode.q/k/v (one un-rotated token), prep.cache_k/v decode.cache_k/v, and
+ * prep.mix_out is required.  On the TMA-bulk decode path this is one launch:
+ * the cache is streamed over rows [0, seq_len - 1) while the new row, written
+ * by the same launch, joins the softmax from registers; other paths run the
+ * two launches.  The contents of q and k afterwards are unspecified (the
+ * two-launch form rotates them in place, the fused form leaves them).
+ * Replaces the layer's decode sequence at
+ * src/HybridOutlierFactorizedAttention.py:360-416 (gates, RoPE at p, cache
+ * append, fused_hofa_decode). */
+int hofa_decode_step_fwd(const hofa_decode_args* decode, const hofa_prep_args* prep, void* stream);
+
 /* ------------------------------------------------------------------------ */
 const char* hofa_last_error(void);
 int32_t hofa_abi_version(void);

@@ -13,7 +13,7 @@ from .config import InferenceConfig, ModelConfig
 from .modules import RotaryEmbedding, apply_rotary_pos_emb, rotate_half
 
 __all__ = ["ModelConfig", "InferenceConfig", "RotaryEmbedding", "apply_rotary_pos_emb", "rotate_half",
-           "HybridOutlierFactorizedAttention", "fused_hofa_decode", "chunk_gla_inlier_fwd",
+           "HybridOutlierFactorizedAttention", "fused_hofa_decode", "fused_hofa_decode_step", "chunk_gla_inlier_fwd",
            "exact_attention_triton", "prep"]
 
 
@@ -26,6 +26,9 @@ def __getattr__(name):
     if name == "fused_hofa_decode":
         from .hofa_decode import fused_hofa_decode
         return fused_hofa_decode
+    if name == "fused_hofa_decode_step":
+        from .hofa_decode import fused_hofa_decode_step
+        return fused_hofa_decode_step
     if name == "chunk_gla_inlier_fwd":
         from .chunk_gla_inlier import chunk_gla_inlier_fwd
         return chunk_gla_inlier_fwd

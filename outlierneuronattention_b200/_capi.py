@@ -137,6 +137,8 @@ def lib():
                 for fn in ("hofa_decode_fwd", "hofa_prefill_gla_fwd", "hofa_prefill_outlier_fwd", "hofa_prep_fwd"):
                     getattr(L, fn).restype = ctypes.c_int
                     getattr(L, fn).argtypes = [c_void_p, c_void_p]
+                L.hofa_decode_step_fwd.restype = ctypes.c_int
+                L.hofa_decode_step_fwd.argtypes = [c_void_p, c_void_p, c_void_p]
                 L.hofa_last_error.restype = ctypes.c_char_p
                 L.hofa_abi_version.restype = c_int32
                 L.hofa_decode_workspace_size.restype = c_size_t

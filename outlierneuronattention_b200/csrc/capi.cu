@@ -146,6 +146,232 @@ size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
 
 }  // namespace
 
+namespace {
+
+// Validation of hofa_decode_args and the kernel parameters (shared by
+// hofa_decode_fwd and hofa_decode_step_fwd).
+int decode_setup(const hofa_decode_args* a, hofa::DecodeParams& p, int& path, bool& alpha, int& dt) {
+  if (a == nullptr) return fail(HOFA_ERR_INVALID_ARGUMENT, "args is NULL");
+  const int64_t B = a->q.shape[0], H = a->q.shape[1], D = a->q.shape[3];
+  CHECK(a->q, "q", 4, -1, -1, 1, -1);
+  if (B <= 0 || H <= 0) return fail(HOFA_ERR_INVALID_ARGUMENT, "q: empty batch or heads");
+  if (!supported_d(D)) return fail(HOFA_ERR_UNSUPPORTED, "head dim %lld not built (32, 64, 128)", (long long)D);
+  const int R = a->R;
+  if (R < 0 || R > D) return fail(HOFA_ERR_INVALID_ARGUMENT, "R=%d outside [0, D=%lld]", R, (long long)D);
+  const int64_t J = D - R;
+  CHECK(a->k, "k", 4, B, H, 1, D);
+  CHECK(a->v, "v", 4, B, H, 1, D);
+  CHECK(a->y, "y", 4, B, H, 1, D);
+  dt = a->q.dtype;
+  if (a->k.dtype != dt || a->v.dtype != dt || a->y.dtype != dt)
+    return fail(HOFA_ERR_INVALID_ARGUMENT, "q, k, v and y must share one dtype");
+  int64_t L = 0;
+  if (R > 0) {
+    CHECK(a->cache_k, "cache_k", 4, B, H, -1, -1);
+    L = a->cache_k.shape[2];
+    if (a->cache_k.shape[3] < R) return fail(HOFA_ERR_INVALID_ARGUMENT, "cache_k: last dim < R");
+    CHECK(a->cache_v, "cache_v", 4, B, H, L, D);
+    if (a->cache_k.dtype != dt || a->cache_v.dtype != dt)
+      return fail(HOFA_ERR_INVALID_ARGUMENT, "caches must have the dtype of q");
+    if (L < 1) return fail(HOFA_ERR_INVALID_ARGUMENT, "empty cache");
+    if (a->seq_len_dev == nullptr && (a->seq_len < 1 || a->seq_len > L))
+      return fail(HOFA_ERR_INVALID_ARGUMENT, "seq_len=%d outside [1, L=%lld]", a->seq_len, (long long)L);
+  }
+  CHECK(a->state_in, "state_in", 4, B, H, J, D);
+  CHECK(a->state_out, "state_out", 4, B, H, J, D);
+  if (a->state_in.dtype != HOFA_DTYPE_F32 || a->state_out.dtype != HOFA_DTYPE_F32)
+    return fail(HOFA_ERR_INVALID_ARGUMENT, "GLA states must be float32");
+  for (const hofa_tensor* s : {&a->state_in, &a->state_out}) {
+    if (J > 0 && (s->stride[3] != 1 || s->stride[2] % 4 || s->stride[1] % 4 || s->stride[0] % 4 || !aligned16(s->data)))
+      return fail(HOFA_ERR_MISALIGNED, "GLA states need unit stride along D and 16-byte aligned rows");
+  }
+  if (J > 0 && a->state_in.data == a->state_out.data)
+    return fail(HOFA_ERR_INVALID_ARGUMENT, "state_out must not alias state_in");
+
+  memset(&p, 0, sizeof(p));
+  int r = side_bht(a->log_gamma, "log_gamma", B, H, 1, p.slg);
+  if (r) return r;
+  int64_t tmp3[3];
+  r = side_bht(a->mix_g, "mix_g", B, H, 1, tmp3);
+  if (r) return r;
+  p.smg[0] = tmp3[0]; p.smg[1] = tmp3[1];
+  r = head_vec(a->norm_w, "norm_w", H, D, p.snw);
+  if (r) return r;
+  alpha = present(a->log_alpha);
+  if (alpha) {
+    r = alpha_strides(a->log_alpha, B, H, J, p.sla);
+    if (r) return r;
+  }
+
+  const int sms = num_sms();
+  int split = a->split_k;
+  const int len_hint = a->seq_len_dev ? (int)L : a->seq_len;
+  if (split <= 0) split = hofa_decode_choose_split((int)B, (int)H, len_hint, sms);
+  if (split > kMaxSplit) return fail(HOFA_ERR_INVALID_ARGUMENT, "split_k=%d above %d", split, kMaxSplit);
+  if (R == 0) split = 1;
+  const size_t need = hofa_decode_workspace_size((int)B, (int)H, (int)D, split);
+  if (a->workspace == nullptr || a->workspace_bytes < need)
+    return fail(HOFA_ERR_WORKSPACE, "decode workspace needs %zu bytes, got %zu", need, a->workspace_bytes);
+  if (!aligned16(a->workspace)) return fail(HOFA_ERR_MISALIGNED, "workspace must be 16-byte aligned");
+
+  p.q = a->q.data; p.k = a->k.data; p.v = a->v.data;
+  p.cache_k = a->cache_k.data; p.cache_v = a->cache_v.data;
+  p.state_in = (const float*)a->state_in.data; p.state_out = (float*)a->state_out.data;
+  p.log_gamma = a->log_gamma.data; p.mix_g = a->mix_g.data; p.norm_w = a->norm_w.data;
+  p.log_alpha = alpha ? a->log_alpha.data : nullptr;
+  p.y = a->y.data;
+  p.B = (int)B; p.H = (int)H; p.D = (int)D; p.R = R; p.L = (int)L;
+  p.seq_len = a->seq_len; p.seq_len_dev = a->seq_len_dev;
+  p.qk_scale_log2 = a->sm_scale * 1.4426950408889634f;
+  p.eps = a->eps;
+  p.split_k = split;
+  for (int i = 0; i < 2; ++i) { p.sq[i] = a->q.stride[i]; p.sk[i] = a->k.stride[i]; p.sv[i] = a->v.stride[i]; p.sy[i] = a->y.stride[i]; }
+  p.sq[2] = a->q.stride[3]; p.sk[2] = a->k.stride[3]; p.sv[2] = a->v.stride[3]; p.sy[2] = a->y.stride[3];
+  if (R > 0) {
+    for (int i = 0; i < 4; ++i) { p.sck[i] = a->cache_k.stride[i]; p.scv[i] = a->cache_v.stride[i]; }
+  }
+  for (int i = 0; i < 3; ++i) { p.sst[i] = a->state_in.stride[i]; p.sso[i] = a->state_out.stride[i]; }
+  p.dt_lg = a->log_gamma.dtype; p.dt_mg = a->mix_g.dtype; p.dt_nw = a->norm_w.dtype;
+  p.dt_la = alpha ? a->log_alpha.dtype : 0;
+  char* ws = reinterpret_cast<char*>(a->workspace);
+  p.ws_status = reinterpret_cast<int*>(ws);
+  p.ws_count = reinterpret_cast<int*>(ws + 256);
+  p.ws_part = reinterpret_cast<float*>(ws + 256 + round256((size_t)B * H * sizeof(int)));
+
+  // 16-byte vector path: unit channel stride and 16-byte aligned rows
+  const int es = esize(dt);
+  bool vec = R > 0 && R % 8 == 0;
+  if (vec) {
+    for (const hofa_tensor* c : {&a->cache_k, &a->cache_v}) {
+      vec = vec && c->stride[3] == 1 && aligned16(c->data);
+      for (int i = 0; i < 3; ++i) vec = vec && ((c->stride[i] * es) % 16 == 0 || c->shape[i] == 1);
+    }
+  }
+  // TMA bulk path: additionally, every (b,h) slab of cache rows is contiguous
+  const bool bulk = vec && a->cache_k.stride[2] == R && a->cache_v.stride[2] == D && !getenv_flag("HOFA_DECODE_NO_BULK");
+  path = bulk ? 2 : (vec ? 1 : 0);
+  // bulk ring: 64-token slots; a slot is always consumed by the same warp,
+  // which requires stages % consumer_warps == 0
+  p.consumer_warps = 4;
+  p.stages = es == 4 ? 4 : 8;
+  if (const char* v = getenv("HOFA_DECODE_WARPS")) p.consumer_warps = atoi(v) == 8 ? 8 : 4;
+  if (const char* v = getenv("HOFA_DECODE_STAGES")) {
+    const int n = atoi(v);
+    if (n >= 2 && n <= 16) p.stages = n;
+  }
+  p.stages = ((p.stages + p.consumer_warps - 1) / p.consumer_warps) * p.consumer_warps;
+  while (p.stages > p.consumer_warps && (size_t)p.stages * 64 * (R + D) * es > 200 * 1024) p.stages -= p.consumer_warps;
+  if (p.stages > 16 || (size_t)p.stages * 64 * (R + D) * es > 200 * 1024) {
+    p.consumer_warps = 4;
+    p.stages = 4;
+  }
+  return HOFA_OK;
+}
+
+// Validation of hofa_prep_args and the kernel parameters (shared by
+// hofa_prep_fwd and hofa_decode_step_fwd).  `empty` is set for N == 0.
+int prep_setup(const hofa_prep_args* a, hofa::PrepParams& p, int& dt, bool& empty) {
+  if (a == nullptr) return fail(HOFA_ERR_INVALID_ARGUMENT, "args is NULL");
+  const int64_t B = a->q.shape[0], H = a->q.shape[1], N = a->q.shape[2], D = a->q.shape[3];
+  CHECK(a->q, "q", 4, -1, -1, -1, -1);
+  CHECK(a->k, "k", 4, B, H, N, D);
+  if (!supported_d(D)) return fail(HOFA_ERR_UNSUPPORTED, "head dim %lld not built (32, 64, 128)", (long long)D);
+  dt = a->q.dtype;
+  if (a->k.dtype != dt) return fail(HOFA_ERR_INVALID_ARGUMENT, "q and k must share one dtype");
+  const int R = a->R;
+  if (R < 0 || R > D || (R % 2)) return fail(HOFA_ERR_INVALID_ARGUMENT, "R=%d must be even and in [0, D]", R);
+  memset(&p, 0, sizeof(p));
+  CHECK(a->gate_w, "gate_w", 2, H, 2 * D);
+  CHECK(a->gate_b, "gate_b", 1, H);
+  p.sgw[0] = a->gate_w.stride[0]; p.sgw[1] = a->gate_w.stride[1]; p.sgb = a->gate_b.stride[0];
+  if (present(a->mix_w)) {
+    CHECK(a->mix_w, "mix_w", 2, H, 2 * D);
+    CHECK(a->mix_b, "mix_b", 1, H);
+    p.smw[0] = a->mix_w.stride[0]; p.smw[1] = a->mix_w.stride[1]; p.smb = a->mix_b.stride[0];
+  } else if (present(a->fixed_mix)) {
+    CHECK(a->fixed_mix, "fixed_mix", 1, H);
+    p.sfm = a->fixed_mix.stride[0];
+  }
+  int r = side_bht(a->log_gamma, "log_gamma", B, H, N, p.slg);
+  if (r) return r;
+  if (present(a->mix_out)) {
+    if (!present(a->mix_w) && !present(a->fixed_mix))
+      return fail(HOFA_ERR_INVALID_ARGUMENT, "mix_out requested without mix_w or fixed_mix");
+    r = side_bht(a->mix_out, "mix_out", B, H, N, p.smo);
+    if (r) return r;
+  }
+  const bool rope = a->use_rope != 0 && R > 0;
+  if (rope) {
+    CHECK(a->cos, "cos", 2, -1, -1);
+    CHECK(a->sin, "sin", 2, a->cos.shape[0], -1);
+    if (a->cos.shape[1] < R || a->sin.shape[1] < R) return fail(HOFA_ERR_INVALID_ARGUMENT, "RoPE tables narrower than R");
+    if (a->sin.dtype != a->cos.dtype) return fail(HOFA_ERR_INVALID_ARGUMENT, "cos/sin dtypes differ");
+    p.P = (int)a->cos.shape[0];
+    if (a->pos0_dev == nullptr && a->pos0 + N > p.P)
+      return fail(HOFA_ERR_INVALID_ARGUMENT, "RoPE tables hold %d positions, need %lld", p.P, (long long)(a->pos0 + N));
+    p.scos[0] = a->cos.stride[0]; p.scos[1] = a->cos.stride[1];
+    p.ssin[0] = a->sin.stride[0]; p.ssin[1] = a->sin.stride[1];
+    p.dt_cs = a->cos.dtype;
+  }
+  p.L = 0;
+  if (present(a->cache_k) || present(a->cache_v)) {
+    if (R > 0) {
+      CHECK(a->cache_k, "cache_k", 4, B, H, -1, -1);
+      if (a->cache_k.shape[3] < R) return fail(HOFA_ERR_INVALID_ARGUMENT, "cache_k: last dim < R");
+    }
+    const int64_t L = R > 0 ? a->cache_k.shape[2] : a->cache_v.shape[2];
+    CHECK(a->cache_v, "cache_v", 4, B, H, L, D);
+    CHECK(a->v, "v", 4, B, H, N, D);
+    if ((R > 0 && a->cache_k.dtype != dt) || a->cache_v.dtype != dt || a->v.dtype != dt)
+      return fail(HOFA_ERR_INVALID_ARGUMENT, "caches and v must have the dtype of q");
+    if (a->pos0_dev == nullptr && (a->pos0 < 0 || a->pos0 + N > L))
+      return fail(HOFA_ERR_INVALID_ARGUMENT, "cache rows [%d, %lld) outside [0, %lld)", a->pos0,
+                  (long long)(a->pos0 + N), (long long)L);
+    p.L = (int)L;
+    for (int i = 0; i < 4; ++i) {
+      if (R > 0) p.sck[i] = a->cache_k.stride[i];
+      p.scv[i] = a->cache_v.stride[i];
+      p.sv[i] = a->v.stride[i];
+    }
+  }
+  if (a->pos0 < 0) return fail(HOFA_ERR_INVALID_ARGUMENT, "pos0 must be >= 0");
+  if (N == 0) { empty = true; return HOFA_OK; }
+  p.q = a->q.data; p.k = a->k.data; p.v = a->v.data;
+  p.gate_w = a->gate_w.data; p.gate_b = a->gate_b.data;
+  p.mix_w = present(a->mix_w) ? a->mix_w.data : nullptr;
+  p.mix_b = present(a->mix_w) ? a->mix_b.data : nullptr;
+  p.fixed_mix = (!present(a->mix_w) && present(a->fixed_mix)) ? a->fixed_mix.data : nullptr;
+  p.cos = rope ? a->cos.data : nullptr; p.sin = rope ? a->sin.data : nullptr;
+  p.log_gamma = a->log_gamma.data;
+  p.mix_out = present(a->mix_out) ? a->mix_out.data : nullptr;
+  p.cache_k = (R > 0 && present(a->cache_k)) ? a->cache_k.data : nullptr;
+  p.cache_v = present(a->cache_v) ? a->cache_v.data : nullptr;
+  p.B = (int)B; p.H = (int)H; p.N = (int)N; p.D = (int)D; p.R = R;
+  p.pos0 = a->pos0; p.pos0_dev = a->pos0_dev;
+  p.rope = rope;
+  for (int i = 0; i < 4; ++i) { p.sq[i] = a->q.stride[i]; p.sk[i] = a->k.stride[i]; }
+  p.dt_gw = a->gate_w.dtype; p.dt_gb = a->gate_b.dtype;
+  p.dt_mw = p.mix_w ? a->mix_w.dtype : 0; p.dt_mb = p.mix_b ? a->mix_b.dtype : 0;
+  p.dt_fm = p.fixed_mix ? a->fixed_mix.dtype : 0;
+  p.dt_lg = a->log_gamma.dtype; p.dt_mo = p.mix_out ? a->mix_out.dtype : 0;
+  // 16-byte row path: unit channel stride and 16-byte aligned rows for q, k (and v / caches when written)
+  {
+    auto rows16 = [](const hofa_tensor& t) {
+      if (t.stride[3] != 1 || !aligned16(t.data)) return false;
+      for (int i = 0; i < 3; ++i)
+        if ((t.stride[i] * 2) % 16 != 0 && t.shape[i] != 1) return false;
+      return true;
+    };
+    bool vec = dt != HOFA_DTYPE_F32 && R % 8 == 0 && rows16(a->q) && rows16(a->k);
+    if (p.cache_k) vec = vec && rows16(a->cache_k);
+    if (p.cache_v) vec = vec && rows16(a->cache_v) && rows16(a->v);
+    p.vec = vec;
+  }
+  return HOFA_OK;
+}
+
+}  // namespace
+
 namespace hofa {
 // Records `message` as the calling thread's last error and returns `code`
 // (for entry points defined outside this file).
@@ -202,121 +428,11 @@ int hofa_decode_read_status(void* workspace, void* stream, int32_t* status_out) 
 }
 
 int hofa_decode_fwd(const hofa_decode_args* a, void* stream) {
-  if (a == nullptr) return fail(HOFA_ERR_INVALID_ARGUMENT, "args is NULL");
-  const int64_t B = a->q.shape[0], H = a->q.shape[1], D = a->q.shape[3];
-  CHECK(a->q, "q", 4, -1, -1, 1, -1);
-  if (B <= 0 || H <= 0) return fail(HOFA_ERR_INVALID_ARGUMENT, "q: empty batch or heads");
-  if (!supported_d(D)) return fail(HOFA_ERR_UNSUPPORTED, "head dim %lld not built (32, 64, 128)", (long long)D);
-  const int R = a->R;
-  if (R < 0 || R > D) return fail(HOFA_ERR_INVALID_ARGUMENT, "R=%d outside [0, D=%lld]", R, (long long)D);
-  const int64_t J = D - R;
-  CHECK(a->k, "k", 4, B, H, 1, D);
-  CHECK(a->v, "v", 4, B, H, 1, D);
-  CHECK(a->y, "y", 4, B, H, 1, D);
-  const int dt = a->q.dtype;
-  if (a->k.dtype != dt || a->v.dtype != dt || a->y.dtype != dt)
-    return fail(HOFA_ERR_INVALID_ARGUMENT, "q, k, v and y must share one dtype");
-  int64_t L = 0;
-  if (R > 0) {
-    CHECK(a->cache_k, "cache_k", 4, B, H, -1, -1);
-    L = a->cache_k.shape[2];
-    if (a->cache_k.shape[3] < R) return fail(HOFA_ERR_INVALID_ARGUMENT, "cache_k: last dim < R");
-    CHECK(a->cache_v, "cache_v", 4, B, H, L, D);
-    if (a->cache_k.dtype != dt || a->cache_v.dtype != dt)
-      return fail(HOFA_ERR_INVALID_ARGUMENT, "caches must have the dtype of q");
-    if (L < 1) return fail(HOFA_ERR_INVALID_ARGUMENT, "empty cache");
-    if (a->seq_len_dev == nullptr && (a->seq_len < 1 || a->seq_len > L))
-      return fail(HOFA_ERR_INVALID_ARGUMENT, "seq_len=%d outside [1, L=%lld]", a->seq_len, (long long)L);
-  }
-  CHECK(a->state_in, "state_in", 4, B, H, J, D);
-  CHECK(a->state_out, "state_out", 4, B, H, J, D);
-  if (a->state_in.dtype != HOFA_DTYPE_F32 || a->state_out.dtype != HOFA_DTYPE_F32)
-    return fail(HOFA_ERR_INVALID_ARGUMENT, "GLA states must be float32");
-  for (const hofa_tensor* s : {&a->state_in, &a->state_out}) {
-    if (J > 0 && (s->stride[3] != 1 || s->stride[2] % 4 || s->stride[1] % 4 || s->stride[0] % 4 || !aligned16(s->data)))
-      return fail(HOFA_ERR_MISALIGNED, "GLA states need unit stride along D and 16-byte aligned rows");
-  }
-  if (J > 0 && a->state_in.data == a->state_out.data)
-    return fail(HOFA_ERR_INVALID_ARGUMENT, "state_out must not alias state_in");
-
   hofa::DecodeParams p;
-  memset(&p, 0, sizeof(p));
-  int r = side_bht(a->log_gamma, "log_gamma", B, H, 1, p.slg);
-  if (r) return r;
-  int64_t tmp3[3];
-  r = side_bht(a->mix_g, "mix_g", B, H, 1, tmp3);
-  if (r) return r;
-  p.smg[0] = tmp3[0]; p.smg[1] = tmp3[1];
-  r = head_vec(a->norm_w, "norm_w", H, D, p.snw);
-  if (r) return r;
-  const bool alpha = present(a->log_alpha);
-  if (alpha) {
-    r = alpha_strides(a->log_alpha, B, H, J, p.sla);
-    if (r) return r;
-  }
-
-  const int sms = num_sms();
-  int split = a->split_k;
-  const int len_hint = a->seq_len_dev ? (int)L : a->seq_len;
-  if (split <= 0) split = hofa_decode_choose_split((int)B, (int)H, len_hint, sms);
-  if (split > kMaxSplit) return fail(HOFA_ERR_INVALID_ARGUMENT, "split_k=%d above %d", split, kMaxSplit);
-  if (R == 0) split = 1;
-  const size_t need = hofa_decode_workspace_size((int)B, (int)H, (int)D, split);
-  if (a->workspace == nullptr || a->workspace_bytes < need)
-    return fail(HOFA_ERR_WORKSPACE, "decode workspace needs %zu bytes, got %zu", need, a->workspace_bytes);
-  if (!aligned16(a->workspace)) return fail(HOFA_ERR_MISALIGNED, "workspace must be 16-byte aligned");
-
-  p.q = a->q.data; p.k = a->k.data; p.v = a->v.data;
-  p.cache_k = a->cache_k.data; p.cache_v = a->cache_v.data;
-  p.state_in = (const float*)a->state_in.data; p.state_out = (float*)a->state_out.data;
-  p.log_gamma = a->log_gamma.data; p.mix_g = a->mix_g.data; p.norm_w = a->norm_w.data;
-  p.log_alpha = alpha ? a->log_alpha.data : nullptr;
-  p.y = a->y.data;
-  p.B = (int)B; p.H = (int)H; p.D = (int)D; p.R = R; p.L = (int)L;
-  p.seq_len = a->seq_len; p.seq_len_dev = a->seq_len_dev;
-  p.qk_scale_log2 = a->sm_scale * 1.4426950408889634f;
-  p.eps = a->eps;
-  p.split_k = split;
-  for (int i = 0; i < 2; ++i) { p.sq[i] = a->q.stride[i]; p.sk[i] = a->k.stride[i]; p.sv[i] = a->v.stride[i]; p.sy[i] = a->y.stride[i]; }
-  p.sq[2] = a->q.stride[3]; p.sk[2] = a->k.stride[3]; p.sv[2] = a->v.stride[3]; p.sy[2] = a->y.stride[3];
-  if (R > 0) {
-    for (int i = 0; i < 4; ++i) { p.sck[i] = a->cache_k.stride[i]; p.scv[i] = a->cache_v.stride[i]; }
-  }
-  for (int i = 0; i < 3; ++i) { p.sst[i] = a->state_in.stride[i]; p.sso[i] = a->state_out.stride[i]; }
-  p.dt_lg = a->log_gamma.dtype; p.dt_mg = a->mix_g.dtype; p.dt_nw = a->norm_w.dtype;
-  p.dt_la = alpha ? a->log_alpha.dtype : 0;
-  char* ws = reinterpret_cast<char*>(a->workspace);
-  p.ws_status = reinterpret_cast<int*>(ws);
-  p.ws_count = reinterpret_cast<int*>(ws + 256);
-  p.ws_part = reinterpret_cast<float*>(ws + 256 + round256((size_t)B * H * sizeof(int)));
-
-  // 16-byte vector path: unit channel stride and 16-byte aligned rows
-  const int es = esize(dt);
-  bool vec = R > 0 && R % 8 == 0;
-  if (vec) {
-    for (const hofa_tensor* c : {&a->cache_k, &a->cache_v}) {
-      vec = vec && c->stride[3] == 1 && aligned16(c->data);
-      for (int i = 0; i < 3; ++i) vec = vec && ((c->stride[i] * es) % 16 == 0 || c->shape[i] == 1);
-    }
-  }
-  // TMA bulk path: additionally, every (b,h) slab of cache rows is contiguous
-  const bool bulk = vec && a->cache_k.stride[2] == R && a->cache_v.stride[2] == D && !getenv_flag("HOFA_DECODE_NO_BULK");
-  const int path = bulk ? 2 : (vec ? 1 : 0);
-  // bulk ring: 64-token slots; a slot is always consumed by the same warp,
-  // which requires stages % consumer_warps == 0
-  p.consumer_warps = 4;
-  p.stages = es == 4 ? 4 : 8;
-  if (const char* v = getenv("HOFA_DECODE_WARPS")) p.consumer_warps = atoi(v) == 8 ? 8 : 4;
-  if (const char* v = getenv("HOFA_DECODE_STAGES")) {
-    const int n = atoi(v);
-    if (n >= 2 && n <= 16) p.stages = n;
-  }
-  p.stages = ((p.stages + p.consumer_warps - 1) / p.consumer_warps) * p.consumer_warps;
-  while (p.stages > p.consumer_warps && (size_t)p.stages * 64 * (R + D) * es > 200 * 1024) p.stages -= p.consumer_warps;
-  if (p.stages > 16 || (size_t)p.stages * 64 * (R + D) * es > 200 * 1024) {
-    p.consumer_warps = 4;
-    p.stages = 4;
-  }
+  int path = 0, dt = 0;
+  bool alpha = false;
+  const int st = decode_setup(a, p, path, alpha, dt);
+  if (st != HOFA_OK) return st;
   cudaError_t e = hofa::launch_decode(p, dt, path, alpha, reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "hofa_decode_fwd launch");
   return HOFA_OK;
@@ -525,105 +641,69 @@ int hofa_prefill_read_status(void* stream, int32_t* status_out) {
 // gates + RoPE + cache export
 // ---------------------------------------------------------------------------
 int hofa_prep_fwd(const hofa_prep_args* a, void* stream) {
-  if (a == nullptr) return fail(HOFA_ERR_INVALID_ARGUMENT, "args is NULL");
-  const int64_t B = a->q.shape[0], H = a->q.shape[1], N = a->q.shape[2], D = a->q.shape[3];
-  CHECK(a->q, "q", 4, -1, -1, -1, -1);
-  CHECK(a->k, "k", 4, B, H, N, D);
-  if (!supported_d(D)) return fail(HOFA_ERR_UNSUPPORTED, "head dim %lld not built (32, 64, 128)", (long long)D);
-  const int dt = a->q.dtype;
-  if (a->k.dtype != dt) return fail(HOFA_ERR_INVALID_ARGUMENT, "q and k must share one dtype");
-  const int R = a->R;
-  if (R < 0 || R > D || (R % 2)) return fail(HOFA_ERR_INVALID_ARGUMENT, "R=%d must be even and in [0, D]", R);
   hofa::PrepParams p;
-  memset(&p, 0, sizeof(p));
-  CHECK(a->gate_w, "gate_w", 2, H, 2 * D);
-  CHECK(a->gate_b, "gate_b", 1, H);
-  p.sgw[0] = a->gate_w.stride[0]; p.sgw[1] = a->gate_w.stride[1]; p.sgb = a->gate_b.stride[0];
-  if (present(a->mix_w)) {
-    CHECK(a->mix_w, "mix_w", 2, H, 2 * D);
-    CHECK(a->mix_b, "mix_b", 1, H);
-    p.smw[0] = a->mix_w.stride[0]; p.smw[1] = a->mix_w.stride[1]; p.smb = a->mix_b.stride[0];
-  } else if (present(a->fixed_mix)) {
-    CHECK(a->fixed_mix, "fixed_mix", 1, H);
-    p.sfm = a->fixed_mix.stride[0];
-  }
-  int r = side_bht(a->log_gamma, "log_gamma", B, H, N, p.slg);
-  if (r) return r;
-  if (present(a->mix_out)) {
-    if (!present(a->mix_w) && !present(a->fixed_mix))
-      return fail(HOFA_ERR_INVALID_ARGUMENT, "mix_out requested without mix_w or fixed_mix");
-    r = side_bht(a->mix_out, "mix_out", B, H, N, p.smo);
-    if (r) return r;
-  }
-  const bool rope = a->use_rope != 0 && R > 0;
-  if (rope) {
-    CHECK(a->cos, "cos", 2, -1, -1);
-    CHECK(a->sin, "sin", 2, a->cos.shape[0], -1);
-    if (a->cos.shape[1] < R || a->sin.shape[1] < R) return fail(HOFA_ERR_INVALID_ARGUMENT, "RoPE tables narrower than R");
-    if (a->sin.dtype != a->cos.dtype) return fail(HOFA_ERR_INVALID_ARGUMENT, "cos/sin dtypes differ");
-    p.P = (int)a->cos.shape[0];
-    if (a->pos0_dev == nullptr && a->pos0 + N > p.P)
-      return fail(HOFA_ERR_INVALID_ARGUMENT, "RoPE tables hold %d positions, need %lld", p.P, (long long)(a->pos0 + N));
-    p.scos[0] = a->cos.stride[0]; p.scos[1] = a->cos.stride[1];
-    p.ssin[0] = a->sin.stride[0]; p.ssin[1] = a->sin.stride[1];
-    p.dt_cs = a->cos.dtype;
-  }
-  p.L = 0;
-  if (present(a->cache_k) || present(a->cache_v)) {
-    if (R > 0) {
-      CHECK(a->cache_k, "cache_k", 4, B, H, -1, -1);
-      if (a->cache_k.shape[3] < R) return fail(HOFA_ERR_INVALID_ARGUMENT, "cache_k: last dim < R");
-    }
-    const int64_t L = R > 0 ? a->cache_k.shape[2] : a->cache_v.shape[2];
-    CHECK(a->cache_v, "cache_v", 4, B, H, L, D);
-    CHECK(a->v, "v", 4, B, H, N, D);
-    if ((R > 0 && a->cache_k.dtype != dt) || a->cache_v.dtype != dt || a->v.dtype != dt)
-      return fail(HOFA_ERR_INVALID_ARGUMENT, "caches and v must have the dtype of q");
-    if (a->pos0_dev == nullptr && (a->pos0 < 0 || a->pos0 + N > L))
-      return fail(HOFA_ERR_INVALID_ARGUMENT, "cache rows [%d, %lld) outside [0, %lld)", a->pos0,
-                  (long long)(a->pos0 + N), (long long)L);
-    p.L = (int)L;
-    for (int i = 0; i < 4; ++i) {
-      if (R > 0) p.sck[i] = a->cache_k.stride[i];
-      p.scv[i] = a->cache_v.stride[i];
-      p.sv[i] = a->v.stride[i];
-    }
-  }
-  if (a->pos0 < 0) return fail(HOFA_ERR_INVALID_ARGUMENT, "pos0 must be >= 0");
-  if (N == 0) return HOFA_OK;
-  p.q = a->q.data; p.k = a->k.data; p.v = a->v.data;
-  p.gate_w = a->gate_w.data; p.gate_b = a->gate_b.data;
-  p.mix_w = present(a->mix_w) ? a->mix_w.data : nullptr;
-  p.mix_b = present(a->mix_w) ? a->mix_b.data : nullptr;
-  p.fixed_mix = (!present(a->mix_w) && present(a->fixed_mix)) ? a->fixed_mix.data : nullptr;
-  p.cos = rope ? a->cos.data : nullptr; p.sin = rope ? a->sin.data : nullptr;
-  p.log_gamma = a->log_gamma.data;
-  p.mix_out = present(a->mix_out) ? a->mix_out.data : nullptr;
-  p.cache_k = (R > 0 && present(a->cache_k)) ? a->cache_k.data : nullptr;
-  p.cache_v = present(a->cache_v) ? a->cache_v.data : nullptr;
-  p.B = (int)B; p.H = (int)H; p.N = (int)N; p.D = (int)D; p.R = R;
-  p.pos0 = a->pos0; p.pos0_dev = a->pos0_dev;
-  p.rope = rope;
-  for (int i = 0; i < 4; ++i) { p.sq[i] = a->q.stride[i]; p.sk[i] = a->k.stride[i]; }
-  p.dt_gw = a->gate_w.dtype; p.dt_gb = a->gate_b.dtype;
-  p.dt_mw = p.mix_w ? a->mix_w.dtype : 0; p.dt_mb = p.mix_b ? a->mix_b.dtype : 0;
-  p.dt_fm = p.fixed_mix ? a->fixed_mix.dtype : 0;
-  p.dt_lg = a->log_gamma.dtype; p.dt_mo = p.mix_out ? a->mix_out.dtype : 0;
-  // 16-byte row path: unit channel stride and 16-byte aligned rows for q, k (and v / caches when written)
-  {
-    auto rows16 = [](const hofa_tensor& t) {
-      if (t.stride[3] != 1 || !aligned16(t.data)) return false;
-      for (int i = 0; i < 3; ++i)
-        if ((t.stride[i] * 2) % 16 != 0 && t.shape[i] != 1) return false;
-      return true;
-    };
-    bool vec = dt != HOFA_DTYPE_F32 && R % 8 == 0 && rows16(a->q) && rows16(a->k);
-    if (p.cache_k) vec = vec && rows16(a->cache_k);
-    if (p.cache_v) vec = vec && rows16(a->cache_v) && rows16(a->v);
-    p.vec = vec;
-  }
+  int dt = 0;
+  bool empty = false;
+  const int st = prep_setup(a, p, dt, empty);
+  if (st != HOFA_OK || empty) return st;
   cudaError_t e = hofa::launch_prep(p, dt, reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "hofa_prep_fwd launch");
+  return HOFA_OK;
+}
+
+// ---------------------------------------------------------------------------
+// decode step: the new token's prep and the decode in one launch
+// ---------------------------------------------------------------------------
+int hofa_decode_step_fwd(const hofa_decode_args* d, const hofa_prep_args* pr, void* stream) {
+  if (d == nullptr || pr == nullptr) return fail(HOFA_ERR_INVALID_ARGUMENT, "args is NULL");
+  if (pr->q.data != d->q.data || pr->k.data != d->k.data || pr->v.data != d->v.data)
+    return fail(HOFA_ERR_INVALID_ARGUMENT, "prep and decode must name the same q, k, v");
+  if (!present(d->cache_k) || pr->cache_k.data != d->cache_k.data || pr->cache_v.data != d->cache_v.data)
+    return fail(HOFA_ERR_INVALID_ARGUMENT, "prep must append to the decode's caches");
+  if (!present(pr->mix_out)) return fail(HOFA_ERR_INVALID_ARGUMENT, "mix_out is required (the blend weight)");
+  // the new token's position is the decode's last row: seq_len - 1
+  hofa_prep_args pa = *pr;
+  pa.pos0 = d->seq_len_dev != nullptr ? 0 : d->seq_len - 1;
+  pa.pos0_dev = d->seq_len_dev;
+  hofa::PrepParams pp;
+  int pdt = 0;
+  bool empty = false;
+  int st = prep_setup(&pa, pp, pdt, empty);
+  if (st != HOFA_OK) return st;
+  if (pp.N != 1) return fail(HOFA_ERR_INVALID_ARGUMENT, "a decode step takes one token (N=1)");
+  pp.pos0_dev_bias = d->seq_len_dev != nullptr ? -1 : 0;
+  hofa_decode_args da = *d;
+  da.log_gamma = pr->log_gamma;
+  da.mix_g = pr->mix_out;
+  hofa::DecodeParams dp;
+  int path = 0, dt = 0;
+  bool alpha = false;
+  st = decode_setup(&da, dp, path, alpha, dt);
+  if (st != HOFA_OK) return st;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const bool fuse = path == 2 && dp.R > 0 && pdt == dt && !getenv_flag("HOFA_DECODE_STEP_UNFUSED");
+  if (!fuse) {  // the same computation as two launches
+    cudaError_t e = hofa::launch_prep(pp, pdt, s);
+    if (e != cudaSuccess) return cuda_fail(e, "hofa_decode_step_fwd prep launch");
+    e = hofa::launch_decode(dp, dt, path, alpha, s);
+    if (e != cudaSuccess) return cuda_fail(e, "hofa_decode_step_fwd decode launch");
+    return HOFA_OK;
+  }
+  dp.fused_prep = true;
+  dp.consumer_warps = 4;
+  dp.gate_w = pp.gate_w; dp.gate_b = pp.gate_b; dp.mix_w = pp.mix_w; dp.mix_b = pp.mix_b; dp.fixed_mix = pp.fixed_mix;
+  dp.rope_cos = pp.cos; dp.rope_sin = pp.sin;
+  dp.rope_rows = pp.rope ? pp.P : 0;
+  dp.log_gamma_out = pp.log_gamma; dp.mix_out = pp.mix_out;
+  for (int i = 0; i < 2; ++i) {
+    dp.sgw[i] = pp.sgw[i]; dp.smw[i] = pp.smw[i]; dp.scos[i] = pp.scos[i]; dp.ssin[i] = pp.ssin[i];
+    dp.slgo[i] = pp.slg[i]; dp.smo[i] = pp.smo[i];
+  }
+  dp.sgb = pp.sgb; dp.smb = pp.smb; dp.sfm = pp.sfm;
+  dp.dt_gw = pp.dt_gw; dp.dt_gb = pp.dt_gb; dp.dt_mw = pp.dt_mw; dp.dt_mb = pp.dt_mb; dp.dt_fm = pp.dt_fm;
+  dp.dt_cs = pp.dt_cs; dp.dt_lgo = pp.dt_lg; dp.dt_mo = pp.dt_mo;
+  cudaError_t e = hofa::launch_decode(dp, dt, path, alpha, s);
+  if (e != cudaSuccess) return cuda_fail(e, "hofa_decode_step_fwd launch");
   return HOFA_OK;
 }
 

@@ -99,7 +99,8 @@ __device__ __forceinline__ void warp_flush(float m_run, float l_run, float (&acc
 // split's part of y_I = q_I S' -> sm_y (one row of partial sums per group of
 // D/4 threads).  Run by NT threads with indices t in [0, NT).
 template <typename T, int D, bool ALPHA, int NT>
-__device__ __forceinline__ void gla_rows(const DecodeParams& p, int s, int b, int h, int t, float (*sm_y)[D]) {
+__device__ __forceinline__ void gla_rows(const DecodeParams& p, int s, int b, int h, int t, float (*sm_y)[D],
+                                         const float* lg_smem = nullptr) {
   constexpr int D4 = D / 4;
   constexpr int RSUB = NT / D4;
   const int R = p.R, J = D - p.R;
@@ -114,7 +115,7 @@ __device__ __forceinline__ void gla_rows(const DecodeParams& p, int s, int b, in
     float v4[4];
 #pragma unroll
     for (int c = 0; c < 4; ++c) v4[c] = to_f(vp[(int64_t)(4 * c4 + c) * p.sv[2]]);
-    const float lg = ld_any(p.log_gamma, p.dt_lg, b * p.slg[0] + h * p.slg[1]);
+    const float lg = lg_smem != nullptr ? *lg_smem : ld_any(p.log_gamma, p.dt_lg, b * p.slg[0] + h * p.slg[1]);
     const float gam_h = expf(lg);
     const float* sin_ = p.state_in + b * p.sst[0] + h * p.sst[1];
     float* sout = p.state_out + b * p.sso[0] + h * p.sso[1];
@@ -152,7 +153,7 @@ __device__ __forceinline__ EpiloguePrefetch prefetch_epilogue(const DecodeParams
   EpiloguePrefetch e;
   if (d < D) {
     e.nw = ld_any(p.norm_w, p.dt_nw, h * p.snw[0] + d * p.snw[1]);
-    e.mix = ld_any(p.mix_g, p.dt_mg, b * p.smg[0] + h * p.smg[1]);
+    if (!p.fused_prep) e.mix = ld_any(p.mix_g, p.dt_mg, b * p.smg[0] + h * p.smg[1]);  // fused: computed here
   }
   return e;
 }
@@ -169,7 +170,8 @@ __device__ __forceinline__ EpiloguePrefetch prefetch_epilogue(const DecodeParams
 template <typename T, int D, bool CLUSTER, int NW, int RSUB>
 __device__ __forceinline__ void finish(const DecodeParams& p, int s, int b, int h, int tid, int lane, int warp,
                                        int nwarps, DecShared& sh, float (*sm_acc)[D], float (*sm_y)[D],
-                                       float (*sm_all)[4 + 2 * D], uint64_t* comb_bar, EpiloguePrefetch ep) {
+                                       float (*sm_all)[4 + 2 * D], uint64_t* comb_bar, EpiloguePrefetch ep,
+                                       const float* newtok = nullptr) {
   constexpr int PS = 4 + 2 * D;
   const int bh = b * p.H + h;
   float cta_m = -INFINITY;
@@ -188,7 +190,7 @@ __device__ __forceinline__ void finish(const DecodeParams& p, int s, int b, int 
     for (int rr = 0; rr < RSUB; ++rr) part_y += sm_y[rr][d];
   }
 
-  float fin_acc, fin_l, fin_y;
+  float fin_acc, fin_l, fin_y, M_fin = cta_m;
   if (p.split_k == 1) {
     fin_acc = part_acc; fin_l = cta_l; fin_y = part_y;
   } else if constexpr (CLUSTER) {
@@ -213,6 +215,7 @@ __device__ __forceinline__ void finish(const DecodeParams& p, int s, int b, int 
     if (!sm100::mbar_wait_cluster(comb_bar, 0) && tid == 0) atomicOr(p.ws_status, 64);
     float M = -INFINITY;
     for (int q = 0; q < p.split_k; ++q) M = fmaxf(M, sm_all[q][0]);
+    M_fin = M;
     fin_acc = 0.f; fin_l = 0.f; fin_y = 0.f;
 #pragma unroll 4
     for (int q = 0; q < p.split_k; ++q) {
@@ -241,6 +244,7 @@ __device__ __forceinline__ void finish(const DecodeParams& p, int s, int b, int 
     float M = -INFINITY;
 #pragma unroll 8
     for (int q = 0; q < p.split_k; ++q) M = fmaxf(M, __ldcg(all + q * PS));
+    M_fin = M;
     fin_acc = 0.f; fin_l = 0.f; fin_y = 0.f;
 #pragma unroll 8
     for (int q = 0; q < p.split_k; ++q) {
@@ -255,6 +259,16 @@ __device__ __forceinline__ void finish(const DecodeParams& p, int s, int b, int 
     if (tid == 0) p.ws_count[bh] = 0;  // re-arm the ticket for the next launch
   }
 
+  if (newtok != nullptr) {
+    // the new token (score newtok[4] + newtok[5], value newtok[16 + d]) joins the softmax
+    const float sn = newtok[4] + newtok[5];
+    const float M2 = fmaxf(M_fin, sn);
+    const float wo = M_fin == -INFINITY ? 0.f : exp2f(M_fin - M2);
+    const float wn = exp2f(sn - M2);
+    fin_l = fin_l * wo + wn;
+    if (d < D) fin_acc = fin_acc * wo + wn * newtok[16 + d];
+    ep.mix = newtok[2];
+  }
   float sq = (d < D) ? fin_y * fin_y : 0.f;
   sq = warp_sum(sq);
   if (lane == 0) sh.red[warp] = sq;
@@ -367,11 +381,88 @@ decode_reg_kernel(const DecodeParams p) {
 // ============================================================================
 // TMA-bulk variant (cache rows contiguous: row stride R for K, D for V).
 // ============================================================================
+// The new token of a fused decode step (consumer threads, tid < NW * 32):
+// gate = q.Wg[h,:D] + k.Wg[h,D:] + bg on the un-rotated q, k; log decay =
+// logsigmoid(-gate); mix = sigmoid(q.Wm[h,:D] + k.Wm[h,D:] + bm) (or of the
+// fixed blend logit) rounded to the activation dtype; rotate-half RoPE of
+// channels [0, R) at position pos, rounded to the activation dtype as the
+// separate prep kernel stores them; q -> sm_q (scaled), the new score's
+// partial sums -> sm_pre[4..6), v -> sm_pre[16..); split 0 appends the cache
+// row and writes the optional log_gamma / mix outputs.
+template <typename T, int D, int NW>
+__device__ __forceinline__ void prep_new_token(const DecodeParams& p, int s, int b, int h, int tid, int lane,
+                                               int warp, int pos, float* sm_q, float* sm_pre) {
+  const int R = p.R;
+  float gp = 0.f, mp = 0.f;
+  if (tid < D) {
+    const float qf = to_f(reinterpret_cast<const T*>(p.q)[b * p.sq[0] + h * p.sq[1] + tid * p.sq[2]]);
+    const float kf = to_f(reinterpret_cast<const T*>(p.k)[b * p.sk[0] + h * p.sk[1] + tid * p.sk[2]]);
+    const float vf = to_f(reinterpret_cast<const T*>(p.v)[b * p.sv[0] + h * p.sv[1] + tid * p.sv[2]]);
+    gp = fmaf(qf, ld_any(p.gate_w, p.dt_gw, h * p.sgw[0] + tid * p.sgw[1]),
+              kf * ld_any(p.gate_w, p.dt_gw, h * p.sgw[0] + (D + tid) * p.sgw[1]));
+    if (p.mix_w != nullptr)
+      mp = fmaf(qf, ld_any(p.mix_w, p.dt_mw, h * p.smw[0] + tid * p.smw[1]),
+                kf * ld_any(p.mix_w, p.dt_mw, h * p.smw[0] + (D + tid) * p.smw[1]));
+    sm_pre[16 + tid] = vf;
+    sm_pre[16 + D + tid] = qf;
+    sm_pre[16 + 2 * D + tid] = kf;
+  }
+  gp = warp_sum(gp);
+  mp = warp_sum(mp);
+  if (lane == 0 && warp < (D + 31) / 32) { sm_pre[8 + warp] = gp; sm_pre[12 + warp] = mp; }
+  asm volatile("bar.sync 1, %0;" ::"n"(NW * 32) : "memory");  // consumers only
+  float g = ld_any(p.gate_b, p.dt_gb, h * p.sgb);
+  float ml = p.mix_w != nullptr ? ld_any(p.mix_b, p.dt_mb, h * p.smb) : ld_any(p.fixed_mix, p.dt_fm, h * p.sfm);
+#pragma unroll
+  for (int w = 0; w < (D + 31) / 32; ++w) {
+    g += sm_pre[8 + w];
+    if (p.mix_w != nullptr) ml += sm_pre[12 + w];
+  }
+  const float lg = -(fmaxf(g, 0.f) + log1pf(expf(-fabsf(g))));
+  const float mixv = to_f(from_f<T>(1.f / (1.f + expf(-ml))));
+  float prod = 0.f;
+  if (tid < R) {
+    const int half = R / 2;
+    const float qf = sm_pre[16 + D + tid], kf = sm_pre[16 + 2 * D + tid];
+    const float qh = tid < half ? -sm_pre[16 + D + tid + half] : sm_pre[16 + D + tid - half];
+    const float kh = tid < half ? -sm_pre[16 + 2 * D + tid + half] : sm_pre[16 + 2 * D + tid - half];
+    float cs = 1.f, sn = 0.f;
+    if (p.rope_rows > 0) {
+      const int prow = pos < 0 ? 0 : (pos < p.rope_rows ? pos : p.rope_rows - 1);
+      cs = ld_any(p.rope_cos, p.dt_cs, (int64_t)prow * p.scos[0] + tid * p.scos[1]);
+      sn = ld_any(p.rope_sin, p.dt_cs, (int64_t)prow * p.ssin[0] + tid * p.ssin[1]);
+    }
+    const T qr = from_f<T>(qf * cs + qh * sn), kr = from_f<T>(kf * cs + kh * sn);
+    sm_q[tid] = to_f(qr) * p.qk_scale_log2;
+    prod = sm_q[tid] * to_f(kr);
+    if (s == 0) reinterpret_cast<T*>(const_cast<void*>(p.cache_k))[b * p.sck[0] + h * p.sck[1] + (int64_t)pos * p.sck[2] + tid * p.sck[3]] = kr;
+  } else if (tid < D) {
+    sm_q[tid] = 0.f;
+  }
+  if (s == 0 && tid < D)
+    reinterpret_cast<T*>(const_cast<void*>(p.cache_v))[b * p.scv[0] + h * p.scv[1] + (int64_t)pos * p.scv[2] + tid * p.scv[3]] =
+        from_f<T>(sm_pre[16 + tid]);
+  prod = warp_sum(prod);
+  if (lane == 0 && warp < 2) sm_pre[4 + warp] = prod;
+  if (tid == 0) {
+    sm_pre[1] = lg;
+    sm_pre[2] = mixv;
+    if (s == 0 && p.log_gamma_out != nullptr) st_any(p.log_gamma_out, p.dt_lgo, b * p.slgo[0] + h * p.slgo[1], lg);
+    if (s == 0 && p.mix_out != nullptr) st_any(p.mix_out, p.dt_mo, b * p.smo[0] + h * p.smo[1], mixv);
+  }
+}
+
 constexpr int kBulkChunk = 64;  // tokens per bulk chunk (two warp tiles)
 // Warps: NW consumers, then the TMA producer (warp NW), then the GLA warp
 // (warp NW + 1), which updates this split's GLA state rows and its part of
 // y_I while the consumers stream the cache.
-template <typename T, int D, bool ALPHA, bool CLUSTER, int NW>
+//
+// PREP (hofa_decode_step_fwd): the consumers first compute the new token's
+// gates and RoPE (the layer's prep step, src/HybridOutlierFactorizedAttention.py
+// :360-392) into sm_pre, split 0 appends its cache row, the GLA warp waits for
+// the log decay (named barrier 2), the stream covers rows [0, seq_len - 1) and
+// the new token joins the softmax in finish().
+template <typename T, int D, bool ALPHA, bool CLUSTER, int NW, bool PREP>
 __global__ void __launch_bounds__(NW * 32 + 64)
 decode_bulk_kernel(const DecodeParams p) {
   constexpr int G = D / 8, TS = 32 / G, VI = 32 / TS;
@@ -388,16 +479,20 @@ decode_bulk_kernel(const DecodeParams p) {
   __shared__ __align__(16) float sm_all[CLUSTER ? kMaxClusterSplit : 1][4 + 2 * D];  // split partials (rank 0's)
   __shared__ __align__(8) uint64_t full_bar[kMaxStages], empty_bar[kMaxStages];
   __shared__ __align__(8) uint64_t comb_bar;
+  // PREP: [1] log decay, [2] mix, [4..6) new-token score partials, [8..12) / [12..16)
+  // gate / mix dot partials, [16, 16+D) v, [16+D, 16+2D) q, [16+2D, 16+3D) k
+  __shared__ __align__(16) float sm_pre[PREP ? 16 + 3 * D : 1];
   __shared__ int sm_err;
   extern __shared__ __align__(128) unsigned char ring[];  // [NST][chunk*R] K, then [NST][chunk*D] V
   T* sK = reinterpret_cast<T*>(ring);
   T* sV = reinterpret_cast<T*>(ring + (size_t)NST * kBulkChunk * R * sizeof(T));
 
   const int seq_len = resolve_seq_len(p, s, tid);
-  int tps = (seq_len + p.split_k - 1) / p.split_k;
+  const int stream_len = PREP ? seq_len - 1 : seq_len;  // PREP: the newest row comes from registers
+  int tps = (stream_len + p.split_k - 1) / p.split_k;
   tps = (tps + kBulkChunk - 1) & ~(kBulkChunk - 1);
   const int t_begin = s * tps;
-  const int t_end = min(seq_len, t_begin + tps);
+  const int t_end = min(stream_len, t_begin + tps);
   const int nchunks = t_end > t_begin ? (t_end - t_begin + kBulkChunk - 1) / kBulkChunk : 0;
 
   // Slot st of the ring holds chunks st, st+NST, ... and is consumed by warp
@@ -452,11 +547,21 @@ decode_bulk_kernel(const DecodeParams p) {
     }
   } else if (warp == NW + 1) {
     // ---------------- GLA warp: state rows and y_I, beside the streaming ---
-    gla_rows<T, D, ALPHA, 32>(p, s, b, h, lane, sm_y);
+    if constexpr (PREP) {
+      asm volatile("bar.sync 2, %0;" ::"n"(NW * 32 + 32) : "memory");  // the log decay is in sm_pre[1]
+      gla_rows<T, D, ALPHA, 32>(p, s, b, h, lane, sm_y, &sm_pre[1]);
+    } else {
+      gla_rows<T, D, ALPHA, 32>(p, s, b, h, lane, sm_y);
+    }
   } else {
     // ---------------- consumers: q, then the cache stream ------------------
-    load_q<T, D>(p, b, h, tid, sm_q);
-    asm volatile("bar.sync 1, %0;" ::"n"(NW * 32) : "memory");  // consumers only
+    if constexpr (PREP) {
+      prep_new_token<T, D, NW>(p, s, b, h, tid, lane, warp, seq_len - 1, sm_q, sm_pre);
+      asm volatile("bar.sync 2, %0;" ::"n"(NW * 32 + 32) : "memory");  // consumers + GLA warp
+    } else {
+      load_q<T, D>(p, b, h, tid, sm_q);
+      asm volatile("bar.sync 1, %0;" ::"n"(NW * 32) : "memory");  // consumers only
+    }
     const int cg_ = lane % G, ts = lane / G;
     volatile int* verr = &sm_err;
     for (int c = warp; c < nchunks; c += NW) {
@@ -498,13 +603,14 @@ decode_bulk_kernel(const DecodeParams p) {
   }
   __syncthreads();
   if (tid == 0 && sm_err) atomicOr(p.ws_status, 4 * sm_err);
-  finish<T, D, CLUSTER, NW, RSUB>(p, s, b, h, tid, lane, warp, NW + 2, sh, sm_acc, sm_y, sm_all, &comb_bar, ep);
+  finish<T, D, CLUSTER, NW, RSUB>(p, s, b, h, tid, lane, warp, NW + 2, sh, sm_acc, sm_y, sm_all, &comb_bar, ep,
+                                  PREP ? sm_pre : nullptr);
 }
 
-template <typename T, int D, bool ALPHA, bool CLUSTER, int NW>
+template <typename T, int D, bool ALPHA, bool CLUSTER, int NW, bool PREP>
 cudaError_t launch_bulk(const DecodeParams& p, cudaStream_t st) {
   const size_t smem = (size_t)p.stages * kBulkChunk * (p.R + D) * sizeof(T);
-  auto k = decode_bulk_kernel<T, D, ALPHA, CLUSTER, NW>;
+  auto k = decode_bulk_kernel<T, D, ALPHA, CLUSTER, NW, PREP>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   cudaLaunchConfig_t cfg = {};
@@ -538,12 +644,16 @@ cudaError_t launch_d(const DecodeParams& p, int path, bool alpha, cudaStream_t s
   dim3 grid(p.split_k, p.H, p.B);
   if (path == 2) {
     const bool cluster = p.split_k > 1 && p.split_k <= kMaxClusterSplit;
-    if (p.consumer_warps == 8) {
-      if (cluster) return alpha ? launch_bulk<T, D, true, true, 8>(p, st) : launch_bulk<T, D, false, true, 8>(p, st);
-      return alpha ? launch_bulk<T, D, true, false, 8>(p, st) : launch_bulk<T, D, false, false, 8>(p, st);
+    if (p.fused_prep) {  // decode step with the new token's prep (4 consumer warps)
+      if (cluster) return alpha ? launch_bulk<T, D, true, true, 4, true>(p, st) : launch_bulk<T, D, false, true, 4, true>(p, st);
+      return alpha ? launch_bulk<T, D, true, false, 4, true>(p, st) : launch_bulk<T, D, false, false, 4, true>(p, st);
     }
-    if (cluster) return alpha ? launch_bulk<T, D, true, true, 4>(p, st) : launch_bulk<T, D, false, true, 4>(p, st);
-    return alpha ? launch_bulk<T, D, true, false, 4>(p, st) : launch_bulk<T, D, false, false, 4>(p, st);
+    if (p.consumer_warps == 8) {
+      if (cluster) return alpha ? launch_bulk<T, D, true, true, 8, false>(p, st) : launch_bulk<T, D, false, true, 8, false>(p, st);
+      return alpha ? launch_bulk<T, D, true, false, 8, false>(p, st) : launch_bulk<T, D, false, false, 8, false>(p, st);
+    }
+    if (cluster) return alpha ? launch_bulk<T, D, true, true, 4, false>(p, st) : launch_bulk<T, D, false, true, 4, false>(p, st);
+    return alpha ? launch_bulk<T, D, true, false, 4, false>(p, st) : launch_bulk<T, D, false, false, 4, false>(p, st);
   } else if (path == 1) {
     if (alpha) decode_reg_kernel<T, D, true, true><<<grid, kConsumers, 0, st>>>(p);
     else decode_reg_kernel<T, D, true, false><<<grid, kConsumers, 0, st>>>(p);

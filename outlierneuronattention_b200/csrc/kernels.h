@@ -32,6 +32,18 @@ struct DecodeParams {
   int* ws_status;
   int stages;                 // bulk ring depth (64-token chunks)
   int consumer_warps;         // bulk kernel consumer warps: 4 or 8
+  // hofa_decode_step_fwd (bulk kernel): the new token's gates, RoPE and cache
+  // row are computed in the same launch.  q, k, v are then un-rotated; the
+  // cache is streamed over rows [0, seq_len - 1) and the new token (row
+  // seq_len - 1) joins the softmax from registers; log_gamma / mix_g above
+  // are unused (log_gamma_out / mix_out, when non-null, receive them).
+  bool fused_prep;
+  const void* gate_w; const void* gate_b; const void* mix_w; const void* mix_b; const void* fixed_mix;
+  const void* rope_cos; const void* rope_sin;
+  void* log_gamma_out; void* mix_out;
+  int rope_rows;              // rows of the RoPE tables (0: no RoPE)
+  int64_t sgw[2], sgb, smw[2], smb, sfm, scos[2], ssin[2], slgo[2], smo[2];
+  int dt_gw, dt_gb, dt_mw, dt_mb, dt_fm, dt_cs, dt_lgo, dt_mo;
 };
 
 // path: 0 = strided register loads, 1 = 16-byte register loads, 2 = TMA bulk ring
@@ -84,6 +96,7 @@ struct PrepParams {
   void* cache_k; void* cache_v;
   int B, H, N, D, R;
   int pos0; const int* pos0_dev;
+  int pos0_dev_bias;           // added to *pos0_dev (a device seq_len gives position seq_len - 1)
   int L;                       // cache rows (bound for the append)
   int P;                       // rows of the RoPE tables
   bool rope;

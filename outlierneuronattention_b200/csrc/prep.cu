@@ -73,7 +73,7 @@ prep_kernel(const PrepParams p) {
   }
   __syncwarp();
 
-  int pos = (p.pos0_dev != nullptr ? *p.pos0_dev : p.pos0) + n;
+  int pos = (p.pos0_dev != nullptr ? *p.pos0_dev + p.pos0_dev_bias : p.pos0) + n;
   const int R = p.R, half = R / 2;
   if (p.rope && R > 0) {
     const int prow = pos < 0 ? 0 : (pos < p.P ? pos : p.P - 1);
@@ -155,7 +155,7 @@ prep_vec_kernel(const PrepParams p) {
     const float mlog = has_mix ? ml + ld_any(p.mix_b, p.dt_mb, h * p.smb) : ld_any(p.fixed_mix, p.dt_fm, h * p.sfm);
     st_any(p.mix_out, p.dt_mo, b * p.smo[0] + h * p.smo[1] + (int64_t)n * p.smo[2], 1.f / (1.f + expf(-mlog)));
   }
-  const int pos = (p.pos0_dev != nullptr ? *p.pos0_dev : p.pos0) + n;
+  const int pos = (p.pos0_dev != nullptr ? *p.pos0_dev + p.pos0_dev_bias : p.pos0) + n;
   if (RMAX > 0 && p.rope) {
     constexpr int half = RMAX / 2;
     const int prow = pos < 0 ? 0 : (pos < p.P ? pos : p.P - 1);
@@ -203,7 +203,7 @@ cudaError_t launch_t(const PrepParams& p, cudaStream_t st) {
   if constexpr (sizeof(T) == 2) {
     if (p.vec) {
       const dim3 grid((unsigned)((p.N + kVecThreads - 1) / kVecThreads), p.H, p.B);
-      const int r = p.rope ? p.R : 0;
+      const int r = p.R;  // the outlier channels: rotated when p.rope, copied to cache_k either way
       bool launched = true;
 #define HOFA_PREP_VEC(DD, RR) \
   else if (p.D == DD && r == RR) prep_vec_kernel<T, DD, RR><<<grid, kVecThreads, 0, st>>>(p);

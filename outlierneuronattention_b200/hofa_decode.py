@@ -93,3 +93,40 @@ def read_status(device: torch.device, B: int, H: int, D: int) -> int:
     if st != 0:
         raise _capi.HofaError("hofa_decode_read_status", st, _capi.lib().hofa_last_error().decode())
     return int(out.value)
+
+
+def fused_hofa_decode_step(q, k, v, cache_k, cache_v, state_I_in, state_I_out, norm_w, R, seq_len, sm_scale,
+                           gate_w, gate_b, *, mix_w=None, mix_b=None, fixed_mix=None, cos=None, sin=None,
+                           log_alpha=None, eps: float = FP32_EPS, seq_len_dev: Optional[torch.Tensor] = None,
+                           split_k=None, log_gamma_out: Optional[torch.Tensor] = None,
+                           mix_out: Optional[torch.Tensor] = None):
+    """One decode step of the layer with the new token's prep fused in
+    (``hofa_decode_step_fwd``): the gates on the un-rotated q, k
+    (src/HybridOutlierFactorizedAttention.py:67-95, :361), RoPE of channels
+    [0, R) at position ``seq_len - 1`` (:365-375), the cache append at that row
+    (:382-384) and ``fused_hofa_decode`` over rows [0, seq_len) (:386-416).
+
+    q, k, v: [B,H,1,D] un-rotated projections of the new token; cache_k
+    [B,H,L,R] and cache_v [B,H,L,D] pre-allocated (row ``seq_len - 1`` is
+    written); state_I_in/out [B,H,D-R,D] float32; gate_w [H,2D], gate_b [H];
+    the blend from ``mix_w``/``mix_b`` or ``fixed_mix``; RoPE tables ``cos``,
+    ``sin`` (no RoPE when None).  ``seq_len_dev`` (int32 CUDA scalar) replaces
+    ``seq_len`` for CUDA-graph replay.  q and k are left unspecified.
+    Returns (Y [B,H,1,D], log_gamma [B,H,1] float32, mix [B,H,1])."""
+    B, H, N, D = q.shape
+    assert N == 1, "a decode step takes one token (N=1)"
+    y = torch.empty_like(q)
+    lg = log_gamma_out if log_gamma_out is not None else torch.empty(B, H, 1, dtype=torch.float32, device=q.device)
+    mx = mix_out if mix_out is not None else torch.empty(B, H, 1, dtype=q.dtype, device=q.device)
+    dvals = decode_args(q, k, v, cache_k, cache_v, state_I_in, state_I_out, lg, mx, norm_w, R, seq_len, sm_scale, y,
+                        split_k, log_alpha, eps, seq_len_dev)
+    pvals = flat(tview(q), tview(k), tview(v), tview(gate_w), tview(gate_b), tview(mix_w), tview(mix_b),
+                 tview(fixed_mix), tview(cos), tview(sin), tview(lg), tview(mx), tview(cache_k), tview(cache_v),
+                 int(R), 0, 0, 1 if cos is not None else 0)
+    L = _capi.lib()
+    dbuf = _capi.FORMATS[DecodeArgs].pack(*dvals)
+    pbuf = _capi.FORMATS[_capi.PrepArgs].pack(*pvals)
+    status = L.hofa_decode_step_fwd(dbuf, pbuf, _capi.stream_handle(q.device))
+    if status != _capi.HOFA_OK:
+        raise _capi.HofaError("hofa_decode_step_fwd", status, L.hofa_last_error().decode())
+    return y, lg, mx

@@ -31,7 +31,7 @@ import torch.nn.functional as F
 from .chunk_gla_inlier import chunk_gla_inlier_fwd, gla_forward
 from .config import ModelConfig
 from .exact_attention import exact_attention_triton
-from .hofa_decode import fused_hofa_decode
+from .hofa_decode import fused_hofa_decode, fused_hofa_decode_step
 from .modules import RotaryEmbedding, apply_rotary_pos_emb
 from .prep import prep
 
@@ -124,7 +124,7 @@ class HybridOutlierFactorizedAttention(nn.Module):
         log_gamma = torch.empty(B, self.num_heads, N, dtype=torch.float32, device=Q.device)
         mix = torch.empty(B, self.num_heads, N, dtype=Q.dtype, device=Q.device) if mix_out else None
         cos, sin = self._rope_tables(pos0 + N) if self.r > 0 else (None, None)
-        prep(Q, K, V, log_gamma=log_gamma, mix_out=mix, cos=cos, sin=sin, R=self.r if cos is not None else 0,
+        prep(Q, K, V, log_gamma=log_gamma, mix_out=mix, cos=cos, sin=sin, R=self.r,
              pos0=pos0, cache_k=cache_k, cache_v=cache_v, use_rope=cos is not None, **self._gate_kwargs())
         return log_gamma, mix
 
@@ -235,16 +235,27 @@ class HybridOutlierFactorizedAttention(nn.Module):
 
         # ----- hybrid step
         seq_idx = cache_seq_len if cache_seq_len is not None else (cache_O[0].shape[2] if cache_O is not None else 0)
+        if state_I is None:
+            state_I = (torch.zeros(B, self.num_heads, self.j, self.d_head, device=x.device, dtype=torch.float32),
+                       torch.empty(B, self.num_heads, self.j, self.d_head, device=x.device, dtype=torch.float32))
+        if cache_O is not None and cache_seq_len is not None and cache_O[0].shape[2] > cache_seq_len:
+            # pre-allocated cache (the serving path): gates, RoPE at row
+            # cache_seq_len, the cache append and the decode core in one launch
+            state_in, state_out = state_I
+            assert state_in.dtype == torch.float32, f"Expected state_in to be float32, got {state_in.dtype}"
+            assert state_in.is_contiguous(), "Expected state_in to be contiguous"
+            cos, sin = self._rope_tables(seq_idx + 1)
+            Y, _, _ = fused_hofa_decode_step(
+                Q, K, V, cache_O[0], cache_O[1], state_in, state_out,
+                self.gla_scale.view(self.num_heads, self.d_head), self.r, cache_seq_len + 1,
+                (self.d_head / self.r) ** 0.5, cos=cos, sin=sin,
+                log_alpha=self.log_alpha if self.learnable_alpha else None, **self._gate_kwargs())
+            return self._out(Y, B, N, dtype_in), cache_O, (state_out, state_in)
         if cache_O is None:
             log_gamma, mix = self._prep(Q, K, V, 1, seq_idx)
             K_past, V_past = K[..., :self.r], V
             cache_O_new = (K_past, V_past)
             cache_seq_len = 0
-        elif cache_seq_len is not None and cache_O[0].shape[2] > cache_seq_len:
-            # pre-allocated cache: rotate and append row cache_seq_len in the same launch
-            log_gamma, mix = self._prep(Q, K, V, 1, seq_idx, cache_k=cache_O[0], cache_v=cache_O[1])
-            K_past, V_past = cache_O
-            cache_O_new = cache_O
         else:
             log_gamma, mix = self._prep(Q, K, V, 1, seq_idx)
             K_past = torch.cat([cache_O[0], K[..., :self.r]], dim=2)
@@ -252,9 +263,6 @@ class HybridOutlierFactorizedAttention(nn.Module):
             cache_O_new = (K_past, V_past)
             cache_seq_len = K_past.shape[2] - 1
 
-        if state_I is None:
-            state_I = (torch.zeros(B, self.num_heads, self.j, self.d_head, device=x.device, dtype=torch.float32),
-                       torch.empty(B, self.num_heads, self.j, self.d_head, device=x.device, dtype=torch.float32))
         state_in, state_out = state_I
         assert state_in.dtype == torch.float32, f"Expected state_in to be float32, got {state_in.dtype}"
         assert state_in.is_contiguous(), "Expected state_in to be contiguous"

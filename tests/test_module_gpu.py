@@ -131,3 +131,36 @@ def test_module_has_reference_parameter_names():
     g = load_golden("hofa_r16_alpha")
     m = make_layer(g)
     assert set(m.state_dict()) == set(g["state_dict"])
+
+
+def test_no_rope_layer_prefill_export_and_preallocated_decode_fp32():
+    """use_rope=False: the outlier cache holds un-rotated keys, written by the
+    prefill export and by the fused decode step."""
+    from outlierneuronattention_b200 import HybridOutlierFactorizedAttention, ModelConfig
+    torch.manual_seed(1)
+    cfg = ModelConfig(d_model=256, num_heads=4, num_layers=1, r=16, chunk_size=64, use_rope=False)
+    m = HybridOutlierFactorizedAttention(cfg)
+    gen = torch.Generator().manual_seed(1)
+    with torch.no_grad():
+        m.gate_proj.weight.copy_(torch.randn(m.gate_proj.weight.shape, generator=gen) * 0.02)
+        m.mix_proj.weight.copy_(torch.randn(m.mix_proj.weight.shape, generator=gen) * 0.02)
+    sd = {k: v.clone() for k, v in m.state_dict().items()}
+    oracle = OracleLayer(LayerShape(256, 4, 16, 64, use_rope=False), sd)
+    T0, T = 40, 48
+    x = torch.randn(2, T, 256, generator=gen)
+    ref_y, ref_cache, ref_state = oracle.forward(x[:, :T0].double(), return_state=True)
+    m = m.cuda().eval()
+    with torch.no_grad():
+        y, cache, state = m(x[:, :T0].cuda(), return_state=True)
+        assert err(y, ref_y) <= 1e-4 and err(cache[0], ref_cache[0]) <= 1e-4
+        Kc = torch.zeros(2, 4, T, 16, device="cuda")
+        Vc = torch.zeros(2, 4, T, 64, device="cuda")
+        Kc[:, :, :T0], Vc[:, :, :T0] = cache
+        cache = (Kc, Vc)
+        oc, ost = ref_cache, ref_state
+        for t in range(T0, T):
+            ys, cache, state = m.forward_step(x[:, t:t + 1].cuda(), cache, state, cache_seq_len=t)
+            oy, oc, ost = oracle.forward_step(x[:, t:t + 1].double(), oc, ost)
+            assert err(ys, oy) <= 1e-4
+    assert err(cache[0], oc[0]) <= 1e-4 and err(cache[1], oc[1]) <= 1e-4
+    assert err(state[0], ost) <= 1e-4 * max(1.0, ost.abs().max().item())
