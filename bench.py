@@ -344,6 +344,7 @@ def run_ours(args):
         out["prefill"] = measure_prefill(dev)
     if not args.no_config4 and world == 1:
         out["config4"] = measure_config4(dev)
+        out["layer_step"] = [measure_layer_step(dev, B=1), measure_layer_step(dev, B=4)]
     if not args.no_config4 and world > 1:
         out["config4_seqpar"] = measure_seqpar(dev, world)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -508,6 +509,53 @@ def measure_seqpar(dev, world, steps=3, warmup=2):
             "sharding": f"zig-zag: {2 * world} blocks of {T4 // (2 * world)} tokens, rank r owns r and {2 * world - 1}-r",
             "exchange": "NCCL all_gather of K_O/V (async, overlaps the first GLA pass) and of GLA block states",
             "timed": "gla (2 passes) + exchange + outlier attention, max over ranks"}
+
+
+def measure_layer_step(dev, B=4, steps=64, reps=5):
+    """Layer-level decode step (the drop-in module's forward_step with a
+    pre-allocated cache of L=4096 rows, d_model=1024, H=16, r=16, bf16
+    weights): q/k/v projections, the fused decode step (hofa_decode_step_fwd:
+    gates, RoPE, cache append and the attention core in one launch) and the
+    output projection, replayed from a CUDA graph; also the same step with
+    the new token's prep as a separate launch."""
+    from outlierneuronattention_b200 import HybridOutlierFactorizedAttention, ModelConfig
+    torch.manual_seed(0)
+    cfg = ModelConfig(d_model=1024, num_heads=H, num_layers=1, r=R, chunk_size=64)
+    m = HybridOutlierFactorizedAttention(cfg).to(device=dev, dtype=torch.bfloat16).eval()
+    g = torch.Generator(device=dev).manual_seed(9)
+    x = torch.randn(B, 1, 1024, device=dev, generator=g).to(torch.bfloat16)
+    # 4 rotating caches (4 x 42 MB at B=4 > L2), so each step streams its cache from HBM
+    caches = [((torch.randn(B, H, L, R, device=dev, generator=g) * KEY_STD).to(torch.bfloat16),
+               (torch.randn(B, H, L, D, device=dev, generator=g) * VAL_STD).to(torch.bfloat16)) for _ in range(4)]
+    st = (torch.randn(B, H, J, D, device=dev, generator=g) * 0.1, torch.empty(B, H, J, D, device=dev))
+    out = {}
+    for mode in ("fused", "two_launches"):
+        if mode == "two_launches":
+            os.environ["HOFA_DECODE_STEP_UNFUSED"] = "1"
+        stream = torch.cuda.Stream(dev)
+        with torch.no_grad(), torch.cuda.stream(stream):
+            for i in range(4):
+                m.forward_step(x, caches[i], st, cache_seq_len=L - 1)
+            stream.synchronize()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=stream):
+                for i in range(steps):
+                    m.forward_step(x, caches[i % 4], st, cache_seq_len=L - 1)
+            graph.replay()
+            stream.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            for _ in range(reps):
+                graph.replay()
+            e1.record(stream)
+            stream.synchronize()
+        del graph
+        os.environ.pop("HOFA_DECODE_STEP_UNFUSED", None)
+        out[f"{mode}_us_per_step"] = round(e0.elapsed_time(e1) * 1e3 / (reps * steps), 3)
+    out.update({"workload": f"config1-layer-forward_step-B{B}-L{L}", "d_model": 1024,
+                "tokens_per_s": round(B / (out["fused_us_per_step"] / 1e6), 1),
+                "note": "projections (cuBLAS) + fused decode step + out_proj per step"})
+    return out
 
 
 # ----------------------------------------------------------------------------- CPU arm

@@ -97,13 +97,24 @@ class HybridOutlierFactorizedAttention(nn.Module):
             mix_g = None
         return gate_logits.unsqueeze(-1), mix_g
 
+    def _qkv_weight(self):
+        """[W_q / d_h^(1/4); W_k / d_h^(1/4); W_v] as one [3*H*d_h, d_model]
+        weight (the reference's scaling, :100-104, folded in fp32), rebuilt
+        whenever one of the three weights is replaced or modified in place."""
+        ws = (self.W_q.weight, self.W_k.weight, self.W_v.weight)
+        key = tuple((w.data_ptr(), w._version, w.dtype, w.device) for w in ws)
+        if getattr(self, "_qkv_key", None) != key:
+            sf = self.d_head ** 0.25
+            self._qkv_w = torch.cat([(ws[0].float() / sf).to(ws[0].dtype), (ws[1].float() / sf).to(ws[1].dtype),
+                                     ws[2]], dim=0).detach()
+            self._qkv_key = key
+        return self._qkv_w
+
     def _project(self, x):
+        """Q, K, V [B,H,N,d_h] as strided views of one projection GEMM."""
         B, N, _ = x.shape
-        sf = self.d_head ** 0.25
-        Q = (self.W_q(x) / sf).view(B, N, self.num_heads, self.d_head).transpose(1, 2)
-        K = (self.W_k(x) / sf).view(B, N, self.num_heads, self.d_head).transpose(1, 2)
-        V = self.W_v(x).view(B, N, self.num_heads, self.d_head).transpose(1, 2)
-        return Q, K, V
+        qkv = F.linear(x, self._qkv_weight()).view(B, N, 3, self.num_heads, self.d_head)
+        return qkv[:, :, 0].transpose(1, 2), qkv[:, :, 1].transpose(1, 2), qkv[:, :, 2].transpose(1, 2)
 
     def _gate_kwargs(self):
         kw = dict(gate_w=self.gate_proj.weight, gate_b=self.gate_proj.bias)
