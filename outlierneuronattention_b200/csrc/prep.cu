@@ -116,19 +116,36 @@ prep_kernel(const PrepParams p) {
 // channel stride, 16-byte aligned rows and R % 8 == 0.
 constexpr int kVecThreads = 128;
 
+// Threads [0, kVecThreads) compute the gates and RoPE of one token each;
+// threads [kVecThreads, 2*kVecThreads) copy the same tokens' v rows into the
+// V cache meanwhile (the copy then costs no round trip of its own).
 template <typename T, int D, int RMAX>  // RMAX == R (compile-time, so RoPE stays in registers)
-__global__ void __launch_bounds__(kVecThreads)
+__global__ void __launch_bounds__(2 * kVecThreads)
 prep_vec_kernel(const PrepParams p) {
   constexpr int G = D / 8;  // 16-byte groups of 8 channels (2-byte types)
   __shared__ float w_gate[2 * D], w_mix[2 * D];
   const int h = blockIdx.y, b = blockIdx.z;
+  if (threadIdx.x >= kVecThreads) {
+    const int nv = blockIdx.x * kVecThreads + threadIdx.x - kVecThreads;
+    const int posv = (p.pos0_dev != nullptr ? *p.pos0_dev + p.pos0_dev_bias : p.pos0) + nv;
+    if (nv < p.N && p.cache_v != nullptr && posv >= 0 && posv < p.L) {
+      const T* vp = reinterpret_cast<const T*>(p.v) + b * p.sv[0] + h * p.sv[1] + (int64_t)nv * p.sv[2];
+      T* cv = reinterpret_cast<T*>(p.cache_v) + b * p.scv[0] + h * p.scv[1] + (int64_t)posv * p.scv[2];
+      uint4 rowv[G];
+#pragma unroll
+      for (int c = 0; c < G; ++c) rowv[c] = *reinterpret_cast<const uint4*>(vp + 8 * c);
+#pragma unroll
+      for (int c = 0; c < G; ++c) *reinterpret_cast<uint4*>(cv + 8 * c) = rowv[c];
+    }
+    return;
+  }
   const int n = blockIdx.x * kVecThreads + threadIdx.x;
   const bool has_mix = p.mix_w != nullptr;
   for (int i = threadIdx.x; i < 2 * D; i += kVecThreads) {
     w_gate[i] = ld_any(p.gate_w, p.dt_gw, h * p.sgw[0] + i * p.sgw[1]);
     w_mix[i] = has_mix ? ld_any(p.mix_w, p.dt_mw, h * p.smw[0] + i * p.smw[1]) : 0.f;
   }
-  __syncthreads();
+  asm volatile("bar.sync 1, %0;" ::"n"(kVecThreads) : "memory");  // the gate/RoPE threads only
   if (n >= p.N) return;
   T* qp = reinterpret_cast<T*>(p.q) + b * p.sq[0] + h * p.sq[1] + (int64_t)n * p.sq[2];
   T* kp = reinterpret_cast<T*>(p.k) + b * p.sk[0] + h * p.sk[1] + (int64_t)n * p.sk[2];
@@ -160,10 +177,28 @@ prep_vec_kernel(const PrepParams p) {
     constexpr int half = RMAX / 2;
     const int prow = pos < 0 ? 0 : (pos < p.P ? pos : p.P - 1);
     float qr[RMAX > 0 ? RMAX : 1], kr[RMAX > 0 ? RMAX : 1];
+    float csv[RMAX > 0 ? RMAX : 1], snv[RMAX > 0 ? RMAX : 1];
+    const float* cs_row = reinterpret_cast<const float*>(p.cos) + (int64_t)prow * p.scos[0];
+    const float* sn_row = reinterpret_cast<const float*>(p.sin) + (int64_t)prow * p.ssin[0];
+    if (RMAX % 4 == 0 && p.dt_cs == HOFA_DTYPE_F32 && p.scos[1] == 1 && p.ssin[1] == 1 &&
+        ((reinterpret_cast<uintptr_t>(cs_row) | reinterpret_cast<uintptr_t>(sn_row)) & 15u) == 0) {
+#pragma unroll
+      for (int c = 0; c < RMAX; c += 4) {  // contiguous fp32 table rows: 16-byte loads
+        const float4 a = *reinterpret_cast<const float4*>(cs_row + c);
+        const float4 z = *reinterpret_cast<const float4*>(sn_row + c);
+        csv[c] = a.x; csv[c + 1] = a.y; csv[c + 2] = a.z; csv[c + 3] = a.w;
+        snv[c] = z.x; snv[c + 1] = z.y; snv[c + 2] = z.z; snv[c + 3] = z.w;
+      }
+    } else {
+#pragma unroll
+      for (int c = 0; c < RMAX; ++c) {
+        csv[c] = ld_any(p.cos, p.dt_cs, (int64_t)prow * p.scos[0] + c * p.scos[1]);
+        snv[c] = ld_any(p.sin, p.dt_cs, (int64_t)prow * p.ssin[0] + c * p.ssin[1]);
+      }
+    }
 #pragma unroll
     for (int c = 0; c < RMAX; ++c) {
-      const float cs = ld_any(p.cos, p.dt_cs, (int64_t)prow * p.scos[0] + c * p.scos[1]);
-      const float sn = ld_any(p.sin, p.dt_cs, (int64_t)prow * p.ssin[0] + c * p.ssin[1]);
+      const float cs = csv[c], sn = snv[c];
       const float qh = c < half ? -qo[c + half] : qo[c - half];
       const float kh = c < half ? -ko[c + half] : ko[c - half];
       qr[c] = qo[c] * cs + qh * sn;
@@ -190,12 +225,6 @@ prep_vec_kernel(const PrepParams p) {
       *reinterpret_cast<uint4*>(ck + 8 * c) = *reinterpret_cast<const uint4*>(tk);
     }
   }
-  if (p.cache_v != nullptr && pos >= 0 && pos < p.L) {
-    const T* vp = reinterpret_cast<const T*>(p.v) + b * p.sv[0] + h * p.sv[1] + (int64_t)n * p.sv[2];
-    T* cv = reinterpret_cast<T*>(p.cache_v) + b * p.scv[0] + h * p.scv[1] + (int64_t)pos * p.scv[2];
-#pragma unroll
-    for (int c = 0; c < G; ++c) *reinterpret_cast<uint4*>(cv + 8 * c) = *reinterpret_cast<const uint4*>(vp + 8 * c);
-  }
 }
 
 template <typename T>
@@ -206,7 +235,7 @@ cudaError_t launch_t(const PrepParams& p, cudaStream_t st) {
       const int r = p.R;  // the outlier channels: rotated when p.rope, copied to cache_k either way
       bool launched = true;
 #define HOFA_PREP_VEC(DD, RR) \
-  else if (p.D == DD && r == RR) prep_vec_kernel<T, DD, RR><<<grid, kVecThreads, 0, st>>>(p);
+  else if (p.D == DD && r == RR) prep_vec_kernel<T, DD, RR><<<grid, 2 * kVecThreads, 0, st>>>(p);
       if (false) {}
       HOFA_PREP_VEC(64, 0) HOFA_PREP_VEC(64, 8) HOFA_PREP_VEC(64, 16) HOFA_PREP_VEC(64, 32)
       HOFA_PREP_VEC(128, 0) HOFA_PREP_VEC(128, 16) HOFA_PREP_VEC(128, 32) HOFA_PREP_VEC(128, 64)
