@@ -17,7 +17,7 @@
 
 namespace hofa {
 int gla_internal_chunk(int D);
-size_t gla_tc_workspace_bytes(int64_t B, int64_t H, int64_t T, int64_t J);
+size_t gla_tc_workspace_bytes(int64_t B, int64_t H, int64_t T, int64_t J, int64_t D);
 bool gla_tc_eligible(const GlaParams& p, int dtype);
 cudaError_t launch_gla_tc(const GlaParams& p, int dtype, cudaStream_t st, bool* taken);
 int gla_tc_chunk();
@@ -468,7 +468,7 @@ size_t hofa_gla_workspace_size(int32_t B, int32_t H, int32_t T, int32_t D, int32
   if (nseg > nchunks) nseg = nchunks;
   const int64_t J = D - R;
   const size_t cuda_core = (size_t)B * H * nseg * (J * D + J) * sizeof(float) + 256;
-  const size_t tensor_core = hofa::gla_tc_workspace_bytes(B, H, T, J);
+  const size_t tensor_core = hofa::gla_tc_workspace_bytes(B, H, T, J, D);
   return cuda_core > tensor_core ? cuda_core : tensor_core;
 }
 
@@ -519,7 +519,7 @@ int hofa_prefill_gla_fwd(const hofa_gla_args* a, void* stream) {
     hofa::GlaParams tp;
     memset(&tp, 0, sizeof(tp));
     tp.D = (int)D; tp.R = R; tp.log_alpha = alpha ? a->log_alpha.data : nullptr;
-    const size_t need_tc = hofa::gla_tc_workspace_bytes(B, H, T, J);
+    const size_t need_tc = hofa::gla_tc_workspace_bytes(B, H, T, J, D);
     if (hofa::gla_tc_eligible(tp, dt) && a->workspace != nullptr && a->workspace_bytes >= need_tc &&
         ((reinterpret_cast<uintptr_t>(a->workspace) & 15u) == 0)) {
       tp = p;  // side-tensor strides filled above
@@ -544,7 +544,7 @@ int hofa_prefill_gla_fwd(const hofa_gla_args* a, void* stream) {
       tp.dt_mg = p.fuse ? a->mix_g.dtype : 0;
       tp.dt_gs = p.fuse ? a->gla_scale.dtype : 0;
       tp.ws_state = reinterpret_cast<float*>(a->workspace);
-      tp.ws_decay = tp.ws_state + (size_t)B * H * tp.nseg * J * 64;
+      tp.ws_decay = tp.ws_state + (size_t)B * H * tp.nseg * J * D;
       bool taken = false;
       cudaError_t e = hofa::launch_gla_tc(tp, dt, reinterpret_cast<cudaStream_t>(stream), &taken);
       if (e != cudaSuccess) return cuda_fail(e, "hofa_prefill_gla_fwd launch (tensor cores)");

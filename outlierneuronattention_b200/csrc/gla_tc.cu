@@ -1,22 +1,24 @@
 // Prefill GLA on the tensor cores (tcgen05 + TMEM + TMA), chunk-parallel.
 //
 // Replaces chunk_gla_fwd_kernel (src/chunk_gla_inlier.py:5-150) for bf16/f16
-// inputs with head dim 64 and a per-head scalar decay (no log_alpha).  The
+// inputs with head dim 64 or 128 and a per-head scalar decay (no log_alpha).
+// Operand tiles are [128 tokens x D channels] in 64-channel column blocks of
+// 128-byte swizzled rows (one TMA box each), so D = 128 uses two blocks.  The
 // reference runs one program per (b,h) that walks every chunk in sequence; here
 // every 128-token chunk of every (b,h) is its own CTA in two of three launches:
 //
 //   A  gla_tc_state_kernel   (one CTA per chunk c)
 //        G   = inclusive cumsum of log_gamma over the chunk, G_C = its total
 //        Kd  = K_I * exp(G_C - G_t)        (rows of the K tile, in shared memory)
-//        dS  = Kd^T V                      tcgen05.mma, M = 64 (inlier rows, padded),
-//                                          N = 64, K = 128 tokens, A and B MN-major
-//        -> workspace: dS_c [J x 64] fp32 and G_C
+//        dS  = Kd^T V                      tcgen05.mma, M = 64 or 128 (inlier rows,
+//                                          padded), N = D, K = 128 tokens, A and B MN-major
+//        -> workspace: dS_c [J x D] fp32 and G_C
 //   B  gla_tc_scan_kernel    (one thread per state element of a head)
 //        S_0 = state_init or 0;  start_c = S before chunk c;  S <- exp(G_C) S + dS_c
 //        start_c overwrites dS_c in the workspace; the last S goes to state_out
 //   C  gla_tc_out_kernel     (one CTA per chunk c)
 //        A   = Q_I K_I^T            tcgen05.mma M=128, N=128, K=J (A/B K-major)
-//        Y2  = Q_I start_c          tcgen05.mma M=128, N=64,  K=J (start_c as a bf16
+//        Y2  = Q_I start_c          tcgen05.mma M=128, N=D,   K=J (start_c as a bf16
 //                                   MN-major operand)
 //        P   = A * exp(G_i - G_j) [j <= i]  -> bf16, written back into TMEM
 //        Y1  = P V                  tcgen05.mma, A = P from TMEM, V MN-major
@@ -45,8 +47,19 @@ namespace {
 
 constexpr int kC = 128;           // tokens per chunk
 constexpr int kThreads = 128;
-constexpr uint32_t kTile = kC * 128;  // one [128 rows x 128 B] operand tile
-constexpr size_t kOutSmem = 80 * 1024;  // keeps <= 2 CTAs (2 x 256 TMEM columns) per SM
+constexpr uint32_t kTile = kC * 128;  // one [128 rows x 128 B] column block (64 channels)
+
+template <int D>
+struct Geo {
+  static constexpr int NB = D / 64;                      // 64-channel column blocks
+  static constexpr uint32_t OP = NB * kTile;             // one operand tile (128 tokens x D)
+  static constexpr uint32_t LBO = NB > 1 ? kTile : 16;   // byte distance of the column blocks
+  static constexpr int STATE_M = D == 64 ? 64 : 128;     // MMA M of the state kernel
+  static constexpr uint32_t OUT_COLS = D == 64 ? 256 : 512;  // A (128) + Y1 (D) + Y2 (D), power of two
+  static constexpr size_t STATE_SMEM = 2 * OP + 1024 + 256;
+  // D = 64: 80 KB keeps <= 2 CTAs (2 x 256 TMEM columns) per SM; D = 128: one CTA
+  static constexpr size_t OUT_SMEM = D == 64 ? 80 * 1024 : 4 * OP + 1024 + 4096;
+};
 
 __device__ __forceinline__ uint32_t pack2(float a, float b, bool bf16) {
   if (bf16) {
@@ -79,17 +92,18 @@ __device__ __forceinline__ void fence_async_smem() {
 // ---------------------------------------------------------------------------
 // A: per-chunk state contribution dS = (K * exp(G_C - G_t))^T V
 // ---------------------------------------------------------------------------
-template <typename T>
+template <typename T, int D>
 __global__ void __launch_bounds__(kThreads)
 gla_tc_state_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
                     const GlaParams p) {
+  using Gm = Geo<D>;
   constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
-  constexpr uint32_t IDESC = sm100::idesc_f16(BF16, true, true, 64, 64);
+  constexpr uint32_t IDESC = sm100::idesc_f16(BF16, true, true, Gm::STATE_M, D);
   extern __shared__ unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* sK = base;
-  unsigned char* sV = base + kTile;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(base + 2 * kTile);
+  unsigned char* sV = base + Gm::OP;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + 2 * Gm::OP);
   float* sm_warp = reinterpret_cast<float*>(bars + 4);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm_warp + 4);
   int* err = reinterpret_cast<int*>(tmem_slot + 1);
@@ -105,7 +119,7 @@ gla_tc_state_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
     sm100::fence_mbar_init();
   }
   if (warp == 0) {
-    sm100::tmem_alloc(tmem_slot, 64);
+    sm100::tmem_alloc(tmem_slot, D);
     sm100::tmem_relinquish();
   }
   sm100::tc_fence_before();
@@ -113,9 +127,12 @@ gla_tc_state_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
   sm100::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   if (tid == 0) {
-    sm100::mbar_arrive_expect_tx(&bars[0], 2 * kTile);
-    sm100::tma_load_4d(sK, &tk, p.R, t0, h, b, &bars[0]);
-    sm100::tma_load_4d(sV, &tv, 0, t0, h, b, &bars[0]);
+    sm100::mbar_arrive_expect_tx(&bars[0], 2 * Gm::OP);
+#pragma unroll
+    for (int nb = 0; nb < Gm::NB; ++nb) {
+      sm100::tma_load_4d(sK + nb * kTile, &tk, p.R + 64 * nb, t0, h, b, &bars[0]);
+      sm100::tma_load_4d(sV + nb * kTile, &tv, 64 * nb, t0, h, b, &bars[0]);
+    }
   }
   const int t = t0 + tid;
   const float g = t < p.T ? ld_any(p.log_gamma, p.dt_lg, b * p.slg[0] + h * p.slg[1] + (int64_t)t * p.slg[2]) : 0.f;
@@ -126,22 +143,25 @@ gla_tc_state_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
   if (!sm100::mbar_wait(&bars[0], 0)) atomicOr(err, 1);
   __syncthreads();
   const float gc = sm_gc;
-  // Kd: scale this thread's K row (all 128 bytes; swizzling only permutes chunks within the row)
+  // Kd: scale this thread's K row (every column block; swizzling only permutes chunks within a row)
   {
-    const float w = exp2f((gc - G) * kLog2e);
-    uint4* row = reinterpret_cast<uint4*>(sK + tid * 128);
+    const float w = sm100::ex2_approx((gc - G) * kLog2e);
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      uint4 u = row[q];
-      uint32_t* pu = reinterpret_cast<uint32_t*>(&u);
+    for (int nb = 0; nb < Gm::NB; ++nb) {
+      uint4* row = reinterpret_cast<uint4*>(sK + nb * kTile + tid * 128);
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float a, bb;
-        if (BF16) bf16x2_to_f(pu[e], a, bb);
-        else f16x2_to_f(pu[e], a, bb);
-        pu[e] = pack2(a * w, bb * w, BF16);
+      for (int q = 0; q < 8; ++q) {
+        uint4 u = row[q];
+        uint32_t* pu = reinterpret_cast<uint32_t*>(&u);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          float a, bb;
+          if (BF16) bf16x2_to_f(pu[e], a, bb);
+          else f16x2_to_f(pu[e], a, bb);
+          pu[e] = pack2(a * w, bb * w, BF16);
+        }
+        row[q] = u;
       }
-      row[q] = u;
     }
   }
   fence_async_smem();
@@ -149,8 +169,8 @@ gla_tc_state_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
   __syncthreads();
   if (tid == 0 && !*verr) {
     sm100::tc_fence_after();
-    const uint64_t adesc = sm100::smem_desc(sK, 16, 1024, sm100::kSwizzle128);
-    const uint64_t bdesc = sm100::smem_desc(sV, 16, 1024, sm100::kSwizzle128);
+    const uint64_t adesc = sm100::smem_desc(sK, Gm::LBO, 1024, sm100::kSwizzle128);
+    const uint64_t bdesc = sm100::smem_desc(sV, Gm::LBO, 1024, sm100::kSwizzle128);
 #pragma unroll
     for (int ks = 0; ks < kC / 16; ++ks)
       sm100::mma_ss(tmem, adesc + (uint64_t)(ks * 2048 >> 4), bdesc + (uint64_t)(ks * 2048 >> 4), IDESC, ks > 0);
@@ -158,16 +178,17 @@ gla_tc_state_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
   }
   if (!*verr && !sm100::mbar_wait(&bars[1], 0)) atomicOr(err, 1);
   sm100::tc_fence_after();
-  // D (M = 64): row j lives in lane 32*(j/16) + j%16
-  const int j = 16 * warp + lane;
+  // D (M = 64): row j lives in lane 32*(j/16) + j%16; (M = 128): row j in lane j
+  const int j = Gm::STATE_M == 64 ? 16 * warp + lane : tid;
+  const bool row_ok = (Gm::STATE_M == 64 ? lane < 16 : true) && j < p.J && !*verr;
   const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
-  float* dst = p.ws_state + (((int64_t)bh * p.nseg + c) * p.J + j) * 64;
+  float* dst = p.ws_state + (((int64_t)bh * p.nseg + c) * p.J + j) * D;
 #pragma unroll
-  for (int half = 0; half < 2; ++half) {
+  for (int half = 0; half < D / 32; ++half) {
     uint32_t r[32];
     sm100::tmem_ld32(taddr + half * 32, r);
     sm100::tc_wait_ld();
-    if (lane < 16 && j < p.J && !*verr) {
+    if (row_ok) {
 #pragma unroll
       for (int i = 0; i < 32; i += 4)
         *reinterpret_cast<float4*>(dst + half * 32 + i) =
@@ -178,22 +199,22 @@ gla_tc_state_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
   sm100::tc_fence_before();
   __syncthreads();
   if (*err && tid == 0) atomicOr(&g_gla_tc_status, 1);
-  if (warp == 0) sm100::tmem_dealloc(tmem, 64);
+  if (warp == 0) sm100::tmem_dealloc(tmem, D);
 }
 
 // ---------------------------------------------------------------------------
 // B: scan over chunks (start state of every chunk, final state)
 // ---------------------------------------------------------------------------
 __global__ void __launch_bounds__(256) gla_tc_scan_kernel(const GlaParams p) {
-  const int e = blockIdx.x * 256 + threadIdx.x;  // element j*64 + d of the head's state
+  const int e = blockIdx.x * 256 + threadIdx.x;  // element j*D + d of the head's state
   const int h = blockIdx.y, b = blockIdx.z;
-  if (e >= p.J * 64) return;
-  const int j = e / 64, d = e % 64;
+  if (e >= p.J * p.D) return;
+  const int j = e / p.D, d = e % p.D;
   const int64_t bh = (int64_t)b * p.H + h;
   float S = p.state_init ? p.state_init[b * p.ssi[0] + h * p.ssi[1] + j * p.ssi[2] + d] : 0.f;
-  float* ws = p.ws_state + bh * p.nseg * p.J * 64 + e;
+  float* ws = p.ws_state + bh * p.nseg * p.J * p.D + e;
   const float* gc = p.ws_decay + bh * p.nseg;
-  const int64_t cs = (int64_t)p.J * 64;
+  const int64_t cs = (int64_t)p.J * p.D;
   // 16 chunk contributions per round trip: their loads are independent, only
   // the fmaf chain is sequential
   constexpr int kU = 16;
@@ -219,23 +240,23 @@ __global__ void __launch_bounds__(256) gla_tc_scan_kernel(const GlaParams p) {
 // ---------------------------------------------------------------------------
 // C: per-chunk output
 // ---------------------------------------------------------------------------
-template <typename T>
+template <typename T, int D>
 __global__ void __launch_bounds__(kThreads, 1)
 gla_tc_out_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                   const __grid_constant__ CUtensorMap tv, const GlaParams p) {
+  using Gm = Geo<D>;
   constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr uint32_t IDESC_A = sm100::idesc_f16(BF16, false, false, 128, 128);
-  constexpr uint32_t IDESC_Y2 = sm100::idesc_f16(BF16, false, true, 128, 64);
-  constexpr uint32_t IDESC_Y1 = sm100::idesc_f16(BF16, false, true, 128, 64);
+  constexpr uint32_t IDESC_Y = sm100::idesc_f16(BF16, false, true, 128, D);
   extern __shared__ unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* sQ = base;
-  unsigned char* sK = base + kTile;
-  unsigned char* sV = base + 2 * kTile;
-  unsigned char* sS = base + 3 * kTile;            // start state, [64 rows j][64 d] bf16, 8 KB
-  float* sG = reinterpret_cast<float*>(sS + 64 * 128);     // cumulative log2 decay per token
-  float* sGS = sG + kC;                                     // gla_scale[h, 0:64]
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sGS + 64);
+  unsigned char* sK = base + Gm::OP;
+  unsigned char* sV = base + 2 * Gm::OP;
+  unsigned char* sS = base + 3 * Gm::OP;              // start state, [128 rows j][D] bf16 MN-major blocks
+  float* sG = reinterpret_cast<float*>(sS + Gm::OP);  // cumulative log2 decay per token
+  float* sGS = sG + kC;                                // gla_scale[h, 0:D]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sGS + D);
   float* sm_warp = reinterpret_cast<float*>(bars + 4);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm_warp + 4);
   int* err = reinterpret_cast<int*>(tmem_slot + 1);
@@ -252,43 +273,49 @@ gla_tc_out_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
     sm100::fence_mbar_init();
   }
   if (warp == 0) {
-    sm100::tmem_alloc(tmem_slot, 256);
+    sm100::tmem_alloc(tmem_slot, Gm::OUT_COLS);
     sm100::tmem_relinquish();
   }
   sm100::tc_fence_before();
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tA = tmem, tY1 = tmem + 128, tY2 = tmem + 192;
+  const uint32_t tA = tmem, tY1 = tmem + 128, tY2 = tmem + 128 + D;
   const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
   if (tid == 0) {
-    sm100::mbar_arrive_expect_tx(&bars[0], 3 * kTile);
-    sm100::tma_load_4d(sQ, &tq, p.R, t0, h, b, &bars[0]);
-    sm100::tma_load_4d(sK, &tk, p.R, t0, h, b, &bars[0]);
-    sm100::tma_load_4d(sV, &tv, 0, t0, h, b, &bars[0]);
+    sm100::mbar_arrive_expect_tx(&bars[0], 3 * Gm::OP);
+#pragma unroll
+    for (int nb = 0; nb < Gm::NB; ++nb) {
+      sm100::tma_load_4d(sQ + nb * kTile, &tq, p.R + 64 * nb, t0, h, b, &bars[0]);
+      sm100::tma_load_4d(sK + nb * kTile, &tk, p.R + 64 * nb, t0, h, b, &bars[0]);
+      sm100::tma_load_4d(sV + nb * kTile, &tv, 64 * nb, t0, h, b, &bars[0]);
+    }
   }
-  // start state of this chunk -> bf16 MN-major operand (row j = 128 bytes, 128B swizzle)
+  // start state of this chunk -> bf16 MN-major operand (row j = 128 bytes per block, 128B swizzle)
   if (tid < 16 * KS) {
     const int j = tid;
-    uint4* row = reinterpret_cast<uint4*>(sS + j * 128);
-    const float* src = p.ws_state + (((int64_t)bh * p.nseg + c) * J + j) * 64;
+    const float* src = p.ws_state + (((int64_t)bh * p.nseg + c) * J + j) * D;
 #pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      uint4 u = make_uint4(0, 0, 0, 0);
-      if (j < J) {
-        const float4 a = *reinterpret_cast<const float4*>(src + q * 8);
-        const float4 bq = *reinterpret_cast<const float4*>(src + q * 8 + 4);
-        u.x = pack2(a.x, a.y, BF16); u.y = pack2(a.z, a.w, BF16);
-        u.z = pack2(bq.x, bq.y, BF16); u.w = pack2(bq.z, bq.w, BF16);
+    for (int nb = 0; nb < Gm::NB; ++nb) {
+      uint4* row = reinterpret_cast<uint4*>(sS + nb * kTile + j * 128);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        uint4 u = make_uint4(0, 0, 0, 0);
+        if (j < J) {
+          const float4 a = *reinterpret_cast<const float4*>(src + nb * 64 + q * 8);
+          const float4 bq = *reinterpret_cast<const float4*>(src + nb * 64 + q * 8 + 4);
+          u.x = pack2(a.x, a.y, BF16); u.y = pack2(a.z, a.w, BF16);
+          u.z = pack2(bq.x, bq.y, BF16); u.w = pack2(bq.z, bq.w, BF16);
+        }
+        row[q ^ (j & 7)] = u;
       }
-      row[q ^ (j & 7)] = u;
     }
   }
   const int t = t0 + tid;
   const float g = t < p.T ? ld_any(p.log_gamma, p.dt_lg, b * p.slg[0] + h * p.slg[1] + (int64_t)t * p.slg[2]) : 0.f;
   const float G = block_scan128(g, sm_warp, tid) * kLog2e;   // log2 units from here on
   sG[tid] = G;
-  if (tid < 64) sGS[tid] = p.fuse ? ld_any(p.gla_scale, p.dt_gs, h * p.sgs[0] + tid * p.sgs[1]) : 1.f;
+  for (int d = tid; d < D; d += kThreads) sGS[d] = p.fuse ? ld_any(p.gla_scale, p.dt_gs, h * p.sgs[0] + d * p.sgs[1]) : 1.f;
   float mix = 0.f;
   if (p.fuse && t < p.T) mix = ld_any(p.mix_g, p.dt_mg, b * p.smg[0] + h * p.smg[1] + (int64_t)t * p.smg[2]);
   fence_async_smem();
@@ -300,10 +327,12 @@ gla_tc_out_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
     sm100::tc_fence_after();
     const uint64_t qdesc = sm100::smem_desc(sQ, 16, 1024, sm100::kSwizzle128);
     const uint64_t kdesc = sm100::smem_desc(sK, 16, 1024, sm100::kSwizzle128);
-    const uint64_t sdesc = sm100::smem_desc(sS, 16, 1024, sm100::kSwizzle128);
-    for (int ks = 0; ks < KS; ++ks) sm100::mma_ss(tA, qdesc + 2 * ks, kdesc + 2 * ks, IDESC_A, ks > 0);
+    const uint64_t sdesc = sm100::smem_desc(sS, Gm::LBO, 1024, sm100::kSwizzle128);
+    // K-major steps of 16 channels: 4 per 128-byte block (32 B each), blocks kTile apart
+    auto kstep = [](int ks) { return (uint64_t)(((ks >> 2) * kTile + (ks & 3) * 32) >> 4); };
+    for (int ks = 0; ks < KS; ++ks) sm100::mma_ss(tA, qdesc + kstep(ks), kdesc + kstep(ks), IDESC_A, ks > 0);
     for (int ks = 0; ks < KS; ++ks)
-      sm100::mma_ss(tY2, qdesc + 2 * ks, sdesc + (uint64_t)(ks * 2048 >> 4), IDESC_Y2, ks > 0);
+      sm100::mma_ss(tY2, qdesc + kstep(ks), sdesc + (uint64_t)(ks * 2048 >> 4), IDESC_Y, ks > 0);
     sm100::mma_commit(&bars[1]);
   }
   if (!*verr && !sm100::mbar_wait(&bars[1], 0)) atomicOr(err, 1);
@@ -334,55 +363,68 @@ gla_tc_out_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
   __syncthreads();
   if (tid == 0 && !*verr) {
     sm100::tc_fence_after();
-    const uint64_t vdesc = sm100::smem_desc(sV, 16, 1024, sm100::kSwizzle128);
+    const uint64_t vdesc = sm100::smem_desc(sV, Gm::LBO, 1024, sm100::kSwizzle128);
 #pragma unroll
     for (int kk = 0; kk < kC / 16; ++kk)
-      sm100::mma_ts(tY1, tA + kk * 8, vdesc + (uint64_t)(kk * 2048 >> 4), IDESC_Y1, kk > 0);
+      sm100::mma_ts(tY1, tA + kk * 8, vdesc + (uint64_t)(kk * 2048 >> 4), IDESC_Y, kk > 0);
     sm100::mma_commit(&bars[1]);
   }
   if (!*verr && !sm100::mbar_wait(&bars[1], 1)) atomicOr(err, 1);
   sm100::tc_fence_after();
 
-  // epilogue: y = Y1 + exp(G_i) Y2, fused (1 - mix) * gla_scale * RMSNorm(y)
-  float y[64];
+  // epilogue: y = Y1 + exp(G_i) Y2, fused (1 - mix) * gla_scale * RMSNorm(y); two passes over
+  // 32-column chunks of TMEM (sum of squares, then the scaled store)
   const float eg = sm100::ex2_approx(G);
+  float scale = 1.f;
+  if (p.fuse) {
+    float ss = 0.f;
 #pragma unroll
-  for (int cc = 0; cc < 64; cc += 32) {
+    for (int cc = 0; cc < D; cc += 32) {
+      uint32_t a[32], bb[32];
+      sm100::tmem_ld32(tY1 + lane_off + cc, a);
+      sm100::tmem_ld32(tY2 + lane_off + cc, bb);
+      sm100::tc_wait_ld();
+#pragma unroll
+      for (int u = 0; u < 32; ++u) {
+        const float y = fmaf(eg, __uint_as_float(bb[u]), __uint_as_float(a[u]));
+        ss = fmaf(y, y, ss);
+      }
+    }
+    scale = rsqrtf(ss / (float)D + p.eps) * (1.f - mix);
+  }
+  const bool store = t < p.T && !*verr;
+  T* yp = reinterpret_cast<T*>(p.y) + b * p.sy[0] + h * p.sy[1] + (int64_t)(store ? t : 0) * p.sy[2];
+  const bool vec = p.sy[3] == 1 && (reinterpret_cast<uintptr_t>(yp) & 15u) == 0;
+#pragma unroll
+  for (int cc = 0; cc < D; cc += 32) {
     uint32_t a[32], bb[32];
-    sm100::tmem_ld32(tY1 + lane_off + cc, a);
+    sm100::tmem_ld32(tY1 + lane_off + cc, a);  // warp-collective: every lane executes it
     sm100::tmem_ld32(tY2 + lane_off + cc, bb);
     sm100::tc_wait_ld();
+    if (store) {
+      float y[32];
 #pragma unroll
-    for (int u = 0; u < 32; ++u) y[cc + u] = fmaf(eg, __uint_as_float(bb[u]), __uint_as_float(a[u]));
-  }
-  if (t < p.T && !*verr) {
-    float scale = 1.f;
-    if (p.fuse) {
-      float ss = 0.f;
+      for (int u = 0; u < 32; ++u) y[u] = fmaf(eg, __uint_as_float(bb[u]), __uint_as_float(a[u])) * scale * sGS[cc + u];
+      if (vec) {
 #pragma unroll
-      for (int d = 0; d < 64; ++d) ss = fmaf(y[d], y[d], ss);
-      scale = rsqrtf(ss / 64.f + p.eps) * (1.f - mix);
-    }
-    T* yp = reinterpret_cast<T*>(p.y) + b * p.sy[0] + h * p.sy[1] + (int64_t)t * p.sy[2];
-    if (p.sy[3] == 1 && (reinterpret_cast<uintptr_t>(yp) & 15u) == 0) {
+        for (int d = 0; d < 32; d += 8) {
+          uint4 w;
+          w.x = pack2(y[d], y[d + 1], BF16);
+          w.y = pack2(y[d + 2], y[d + 3], BF16);
+          w.z = pack2(y[d + 4], y[d + 5], BF16);
+          w.w = pack2(y[d + 6], y[d + 7], BF16);
+          *reinterpret_cast<uint4*>(yp + cc + d) = w;
+        }
+      } else {
 #pragma unroll
-      for (int d = 0; d < 64; d += 8) {
-        uint4 w;
-        w.x = pack2(y[d] * scale * sGS[d], y[d + 1] * scale * sGS[d + 1], BF16);
-        w.y = pack2(y[d + 2] * scale * sGS[d + 2], y[d + 3] * scale * sGS[d + 3], BF16);
-        w.z = pack2(y[d + 4] * scale * sGS[d + 4], y[d + 5] * scale * sGS[d + 5], BF16);
-        w.w = pack2(y[d + 6] * scale * sGS[d + 6], y[d + 7] * scale * sGS[d + 7], BF16);
-        *reinterpret_cast<uint4*>(yp + d) = w;
+        for (int d = 0; d < 32; ++d) yp[(int64_t)(cc + d) * p.sy[3]] = from_f<T>(y[d]);
       }
-    } else {
-#pragma unroll
-      for (int d = 0; d < 64; ++d) yp[(int64_t)d * p.sy[3]] = from_f<T>(y[d] * scale * sGS[d]);
     }
   }
   sm100::tc_fence_before();
   __syncthreads();
   if (*err && tid == 0) atomicOr(&g_gla_tc_status, 1);
-  if (warp == 0) sm100::tmem_dealloc(tmem, 256);
+  if (warp == 0) sm100::tmem_dealloc(tmem, Gm::OUT_COLS);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -399,14 +441,14 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// [B,H,T,64] operand map with a (64 channels x 128 tokens) box, 128-byte swizzle
-bool make_map(CUtensorMap* m, const void* ptr, bool bf16, int64_t T, int64_t H, int64_t B, const int64_t* s) {
+// [B,H,T,D] operand map with a (64 channels x 128 tokens) box, 128-byte swizzle
+bool make_map(CUtensorMap* m, const void* ptr, bool bf16, int64_t D, int64_t T, int64_t H, int64_t B, const int64_t* s) {
   auto fn = encode_fn();
   if (fn == nullptr) return false;
   if ((reinterpret_cast<uintptr_t>(ptr) & 15u) != 0 || s[3] != 1) return false;
   const int64_t sb = B > 1 ? s[0] : 8, sh = H > 1 ? s[1] : 8;
   if (s[2] % 8 || sh % 8 || sb % 8 || s[2] <= 0 || sh <= 0 || sb <= 0) return false;
-  cuuint64_t dims[4] = {64, (cuuint64_t)T, (cuuint64_t)H, (cuuint64_t)B};
+  cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)T, (cuuint64_t)H, (cuuint64_t)B};  // channels past D read as 0
   cuuint64_t strides[3] = {(cuuint64_t)(s[2] * 2), (cuuint64_t)(sh * 2), (cuuint64_t)(sb * 2)};
   cuuint32_t box[4] = {64, (cuuint32_t)kC, 1, 1};
   cuuint32_t estr[4] = {1, 1, 1, 1};
@@ -415,44 +457,43 @@ bool make_map(CUtensorMap* m, const void* ptr, bool bf16, int64_t T, int64_t H, 
             CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <typename T>
+template <typename T, int D>
 cudaError_t launch_t(const GlaParams& p, cudaStream_t st, bool* taken) {
+  using Gm = Geo<D>;
   const bool bf16 = std::is_same<T, __nv_bfloat16>::value;
   CUtensorMap mq, mk, mv;
-  if (!make_map(&mq, p.q, bf16, p.T, p.H, p.B, p.sq) || !make_map(&mk, p.k, bf16, p.T, p.H, p.B, p.sk) ||
-      !make_map(&mv, p.v, bf16, p.T, p.H, p.B, p.sv))
+  if (!make_map(&mq, p.q, bf16, D, p.T, p.H, p.B, p.sq) || !make_map(&mk, p.k, bf16, D, p.T, p.H, p.B, p.sk) ||
+      !make_map(&mv, p.v, bf16, D, p.T, p.H, p.B, p.sv))
     return cudaSuccess;
-  const size_t smemA = 2 * kTile + 1024 + 256;
-  const size_t smemC = kOutSmem;
-  auto kA = gla_tc_state_kernel<T>;
-  auto kC_ = gla_tc_out_kernel<T>;
-  cudaError_t e = cudaFuncSetAttribute(kA, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smemA);
+  auto kA = gla_tc_state_kernel<T, D>;
+  auto kC_ = gla_tc_out_kernel<T, D>;
+  cudaError_t e = cudaFuncSetAttribute(kA, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Gm::STATE_SMEM);
   if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(kC_, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smemC);
+  e = cudaFuncSetAttribute(kC_, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Gm::OUT_SMEM);
   if (e != cudaSuccess) return e;
   *taken = true;
   const dim3 grid(p.nseg, p.H, p.B);
-  kA<<<grid, kThreads, smemA, st>>>(mk, mv, p);
+  kA<<<grid, kThreads, Gm::STATE_SMEM, st>>>(mk, mv, p);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  gla_tc_scan_kernel<<<dim3((p.J * 64 + 255) / 256, p.H, p.B), 256, 0, st>>>(p);
+  gla_tc_scan_kernel<<<dim3((p.J * D + 255) / 256, p.H, p.B), 256, 0, st>>>(p);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  kC_<<<grid, kThreads, smemC, st>>>(mq, mk, mv, p);
+  kC_<<<grid, kThreads, Gm::OUT_SMEM, st>>>(mq, mk, mv, p);
   return cudaGetLastError();
 }
 
 }  // namespace
 
 // Workspace bytes of the tensor-core path (start states + chunk decays).
-size_t gla_tc_workspace_bytes(int64_t B, int64_t H, int64_t T, int64_t J) {
+size_t gla_tc_workspace_bytes(int64_t B, int64_t H, int64_t T, int64_t J, int64_t D) {
   const int64_t nc = (T + kC - 1) / kC;
-  return (size_t)(B * H * nc * (J * 64 + 1)) * sizeof(float) + 256;
+  return (size_t)(B * H * nc * (J * D + 1)) * sizeof(float) + 256;
 }
 
 bool gla_tc_eligible(const GlaParams& p, int dtype) {
   const char* off = getenv("HOFA_GLA_NO_TC");
   if (off != nullptr && off[0] != '\0' && off[0] != '0') return false;
-  return (dtype == HOFA_DTYPE_BF16 || dtype == HOFA_DTYPE_F16) && p.D == 64 && p.R % 8 == 0 && p.R < 64 &&
-         p.log_alpha == nullptr;
+  return (dtype == HOFA_DTYPE_BF16 || dtype == HOFA_DTYPE_F16) && (p.D == 64 || p.D == 128) && p.R % 8 == 0 &&
+         p.R < p.D && p.log_alpha == nullptr;
 }
 
 // p.nseg must hold the chunk count ceil(T / 128), p.ws_state / p.ws_decay the
@@ -460,8 +501,9 @@ bool gla_tc_eligible(const GlaParams& p, int dtype) {
 // be built for these strides (the caller then uses the CUDA-core kernel).
 cudaError_t launch_gla_tc(const GlaParams& p, int dtype, cudaStream_t st, bool* taken) {
   *taken = false;
-  if (dtype == HOFA_DTYPE_BF16) return launch_t<__nv_bfloat16>(p, st, taken);
-  return launch_t<__half>(p, st, taken);
+  if (dtype == HOFA_DTYPE_BF16)
+    return p.D == 64 ? launch_t<__nv_bfloat16, 64>(p, st, taken) : launch_t<__nv_bfloat16, 128>(p, st, taken);
+  return p.D == 64 ? launch_t<__half, 64>(p, st, taken) : launch_t<__half, 128>(p, st, taken);
 }
 
 int gla_tc_chunk() { return kC; }

@@ -58,7 +58,7 @@ def test_gla_segments_and_initial_state(nseg):
     from outlierneuronattention_b200.chunk_gla_inlier import gla_forward
     B, H, T, D, r = 2, 2, 700, 64, 16
     q, k, v, lg, mix, gs = rand_qkv(B, H, T, D, torch.float32, seed=100 + nseg)
-    s0 = torch.randn(B, H, D - r, D) * 0.3
+    s0 = torch.randn(B, H, D - r, D, generator=torch.Generator().manual_seed(61)) * 0.3
     st = torch.empty(B, H, D - r, D, device="cuda")
     Y = gla_forward(q.cuda(), k.cuda(), v.cuda(), lg.cuda(), r, mix_g=mix.cuda(), gla_scale=gs.cuda(),
                     state_out=st, initial_state=s0.cuda(), num_segments=nseg)
@@ -84,13 +84,16 @@ def test_gla_learnable_alpha_strong_decay():
     from outlierneuronattention_b200 import chunk_gla_inlier_fwd
     B, H, T, D, r = 1, 2, 256, 64, 16
     q, k, v, _, mix, gs = rand_qkv(B, H, T, D, torch.float32, seed=55)
-    lg = F.logsigmoid(torch.randn(B, H, T) * 2.0 - 3.0)  # gamma ~ 0.05
-    la = torch.randn(1, H, 1, D - r) * 0.5
+    g = torch.Generator().manual_seed(56)  # inputs independent of the tests that ran before
+    lg = F.logsigmoid(torch.randn(B, H, T, generator=g) * 2.0 - 3.0)  # gamma ~ 0.05
+    la = torch.randn(1, H, 1, D - r, generator=g) * 0.5
     Y, st = chunk_gla_inlier_fwd(q.cuda(), k.cuda(), v.cuda(), lg.cuda(), r, 64, log_alpha=la.cuda(),
                                  mix_g=mix.cuda(), gla_scale=gs.cuda())
     Yr, Sr = chunk_gla_core(q, k, v, lg, r, 64, log_alpha=la, mix_g=mix, gla_scale=gs, eps=1e-5)
     assert torch.isfinite(Y).all()
-    assert maxabs(Y, Yr) <= 1e-4
+    # strong decay keeps the pre-norm output small and RMSNorm scales its fp32
+    # rounding up with it: bound the error relative to the output's size
+    assert maxabs(Y, Yr) <= 1e-4 * max(1.0, Yr.abs().max().item()), (maxabs(Y, Yr), Yr.abs().max().item())
     assert maxabs(st[:, :, :D - r, :D], Sr) <= 1e-5 * max(1.0, Sr.abs().max().item())
 
 
@@ -100,7 +103,7 @@ def test_outlier_attention(dtype, T):
     from outlierneuronattention_b200 import exact_attention_triton
     B, H, D, r = 2, 3, 64, 16
     q, k, v, _, mix, _ = rand_qkv(B, H, T, D, dtype, seed=T + 1, scale=1.0)
-    base = (torch.randn(B, H, T, D) * 0.1).to(dtype)
+    base = (torch.randn(B, H, T, D, generator=torch.Generator().manual_seed(T)) * 0.1).to(dtype)
     out = base.cuda().clone()
     exact_attention_triton(q.cuda(), k.cuda(), v.cuda(), r, 2.0, mix.cuda(), out=out)
     ref = outlier_attention_core(q, k, v, r, 2.0, mix, out=base)
@@ -177,7 +180,7 @@ def test_outlier_tensor_core_path(monkeypatch, dtype, B, H, T, D, r, qoff):
     from outlierneuronattention_b200 import exact_attention_triton
     q, k, v, _, mix, _ = rand_qkv(B, H, T, D, dtype, seed=T + D + r, scale=1.0)
     qs, ms = q[:, :, qoff:], mix[:, :, qoff:]
-    base = (torch.randn(B, H, T - qoff, D) * 0.1).to(dtype)
+    base = (torch.randn(B, H, T - qoff, D, generator=torch.Generator().manual_seed(T + D)) * 0.1).to(dtype)
     ref = outlier_attention_core(qs, k, v, r, math.sqrt(D / r), ms, out=base, q_offset=qoff)
     assert _prefill_status() == 0
     outs = {}
@@ -195,17 +198,19 @@ def test_outlier_tensor_core_path(monkeypatch, dtype, B, H, T, D, r, qoff):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
-@pytest.mark.parametrize("B,H,T,r,fuse,init", [(1, 1, 128, 16, True, False), (2, 3, 1000, 16, True, True),
-                                               (1, 2, 129, 16, False, False), (1, 2, 300, 0, True, False),
-                                               (2, 2, 257, 32, True, True), (1, 1, 64, 8, False, True)])
-def test_gla_tensor_core_path(monkeypatch, dtype, B, H, T, r, fuse, init):
-    """The chunk-parallel tcgen05 GLA (bf16/f16, d_h = 64, scalar decay) and the
-    CUDA-core GLA agree with the oracle on the same inputs, including a seeded
-    initial state; the tensor-core kernels' bounded waits never ran out."""
+@pytest.mark.parametrize("B,H,T,r,fuse,init,D", [(1, 1, 128, 16, True, False, 64), (2, 3, 1000, 16, True, True, 64),
+                                                 (1, 2, 129, 16, False, False, 64), (1, 2, 300, 0, True, False, 64),
+                                                 (2, 2, 257, 32, True, True, 64), (1, 1, 64, 8, False, True, 64),
+                                                 (1, 1, 128, 16, True, False, 128), (2, 2, 300, 32, True, True, 128),
+                                                 (1, 2, 257, 64, False, False, 128), (2, 1, 129, 8, True, True, 128),
+                                                 (1, 1, 200, 0, True, False, 128), (1, 1, 1000, 16, True, True, 128)])
+def test_gla_tensor_core_path(monkeypatch, dtype, B, H, T, r, fuse, init, D):
+    """The chunk-parallel tcgen05 GLA (bf16/f16, d_h = 64 or 128, scalar decay)
+    and the CUDA-core GLA agree with the oracle on the same inputs, including a
+    seeded initial state; the tensor-core kernels' bounded waits never ran out."""
     from outlierneuronattention_b200.chunk_gla_inlier import gla_forward
-    D = 64
     q, k, v, lg, mix, gs = rand_qkv(B, H, T, D, dtype, seed=T + r)
-    s0 = torch.randn(B, H, D - r, D) * 0.3 if init else None
+    s0 = torch.randn(B, H, D - r, D, generator=torch.Generator().manual_seed(T + r)) * 0.3 if init else None
     Yr, Sr = chunk_gla_core(q, k, v, lg, r, 64, mix_g=mix if fuse else None, gla_scale=gs if fuse else None,
                             eps=1e-5, state_init=s0)
     assert _prefill_status() == 0

@@ -119,7 +119,7 @@ def test_sharded_layer_forward_one_rank_matches_layer_forward(dtype, tol):
             if "gate_proj" in name or "mix_proj" in name:
                 prm.normal_(0, 0.02)
     T = 512
-    x = torch.randn(1, T, 256, device="cuda")
+    x = torch.randn(1, T, 256, generator=torch.Generator().manual_seed(122)).cuda()
     with torch.no_grad(), torch.autocast("cuda", dtype=dtype, enabled=dtype != torch.float32):
         ref, _, (st_ref, _) = layer(x, return_state=True)
         out, st = seqpar.sharded_layer_forward(layer, x, T, return_state=True)
