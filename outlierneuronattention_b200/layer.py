@@ -249,6 +249,8 @@ class HybridOutlierFactorizedAttention(nn.Module):
         if state_I is None:
             state_I = (torch.zeros(B, self.num_heads, self.j, self.d_head, device=x.device, dtype=torch.float32),
                        torch.empty(B, self.num_heads, self.j, self.d_head, device=x.device, dtype=torch.float32))
+        if torch.is_tensor(cache_seq_len):
+            return self._step_device_position(Q, K, V, B, N, dtype_in, cache_O, state_I, cache_seq_len)
         if cache_O is not None and cache_seq_len is not None and cache_O[0].shape[2] > cache_seq_len:
             # pre-allocated cache (the serving path): gates, RoPE at row
             # cache_seq_len, the cache append and the decode core in one launch
@@ -283,6 +285,35 @@ class HybridOutlierFactorizedAttention(nn.Module):
                               self.gla_scale.view(self.num_heads, self.d_head), self.r, cache_seq_len + 1,
                               sm_scale, log_alpha=self.log_alpha if self.learnable_alpha else None)
         return self._out(Y, B, N, dtype_in), cache_O_new, (state_out, state_in)
+
+    def _step_device_position(self, Q, K, V, B, N, dtype_in, cache_O, state_I, cache_seq_len):
+        """Decode step whose position lives on the device: ``cache_seq_len`` is
+        an int32 CUDA scalar holding the rows already in the pre-allocated
+        ``cache_O``, so a decode loop can be captured once in a CUDA graph and
+        replayed with the position advanced on the device (no host value, no
+        synchronisation).  The RoPE tables are sized to the cache's capacity;
+        a position outside the cache is clamped and flagged in the decode
+        workspace's status word."""
+        if cache_O is None:
+            raise ValueError("a device-side cache_seq_len needs a pre-allocated cache_O")
+        if cache_seq_len.dtype != torch.int32 or cache_seq_len.numel() != 1 or not cache_seq_len.is_cuda:
+            raise ValueError("a device-side cache_seq_len is a one-element int32 CUDA tensor")
+        state_in, state_out = state_I
+        assert state_in.dtype == torch.float32, f"Expected state_in to be float32, got {state_in.dtype}"
+        assert state_in.is_contiguous(), "Expected state_in to be contiguous"
+        L = cache_O[0].shape[2]
+        cos, sin = self._rope_tables(L)
+        buf = getattr(self, "_seq_len_dev", None)
+        if buf is None or buf.device != cache_seq_len.device:
+            buf = torch.empty(1, dtype=torch.int32, device=cache_seq_len.device)
+            self._seq_len_dev = buf
+        torch.add(cache_seq_len.view(1), 1, out=buf)  # rows attended: the cache's plus the new one
+        Y, _, _ = fused_hofa_decode_step(
+            Q, K, V, cache_O[0], cache_O[1], state_in, state_out,
+            self.gla_scale.view(self.num_heads, self.d_head), self.r, L, (self.d_head / self.r) ** 0.5,
+            cos=cos, sin=sin, seq_len_dev=buf,
+            log_alpha=self.log_alpha if self.learnable_alpha else None, **self._gate_kwargs())
+        return self._out(Y, B, N, dtype_in), cache_O, (state_out, state_in)
 
     def _append(self, cache_O, K_new, V_new, cache_seq_len):
         if cache_O is None:

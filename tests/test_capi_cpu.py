@@ -143,3 +143,23 @@ def test_choose_split_and_workspace_size():
     assert L.hofa_decode_choose_split(1, 1, 10, 148) == 1
     # workspace: status + tickets + (4 + 2D) floats per (b,h,split)
     assert L.hofa_decode_workspace_size(1, 1, 64, 1) == 256 + 256 + (4 + 128) * 4
+
+
+def test_decode_step_validation():
+    """hofa_decode_step_fwd refuses mismatched tensors before any device work."""
+    B, H, D, R, L = 1, 2, 64, 16, 32
+    dvals = decode_vals(B=B, H=H, D=D, R=R, L=L)
+
+    def prep_vals(q_ptr=FAKE, mix_out=True, cache_k=True):
+        return _capi.flat(tv([B, H, 1, D], ptr=q_ptr), tv([B, H, 1, D]), tv([B, H, 1, D]), tv([H, 2 * D], 0),
+                          tv([H], 0), tv([H, 2 * D], 0), tv([H], 0), _capi.ABSENT, tv([4096, R], 0), tv([4096, R], 0),
+                          tv([B, H, 1], 0), tv([B, H, 1]) if mix_out else _capi.ABSENT,
+                          tv([B, H, L, R]) if cache_k else _capi.ABSENT, tv([B, H, L, D]), R, 0, 0, 1)
+
+    fn = _capi.lib().hofa_decode_step_fwd
+    cases = [(prep_vals(q_ptr=3 * FAKE), "same q, k, v"), (prep_vals(mix_out=False), "mix_out is required"),
+             (prep_vals(cache_k=False), "append to the decode's caches")]
+    for pv, pattern in cases:
+        st = fn(_capi.FORMATS[_capi.DecodeArgs].pack(*dvals), _capi.FORMATS[_capi.PrepArgs].pack(*pv), 0)
+        assert st == 1
+        assert re.search(pattern, _capi.lib().hofa_last_error().decode())

@@ -164,3 +164,65 @@ def test_no_rope_layer_prefill_export_and_preallocated_decode_fp32():
             assert err(ys, oy) <= 1e-4
     assert err(cache[0], oc[0]) <= 1e-4 and err(cache[1], oc[1]) <= 1e-4
     assert err(state[0], ost) <= 1e-4 * max(1.0, ost.abs().max().item())
+
+
+def test_device_position_decode_loop_in_cuda_graph():
+    """forward_step with cache_seq_len as an int32 CUDA scalar: two decode steps
+    (state ping-pong, position advanced on the device) captured once and
+    replayed eight times give the eager host-position loop's outputs."""
+    from outlierneuronattention_b200 import HybridOutlierFactorizedAttention, ModelConfig
+    torch.manual_seed(2)
+    cfg = ModelConfig(d_model=256, num_heads=4, num_layers=1, r=16, chunk_size=64)
+    m = HybridOutlierFactorizedAttention(cfg)
+    gen = torch.Generator().manual_seed(2)
+    with torch.no_grad():
+        m.gate_proj.weight.copy_(torch.randn(m.gate_proj.weight.shape, generator=gen) * 0.02)
+        m.mix_proj.weight.copy_(torch.randn(m.mix_proj.weight.shape, generator=gen) * 0.02)
+    m = m.cuda().eval()
+    T0, NS, CAP = 37, 16, 64
+    x = torch.randn(2, T0 + NS, 256, generator=gen).cuda()
+
+    def prefill():
+        _, (k, v), (s, _) = m(x[:, :T0], return_state=True)
+        K = torch.zeros(2, 4, CAP, 16, device="cuda")
+        V = torch.zeros(2, 4, CAP, 64, device="cuda")
+        K[:, :, :T0], V[:, :, :T0] = k, v
+        return (K, V), s.clone(), torch.empty_like(s)
+
+    with torch.no_grad():
+        cache, sa, sb = prefill()
+        ref, state = [], (sa, sb)
+        for t in range(T0, T0 + NS):
+            y, cache, state = m.forward_step(x[:, t:t + 1], cache, state, cache_seq_len=t)
+            ref.append(y.clone())
+        ref_cache, ref_state = cache, state[0]
+
+        cache, sa, sb = prefill()
+        pos = torch.tensor([T0], dtype=torch.int32, device="cuda")
+        xb = [x[:, T0:T0 + 1].clone(), x[:, T0 + 1:T0 + 2].clone()]
+        s = torch.cuda.Stream()
+        with torch.cuda.stream(s):
+            # warm-up on scratch copies (creates the layer's cached buffers), then capture
+            wc = (cache[0].clone(), cache[1].clone())
+            wp = pos.clone()
+            m.forward_step(xb[0], wc, (sa.clone(), sb.clone()), cache_seq_len=wp)
+            s.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                y0, _, _ = m.forward_step(xb[0], cache, (sa, sb), cache_seq_len=pos)
+                pos.add_(1)
+                y1, _, _ = m.forward_step(xb[1], cache, (sb, sa), cache_seq_len=pos)
+                pos.add_(1)
+            out = []
+            for i in range(NS // 2):
+                xb[0].copy_(x[:, T0 + 2 * i:T0 + 2 * i + 1])
+                xb[1].copy_(x[:, T0 + 2 * i + 1:T0 + 2 * i + 2])
+                g.replay()
+                out += [y0.clone(), y1.clone()]
+            s.synchronize()
+        del g
+    for a, b in zip(out, ref):
+        assert err(a, b) <= 1e-4
+    assert int(pos.item()) == T0 + NS
+    assert err(cache[0], ref_cache[0]) <= 1e-5 and err(cache[1], ref_cache[1]) <= 1e-5
+    assert err(sa, ref_state) <= 1e-4 * max(1.0, ref_state.abs().max().item())
