@@ -24,7 +24,9 @@
 // The running max is raised only when a row's max grows by more than 2^64
 // (bf16; 2^8 for f16, whose largest value is 65504) -- then the row of O is
 // rescaled in TMEM; otherwise P is formed against the stale max, which
-// changes nothing but the common factor removed at the end.
+// changes nothing but the common factor removed at the end.  With bf16 a tile
+// after the first computes its exponentials against the running max at once
+// and only takes the row max when a row's sum shows a growth past 2^64.
 //
 // Exponentials: a share of the exp2 evaluations of each full (unmasked) tile
 // runs on the FMA pipe as a cubic polynomial (exp2_pair_poly), the rest on the
@@ -158,6 +160,7 @@ outlier_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
   constexpr uint32_t IDESC_S = sm100::idesc_f16(BF16, false, false, kRows, kKeys);
   constexpr uint32_t IDESC_O = sm100::idesc_f16(BF16, false, true, kRows, D);
   constexpr uint32_t NCOLS = tmem_cols<D>();
+  constexpr bool SKIPMAX = BF16;  // f16 P (kRaise 8) keeps the row max on every tile
   // lazy rescale threshold (log2 units): P values stay below 2^kRaise.  bf16
   // P and the fp32 row sums and O share fp32's exponent range, so 2^64 (and
   // a row sum below 2^64 times the key count) is far from overflow; f16 P
@@ -300,40 +303,51 @@ outlier_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
         for (int i = 0; i < 32; ++i)
           if (k0 + i > limit) r[i] = __float_as_uint(-INFINITY);
       }
-      float mx[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-        mx[i] = sm100::fmax3(__uint_as_float(r[8 * i]), __uint_as_float(r[8 * i + 1]), __uint_as_float(r[8 * i + 2]));
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        mx[i] = sm100::fmax3(mx[i], __uint_as_float(r[8 * i + 3]), __uint_as_float(r[8 * i + 4]));
-        mx[i] = sm100::fmax3(mx[i], __uint_as_float(r[8 * i + 5]), __uint_as_float(r[8 * i + 6]));
-        mx[i] = fmaxf(mx[i], __uint_as_float(r[8 * i + 7]));
-      }
-      const float mts = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * scale;
-      const bool raise = mts > m_used + kRaise;
-      const float factor = raise ? sm100::ex2_approx(m_used - mts) : 1.f;  // 0 on the first tile
-      if (raise) m_used = mts;
-      // TMEM loads/stores are warp-collective: the whole warp rescales its rows
-      // of O when any of them raised its max (the others multiply by 1), once
-      // O += P_{t-1} V_{t-1} is done (O += P_{t-2} V_{t-2} completed before S_t
-      // was issued, so the parity wait sees the right phase)
-      if (t > 0 && __any_sync(0xffffffffu, raise)) {
-        wait(bar_o, (t - 1) & 1);
-        sm100::tc_fence_after();
-#pragma unroll
-        for (int c = 0; c < D; c += 16) {
-          uint32_t o[16];
-          sm100::tmem_ld16(tO + lane_off + c, o);
-          sm100::tc_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
-          sm100::tmem_st16(tO + lane_off + c, o);
-        }
-      }
       uint32_t pk[16];
-      const float ls = masked ? row_exp<BF16, 0>(r, scale, m_used, pk)   // exact zeros where masked
-                              : row_exp<BF16, EMU>(r, scale, m_used, pk);
+      float ls = 0.f, factor = 1.f;
+      bool slow = true;
+      if (SKIPMAX && !masked && t > 0) {
+        // exponentials against the running max straight away; a row whose max
+        // grew by more than 2^kRaise shows in its sum (>= 2^kRaise, or inf),
+        // and only then does the warp redo the tile with the row max
+        ls = row_exp<BF16, 0>(r, scale, m_used, pk);
+        slow = __any_sync(0xffffffffu, !(ls < 1.8446744e19f));  // 2^64
+      }
+      if (slow) {
+        float mx[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          mx[i] = sm100::fmax3(__uint_as_float(r[8 * i]), __uint_as_float(r[8 * i + 1]), __uint_as_float(r[8 * i + 2]));
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          mx[i] = sm100::fmax3(mx[i], __uint_as_float(r[8 * i + 3]), __uint_as_float(r[8 * i + 4]));
+          mx[i] = sm100::fmax3(mx[i], __uint_as_float(r[8 * i + 5]), __uint_as_float(r[8 * i + 6]));
+          mx[i] = fmaxf(mx[i], __uint_as_float(r[8 * i + 7]));
+        }
+        const float mts = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * scale;
+        const bool raise = mts > m_used + kRaise;
+        factor = raise ? sm100::ex2_approx(m_used - mts) : 1.f;  // 0 on the first tile
+        if (raise) m_used = mts;
+        // TMEM loads/stores are warp-collective: the whole warp rescales its rows
+        // of O when any of them raised its max (the others multiply by 1), once
+        // O += P_{t-1} V_{t-1} is done (O += P_{t-2} V_{t-2} completed before S_t
+        // was issued, so the parity wait sees the right phase)
+        if (t > 0 && __any_sync(0xffffffffu, raise)) {
+          wait(bar_o, (t - 1) & 1);
+          sm100::tc_fence_after();
+#pragma unroll
+          for (int c = 0; c < D; c += 16) {
+            uint32_t o[16];
+            sm100::tmem_ld16(tO + lane_off + c, o);
+            sm100::tc_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
+            sm100::tmem_st16(tO + lane_off + c, o);
+          }
+        }
+        ls = masked ? row_exp<BF16, 0>(r, scale, m_used, pk)   // exact zeros where masked
+                    : row_exp<BF16, (EMU > 8 ? 0 : EMU)>(r, scale, m_used, pk);
+      }
       l_sum = l_sum * factor + ls;
       sm100::tmem_st16(tS, pk);   // P_t over the first 16 columns of this row's S_t
       sm100::tc_wait_st();
