@@ -230,3 +230,27 @@ def test_gla_tensor_core_path(monkeypatch, dtype, B, H, T, r, fuse, init, D):
         assert (st.double().cpu() - Sr).abs().max().item() <= 2e-2 * max(1.0, Sr.abs().max().item()), path
     monkeypatch.delenv("HOFA_GLA_NO_TC")
     assert _prefill_status() == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_outlier_tensor_core_growing_logits(dtype):
+    """Scores that grow along the keys (about 0.7 log2 units per key, 90 over
+    128 keys): later tiles raise the running max far past the lazy-rescale
+    threshold, so rows of O are rescaled in TMEM mid-sequence."""
+    from outlierneuronattention_b200.exact_attention import exact_attention_triton
+    B, H, T, D, r = 1, 2, 320, 64, 16
+    g = torch.Generator().manual_seed(77)
+    q = torch.zeros(B, H, T, D)
+    q[..., :r] = 1.0 + 0.05 * torch.randn(B, H, T, r, generator=g)
+    k = torch.zeros(B, H, T, D)
+    k[..., :r] = (torch.arange(T, dtype=torch.float32) / 64).view(1, 1, T, 1) * (1 + 0.05 * torch.randn(B, H, T, r, generator=g))
+    v = torch.randn(B, H, T, D, generator=g)
+    mix = torch.sigmoid(torch.randn(B, H, T, generator=g))
+    q, k, v, mix = (t.to(dtype) for t in (q, k, v, mix))
+    out = exact_attention_triton(q.cuda(), k.cuda(), v.cuda(), r, 2.0, mix.cuda(),
+                                 out=torch.zeros(B, H, T, D, dtype=dtype, device="cuda"))
+    torch.cuda.synchronize()
+    ref = outlier_attention_core(q, k, v, r, 2.0, mix)
+    assert torch.isfinite(out.float()).all()
+    assert maxabs(out, ref) <= 2e-2
+    assert _prefill_status() == 0
