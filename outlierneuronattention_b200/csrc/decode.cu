@@ -487,14 +487,6 @@ decode_bulk_kernel(const DecodeParams p) {
   T* sK = reinterpret_cast<T*>(ring);
   T* sV = reinterpret_cast<T*>(ring + (size_t)NST * kBulkChunk * R * sizeof(T));
 
-  const int seq_len = resolve_seq_len(p, s, tid);
-  const int stream_len = PREP ? seq_len - 1 : seq_len;  // PREP: the newest row comes from registers
-  int tps = (stream_len + p.split_k - 1) / p.split_k;
-  tps = (tps + kBulkChunk - 1) & ~(kBulkChunk - 1);
-  const int t_begin = s * tps;
-  const int t_end = min(stream_len, t_begin + tps);
-  const int nchunks = t_end > t_begin ? (t_end - t_begin + kBulkChunk - 1) / kBulkChunk : 0;
-
   // Slot st of the ring holds chunks st, st+NST, ... and is consumed by warp
   // st % NW only when NST % NW == 0; otherwise a warp could wait on a phase
   // two completions ahead (mbarrier parity waits alias).  The host guarantees
@@ -503,6 +495,14 @@ decode_bulk_kernel(const DecodeParams p) {
     if (tid == 0) atomicOr(p.ws_status, 16);
     return;
   }
+  // this split's token range [t_begin, t_end) of the cache stream
+  auto split_range = [&](int seq_len, int& t_begin, int& t_end) {
+    const int stream_len = PREP ? seq_len - 1 : seq_len;  // PREP: the newest row comes from registers
+    int tps = (stream_len + p.split_k - 1) / p.split_k;
+    tps = (tps + kBulkChunk - 1) & ~(kBulkChunk - 1);
+    t_begin = s * tps;
+    t_end = min(stream_len, t_begin + tps);
+  };
   if (tid == 0) {
     for (int i = 0; i < NST; ++i) {
       sm100::mbar_init(&full_bar[i], 1);
@@ -513,11 +513,29 @@ decode_bulk_kernel(const DecodeParams p) {
     sm100::fence_mbar_init();
   }
   // Programmatic dependent launch: this grid may have been scheduled while the
-  // previous kernel of the stream was still running; wait for it to complete
-  // (and its writes to be visible) before touching global memory, then let
-  // the next kernel start scheduling.
+  // previous kernel of the stream was still running.  Before waiting for it,
+  // the producer only asks L2 to prefetch this split's cache rows (a hint that
+  // reads nothing into the SM: every load below, made after the wait, still
+  // sees all of that kernel's writes), so the rows stream in while the
+  // previous kernel finishes; with a device-side seq_len the range is not
+  // known yet and nothing is prefetched.  Then wait for the previous kernel
+  // (its writes become visible) and let the next kernel start scheduling.
+  if (warp == NW && lane == 0 && p.seq_len_dev == nullptr && p.R > 0 && !p.no_l2_prefetch) {
+    int tb, te;
+    split_range(p.seq_len, tb, te);
+    if (te > tb) {
+      const char* kg = reinterpret_cast<const char*>(p.cache_k) + (b * p.sck[0] + h * p.sck[1] + (int64_t)tb * R) * sizeof(T);
+      const char* vg = reinterpret_cast<const char*>(p.cache_v) + (b * p.scv[0] + h * p.scv[1] + (int64_t)tb * D) * sizeof(T);
+      sm100::prefetch_l2(kg, (uint32_t)((te - tb) * R * sizeof(T)));
+      sm100::prefetch_l2(vg, (uint32_t)((te - tb) * D * sizeof(T)));
+    }
+  }
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const int seq_len = resolve_seq_len(p, s, tid);
+  int t_begin, t_end;
+  split_range(seq_len, t_begin, t_end);
+  const int nchunks = t_end > t_begin ? (t_end - t_begin + kBulkChunk - 1) / kBulkChunk : 0;
   const EpiloguePrefetch ep = prefetch_epilogue<D>(p, b, h, tid);
   __syncthreads();  // barriers initialised; the producer starts streaming at once
   // cluster combine: arrive now, wait just before the first remote access

@@ -32,6 +32,7 @@ struct DecodeParams {
   int* ws_status;
   int stages;                 // bulk ring depth (64-token chunks)
   int consumer_warps;         // bulk kernel consumer warps: 4 or 8
+  bool no_l2_prefetch;        // bulk kernel: skip the L2 prefetch of the cache rows before the grid dependency
   // hofa_decode_step_fwd (bulk kernel): the new token's gates, RoPE and cache
   // row are computed in the same launch.  q, k, v are then un-rotated; the
   // cache is streamed over rows [0, seq_len - 1) and the new token (row

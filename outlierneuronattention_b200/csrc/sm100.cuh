@@ -155,6 +155,12 @@ __device__ __forceinline__ void tma_load_4d(void* dst, const void* tmap, int x, 
       "l"(tmap), "r"(x), "r"(y), "r"(z), "r"(w), "r"(smem_u32(bar))
       : "memory");
 }
+// Prefetch [src, src + bytes) into L2 (16-byte aligned, bytes % 16 == 0).  A
+// hint only: it reads nothing into the SM, and later loads still see every
+// write made before them (L2 is the point of coherence of global memory).
+__device__ __forceinline__ void prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
