@@ -299,13 +299,25 @@ def run_ours(args):
     ck0, cv0, st0 = sets[0]
     e2e_steps = max(args.steps, 50)
 
+    # The C ABI call a serving loop makes: hofa_decode_args packed once per
+    # state direction (the GLA state ping-pongs between two buffers) and
+    # hofa_decode_fwd called with it every step.
+    from outlierneuronattention_b200.hofa_decode import decode_args
+    ye = torch.empty(B, H, 1, D, dtype=q.dtype, device=dev)
+    packed = [_capi.FORMATS[_capi.DecodeArgs].pack(*decode_args(dq, dk, dv, ck0, cv0, s_in, s_out, dlg, dmix, nw, R, L,
+                                                                 2.0, ye, split or None))
+              for s_in, s_out in ((st0, outs[0]), (outs[0], st0))]
+    decode_fwd = _capi.lib().hofa_decode_fwd
+    cur = torch.cuda.current_stream(dev)
+    cur_handle = cur.cuda_stream
+
     def e2e_step(i):
         dstage.copy_(hstage, non_blocking=True)
-        s_in, s_out = (st0, outs[0]) if i % 2 == 0 else (outs[0], st0)
-        yy = fused_hofa_decode(dq, dk, dv, ck0, cv0, s_in, s_out, dlg, dmix, nw, R, L, 2.0,
-                               split_k=split or None)
-        yh.copy_(yy, non_blocking=True)
-        torch.cuda.current_stream(dev).synchronize()
+        status = decode_fwd(packed[i % 2], cur_handle)
+        if status != 0:
+            raise RuntimeError(_capi.lib().hofa_last_error().decode())
+        yh.copy_(ye, non_blocking=True)
+        cur.synchronize()
         return float(yh[0, 0, 0, 0])
 
     for i in range(5):
@@ -338,7 +350,9 @@ def run_ours(args):
                       "parallelism": f"batch-sharded decode over {world} GPU(s), no collective"},
            "roofline": roofline,
            "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
-                   "d2h_bytes_per_step": d2h, "api": "outlierneuronattention_b200.fused_hofa_decode"},
+                   "d2h_bytes_per_step": d2h,
+                   "api": "C ABI hofa_decode_fwd with pre-packed hofa_decode_args (ctypes), one staged H2D copy, "
+                          "Y read back to the host every step"},
            "gpu_launches": args.steps, "clocks": clocks}
     if not args.no_prefill:
         out["prefill"] = measure_prefill(dev)
