@@ -4,33 +4,36 @@
 // 45-161): out += mix * softmax(sm_scale * q_r k_r^T, causal) v with r = R
 // query/key channels and D value channels.  One CTA owns 128 query rows of
 // one (b,h): warps 0-3 run the softmax (thread i owns row i, which is TMEM
-// lane i) and warp 4 issues every TMA copy and MMA.  Keys come in tiles of 32.
+// lane i) and warp 4 issues every TMA copy and MMA.  Keys come in tiles of 64.
 //
-//   TMEM: two S/P buffers of 32 fp32 columns and O (D fp32 columns); 128
+//   TMEM: one S/P buffer of 64 fp32 columns and O (D fp32 columns); 128
 //   columns in all at head dim 64, so four CTAs share an SM.
 //   Shared memory: the Q tile and 4-stage K and V rings filled by TMA (4-D
 //   tiled maps over [B,H,T,channels], no multicast).
 //
-//   Issuer, step t:  S_t = Q K_t^T into buffer t%2 (once O += P_{t-2} V_{t-2},
-//                    the buffer's last reader, is done), then
-//                    O += P_{t-1} V_{t-1} once P_{t-1} is complete
-//                    (tcgen05.mma kind::f16; P from TMEM, V from shared memory)
-//   Softmax, tile t: load the row of S_t from TMEM, row max, P = exp2(S*c - m)
-//                    as 16-bit pairs written back over the first 16 columns of
-//                    the same buffer, arrive on the buffer's P barrier.
-//   S_{t+1} is computed while the softmax of tile t runs, and the softmax
-//   never waits for a P V product except to rescale O.
+//   Issuer, step t:  once every softmax warp wrote P_{t-1}:
+//                    O += P_{t-1} V_{t-1} (P from TMEM, V from shared memory),
+//                    then S_t = Q K_t^T into the same buffer and one commit.
+//                    MMAs issued by one thread run in issue order, so S_t
+//                    overwrites P_{t-1} only after the P V product read it,
+//                    and the commit's arrival means O is complete as well.
+//   Softmax, tile t: two 32-column halves: load S from TMEM, P = exp2(S*c - m)
+//                    as 16-bit pairs written back over the columns already
+//                    consumed (P of the tile ends in columns [0, 32)), arrive.
+//   While a CTA's softmax waits for its next S, the warps of the other CTAs
+//   on the SM keep the exponential unit busy.
 //
 // The running max is raised only when a row's max grows by more than 2^64
-// (bf16; 2^8 for f16, whose largest value is 65504) -- then the row of O is
-// rescaled in TMEM; otherwise P is formed against the stale max, which
-// changes nothing but the common factor removed at the end.  With bf16 a tile
-// after the first computes its exponentials against the running max at once
-// and only takes the row max when a row's sum shows a growth past 2^64.
+// (bf16; 2^8 for f16, whose largest value is 65504) -- then the row of O (and
+// the tile's first half of P, when the second half raised it) is rescaled in
+// TMEM; otherwise P is formed against the stale max, which changes nothing
+// but the common factor removed at the end.  With bf16 a half-tile computes
+// its exponentials against the running max at once and only takes the row max
+// when a row's sum shows a growth past 2^64.
 //
-// Exponentials: a share of the exp2 evaluations of each full (unmasked) tile
-// runs on the FMA pipe as a cubic polynomial (exp2_pair_poly), the rest on the
-// MUFU unit, so that neither unit alone bounds the softmax.
+// Exponentials: a share of the exp2 evaluations of each full (unmasked) half
+// can run on the FMA pipe as a cubic polynomial (exp2_pair_poly), the rest on
+// the MUFU unit (HOFA_OUTLIER_EMU; MUFU only by default).
 //
 // Every mbarrier wait is bounded; on a timeout the CTA records an error in
 // g_outlier_tc_status, skips the rest of its work, frees its TMEM and exits.
@@ -50,15 +53,16 @@ __device__ int g_outlier_tc_status;
 namespace {
 
 constexpr int kRows = 128;         // query rows per CTA (TMEM lanes)
-constexpr int kKeys = 32;          // keys per tile
+constexpr int kKeys = 64;          // keys per tile
+constexpr int kHalf = 32;          // the softmax takes a tile in two halves of 32 columns
 constexpr int kSoftmaxWarps = 4;
 constexpr int kThreads = 32 * (kSoftmaxWarps + 1);
 constexpr int kStages = 4;         // K and V ring depth
-constexpr int kEmuDefault = 0;     // of every 8 exp2 pairs of a full tile, this many run on the FMA pipe
+constexpr int kEmuDefault = 0;     // of every 8 exp2 pairs of a full half-tile, this many run on the FMA pipe
 
-// TMEM columns: S/P buffers in [0, 2*kKeys), O in [2*kKeys, 2*kKeys + D), rounded up to a power of two
+// TMEM columns: the S/P buffer in [0, kKeys), O in [kKeys, kKeys + D), rounded up to a power of two
 template <int D>
-constexpr uint32_t tmem_cols() { return 2 * kKeys + D <= 128 ? 128 : 256; }
+constexpr uint32_t tmem_cols() { return kKeys + D <= 128 ? 128 : 256; }
 
 constexpr uint32_t round1k(uint32_t b) { return (b + 1023u) & ~1023u; }
 
@@ -176,10 +180,9 @@ outlier_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
   uint64_t* bar_q = bars + 0;
   uint64_t* bar_k = bars + 1;                 // [kStages] K_t landed
   uint64_t* bar_v = bar_k + kStages;          // [kStages] V_t landed
-  uint64_t* bar_s = bar_v + kStages;          // [2] S_t complete in buffer t%2
-  uint64_t* bar_p = bar_s + 2;                // [2] every softmax warp wrote P_t
-  uint64_t* bar_o = bar_p + 2;                // one phase per O += P V
-  uint64_t* bar_fin = bar_o + 1;              // the last O += P V is done
+  uint64_t* bar_s = bar_v + kStages;          // phase t: S_t (and every earlier MMA) complete
+  uint64_t* bar_p = bar_s + 1;                // phase t: every softmax warp wrote P_t
+  uint64_t* bar_fin = bar_p + 1;              // the last O += P V is done
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_fin + 1);
   int* err_flag = reinterpret_cast<int*>(tmem_slot + 1);
 
@@ -197,11 +200,8 @@ outlier_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
       sm100::mbar_init(&bar_k[i], 1);
       sm100::mbar_init(&bar_v[i], 1);
     }
-    for (int i = 0; i < 2; ++i) {
-      sm100::mbar_init(&bar_s[i], 1);
-      sm100::mbar_init(&bar_p[i], kSoftmaxWarps);
-    }
-    sm100::mbar_init(bar_o, 1);
+    sm100::mbar_init(bar_s, 1);
+    sm100::mbar_init(bar_p, kSoftmaxWarps);
     sm100::mbar_init(bar_fin, 1);
     *err_flag = 0;
     sm100::fence_mbar_init();
@@ -214,12 +214,15 @@ outlier_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tO = tmem + 2 * kKeys;
+  const uint32_t tO = tmem + kKeys;
 
   // Bounded waits.  The CTA's error flag is only read when a phase is not
   // already complete; after the first timeout every later wait and every
   // MMA / copy issue is skipped, while the loops keep their trip counts so
-  // that warp-collective TMEM accesses stay convergent.
+  // that warp-collective TMEM accesses stay convergent.  Phase parities never
+  // alias: a waiter of phase t of bar_s or bar_p is itself what holds back
+  // phase t + 1 (the issuer issues S_{t+1} only after P_t; P_{t+1} needs
+  // S_{t+1}).
   volatile int* verr = err_flag;
   auto wait = [&](uint64_t* bar, uint32_t parity) {
     if (sm100::mbar_try_wait(bar, parity)) return;
@@ -243,40 +246,37 @@ outlier_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
           sm100::tma_load_4d(sV0 + s * L::V_SLOT + g * kKeys * 128, &tv, g * 64, t * kKeys, h, b, &bar_v[s]);
       };
       const uint64_t qdesc = sm100::smem_desc(sQ, 16, 8 * L::RB, SWZ);
-      auto issue_pv = [&](int u) {  // O += P_u V_u
-        wait(&bar_p[u & 1], (u >> 1) & 1);
+      const uint64_t kdesc0 = sm100::smem_desc(sK0, 16, 8 * L::RB, SWZ);
+      const uint64_t vdesc0 = sm100::smem_desc(sV0, kKeys * 128, 1024, sm100::kSwizzle128);
+      auto issue_pv = [&](int u) {  // O += P_u V_u, P_u in TMEM columns [0, kKeys / 2)
+        wait(bar_p, u & 1);
         wait(&bar_v[u % kStages], (u / kStages) & 1);
         if (*verr) return;
         sm100::tc_fence_after();
-        const uint64_t vdesc =
-            sm100::smem_desc(sV0 + (u % kStages) * L::V_SLOT, kKeys * 128, 1024, sm100::kSwizzle128);
+        const uint64_t vdesc = vdesc0 + (uint64_t)(((u % kStages) * L::V_SLOT) >> 4);
 #pragma unroll
         for (int kk = 0; kk < kKeys / 16; ++kk)
-          sm100::mma_ts(tO, tmem + (u & 1) * kKeys + kk * 8, vdesc + (uint64_t)(kk * 2048 >> 4), IDESC_O,
-                        u > 0 || kk > 0);
-        sm100::mma_commit(bar_o);
+          sm100::mma_ts(tO, tmem + kk * 8, vdesc + (uint64_t)(kk * 2048 >> 4), IDESC_O, u > 0 || kk > 0);
       };
       sm100::mbar_arrive_expect_tx(bar_q, L::Q_BYTES);
       sm100::tma_load_4d(sQ, &tq, 0, q0, h, b, bar_q);
       for (int t = 0; t < kStages && t < n; ++t) load_kv(t);
       wait(bar_q, 0);
       for (int t = 0; t < n; ++t) {
-        if (t >= 2) {
-          // O += P_{t-2} V_{t-2} done: S/P buffer t%2 and the K/V slot of tile t-2 are free
-          wait(bar_o, (t - 2) & 1);
-          if (t + 2 < n && !*verr) load_kv(t + 2);
-        }
+        if (t >= 1) issue_pv(t - 1);
         const int s = t % kStages;
         wait(&bar_k[s], (t / kStages) & 1);
         if (!*verr) {
           sm100::tc_fence_after();
-          const uint64_t kdesc = sm100::smem_desc(sK0 + s * L::K_SLOT, 16, 8 * L::RB, SWZ);
+          const uint64_t kdesc = kdesc0 + (uint64_t)((s * L::K_SLOT) >> 4);
 #pragma unroll
           for (int ks = 0; ks < R / 16; ++ks)
-            sm100::mma_ss(tmem + (t & 1) * kKeys, qdesc + 2 * ks, kdesc + 2 * ks, IDESC_S, ks > 0);
-          sm100::mma_commit(&bar_s[t & 1]);
+            sm100::mma_ss(tmem, qdesc + 2 * ks, kdesc + 2 * ks, IDESC_S, ks > 0);
+          sm100::mma_commit(bar_s);
         }
-        if (t >= 1) issue_pv(t - 1);
+        // the slot of tile t - 2 is free: O += P_{t-2} V_{t-2} completed before
+        // S_{t-1}, which the softmax consumed before it wrote P_{t-1}
+        if (t >= 2 && t - 2 + kStages < n && !*verr) load_kv(t - 2 + kStages);
       }
       issue_pv(n - 1);
       sm100::mma_commit(bar_fin);
@@ -287,73 +287,93 @@ outlier_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
     const float scale = p.qk_scale_log2;
     const int row = q0 + tid;
     const int limit = min(row + p.q_offset, p.Tk - 1);   // last visible key of this row
+    const int warp_min_limit = min(q0 + warp * 32 + p.q_offset, p.Tk - 1);
     float m_used = -INFINITY, l_sum = 0.f;
     for (int t = 0; t < n; ++t) {
-      const uint32_t tS = tmem + (t & 1) * kKeys + lane_off;
-      wait(&bar_s[t & 1], (t >> 1) & 1);
+      wait(bar_s, t & 1);
       sm100::tc_fence_after();
-      uint32_t r[32];
-      sm100::tmem_ld32(tS, r);
-      sm100::tc_wait_ld();
+#pragma unroll 1
+      for (int hf = 0; hf < 2; ++hf) {
+        uint32_t r[32];
+        sm100::tmem_ld32(tmem + hf * kHalf + lane_off, r);
+        sm100::tc_wait_ld();
 
-      const int k0 = t * kKeys;
-      const bool masked = k0 + kKeys - 1 > q0 + p.q_offset || k0 + kKeys > p.Tk;
-      if (masked) {
+        const int k0 = t * kKeys + hf * kHalf;
+        const bool masked = k0 + kHalf - 1 > warp_min_limit;   // some key of the half is past some row's limit
+        if (masked) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          if (k0 + i > limit) r[i] = __float_as_uint(-INFINITY);
-      }
-      uint32_t pk[16];
-      float ls = 0.f, factor = 1.f;
-      bool slow = true;
-      if (SKIPMAX && !masked && t > 0) {
-        // exponentials against the running max straight away; a row whose max
-        // grew by more than 2^kRaise shows in its sum (>= 2^kRaise, or inf),
-        // and only then does the warp redo the tile with the row max
-        ls = row_exp<BF16, 0>(r, scale, m_used, pk);
-        slow = __any_sync(0xffffffffu, !(ls < 1.8446744e19f));  // 2^64
-      }
-      if (slow) {
-        float mx[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          mx[i] = sm100::fmax3(__uint_as_float(r[8 * i]), __uint_as_float(r[8 * i + 1]), __uint_as_float(r[8 * i + 2]));
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          mx[i] = sm100::fmax3(mx[i], __uint_as_float(r[8 * i + 3]), __uint_as_float(r[8 * i + 4]));
-          mx[i] = sm100::fmax3(mx[i], __uint_as_float(r[8 * i + 5]), __uint_as_float(r[8 * i + 6]));
-          mx[i] = fmaxf(mx[i], __uint_as_float(r[8 * i + 7]));
+          for (int i = 0; i < 32; ++i)
+            if (k0 + i > limit) r[i] = __float_as_uint(-INFINITY);
         }
-        const float mts = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * scale;
-        const bool raise = mts > m_used + kRaise;
-        factor = raise ? sm100::ex2_approx(m_used - mts) : 1.f;  // 0 on the first tile
-        if (raise) m_used = mts;
-        // TMEM loads/stores are warp-collective: the whole warp rescales its rows
-        // of O when any of them raised its max (the others multiply by 1), once
-        // O += P_{t-1} V_{t-1} is done (O += P_{t-2} V_{t-2} completed before S_t
-        // was issued, so the parity wait sees the right phase)
-        if (t > 0 && __any_sync(0xffffffffu, raise)) {
-          wait(bar_o, (t - 1) & 1);
-          sm100::tc_fence_after();
+        uint32_t pk[16];
+        float ls = 0.f, factor = 1.f;
+        bool slow = true;
+        if (SKIPMAX && !masked && (t | hf) != 0) {
+          // exponentials against the running max straight away; a row whose max
+          // grew by more than 2^kRaise shows in its sum (>= 2^kRaise, inf or
+          // NaN), and only then does the warp redo the half with the row max
+          ls = row_exp<BF16, (EMU > 8 ? 0 : EMU)>(r, scale, m_used, pk);
+          slow = __any_sync(0xffffffffu, !(ls < 1.8446744e19f));  // 2^64
+        }
+        if (slow) {
+          float mx[4];
 #pragma unroll
-          for (int c = 0; c < D; c += 16) {
-            uint32_t o[16];
-            sm100::tmem_ld16(tO + lane_off + c, o);
-            sm100::tc_wait_ld();
+          for (int i = 0; i < 4; ++i)
+            mx[i] = sm100::fmax3(__uint_as_float(r[8 * i]), __uint_as_float(r[8 * i + 1]), __uint_as_float(r[8 * i + 2]));
 #pragma unroll
-            for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
-            sm100::tmem_st16(tO + lane_off + c, o);
+          for (int i = 0; i < 4; ++i) {
+            mx[i] = sm100::fmax3(mx[i], __uint_as_float(r[8 * i + 3]), __uint_as_float(r[8 * i + 4]));
+            mx[i] = sm100::fmax3(mx[i], __uint_as_float(r[8 * i + 5]), __uint_as_float(r[8 * i + 6]));
+            mx[i] = fmaxf(mx[i], __uint_as_float(r[8 * i + 7]));
           }
+          const float mts = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * scale;
+          const bool raise = mts > m_used + kRaise;
+          factor = raise ? sm100::ex2_approx(m_used - mts) : 1.f;  // 0 while m_used is -inf
+          if (raise) m_used = mts;
+          // TMEM loads/stores are warp-collective: the whole warp rescales its
+          // rows when any of them raised its max (the others multiply by 1).
+          // O is quiescent here: S_t's commit arrived after O += P_{t-1} V_{t-1}
+          // completed, and O += P_t V_t waits for this warp's arrival.
+          if (__any_sync(0xffffffffu, raise)) {
+            if (t > 0) {
+#pragma unroll
+              for (int c = 0; c < D; c += 16) {
+                uint32_t o[16];
+                sm100::tmem_ld16(tO + lane_off + c, o);
+                sm100::tc_wait_ld();
+#pragma unroll
+                for (int i = 0; i < 16; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * factor);
+                sm100::tmem_st16(tO + lane_off + c, o);
+              }
+            }
+            if (hf == 1) {
+              // the first half's P (16-bit pairs in columns [0, 16)) was formed
+              // against the old max
+              uint32_t o[16];
+              sm100::tc_wait_st();
+              sm100::tmem_ld16(tmem + lane_off, o);
+              sm100::tc_wait_ld();
+#pragma unroll
+              for (int i = 0; i < 16; ++i) {
+                float a, bb;
+                if (BF16) bf16x2_to_f(o[i], a, bb); else f16x2_to_f(o[i], a, bb);
+                o[i] = pack2(a * factor, bb * factor, BF16);
+              }
+              sm100::tmem_st16(tmem + lane_off, o);
+            }
+          }
+          ls = masked ? row_exp<BF16, 0>(r, scale, m_used, pk)   // exact zeros where masked
+                      : row_exp<BF16, (EMU > 8 ? 0 : EMU)>(r, scale, m_used, pk);
         }
-        ls = masked ? row_exp<BF16, 0>(r, scale, m_used, pk)   // exact zeros where masked
-                    : row_exp<BF16, (EMU > 8 ? 0 : EMU)>(r, scale, m_used, pk);
+        l_sum = l_sum * factor + ls;
+        // P of this half as 16-bit pairs over columns [16 hf, 16 hf + 16), which
+        // the first half's load already consumed
+        sm100::tmem_st16(tmem + hf * 16 + lane_off, pk);
       }
-      l_sum = l_sum * factor + ls;
-      sm100::tmem_st16(tS, pk);   // P_t over the first 16 columns of this row's S_t
       sm100::tc_wait_st();
       sm100::tc_fence_before();
       __syncwarp();
-      if (lane == 0) sm100::mbar_arrive(&bar_p[t & 1]);
+      if (lane == 0) sm100::mbar_arrive(bar_p);
     }
     wait(bar_fin, 0);
     sm100::tc_fence_after();
