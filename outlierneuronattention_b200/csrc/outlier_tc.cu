@@ -188,8 +188,12 @@ outlier_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int nqb = (p.Tq + kRows - 1) / kRows;
-  const int qb = nqb - 1 - (int)blockIdx.x;     // long causal rows first
-  const int h = blockIdx.y, b = blockIdx.z;
+  // one block per (row block, head, batch), numbered so that the row blocks
+  // with the most keys (the last ones) of every head launch first: the CTAs
+  // that finish last are the short ones, which keeps the grid's tail short
+  const int heads = p.H * p.B;
+  const int qb = nqb - 1 - (int)(blockIdx.x / heads);
+  const int h = (int)(blockIdx.x % heads) % p.H, b = (int)(blockIdx.x % heads) / p.H;
   const int q0 = qb * kRows;
   const int last_key = min(p.Tk - 1, q0 + kRows - 1 + p.q_offset);
   const int n = last_key / kKeys + 1;
@@ -508,7 +512,7 @@ cudaError_t launch_dr(const OutlierParams& p, cudaStream_t st, bool* taken) {
   if (!make_map(&mq, p.q, bf16, R, p.Tq, p.H, p.B, sq, R, kRows, qk_swz)) return cudaSuccess;
   if (!make_map(&mk, p.k, bf16, R, p.Tk, p.H, p.B, sk, R, kKeys, qk_swz)) return cudaSuccess;
   if (!make_map(&mv, p.v, bf16, D, p.Tk, p.H, p.B, sv, 64, kKeys, CU_TENSOR_MAP_SWIZZLE_128B)) return cudaSuccess;
-  dim3 grid((p.Tq + kRows - 1) / kRows, p.H, p.B);
+  dim3 grid((unsigned)((p.Tq + kRows - 1) / kRows) * p.H * p.B);
   // HOFA_OUTLIER_EMU (0, 2, 3) overrides how many of every 8 exp2 pairs of a
   // full tile run as the FMA-pipe polynomial (bf16, head dim 64, r = 16)
   if constexpr (std::is_same<T, __nv_bfloat16>::value && D == 64 && R == 16) {
