@@ -253,8 +253,9 @@ outlier_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
       const uint64_t kdesc0 = sm100::smem_desc(sK0, 16, 8 * L::RB, SWZ);
       const uint64_t vdesc0 = sm100::smem_desc(sV0, kKeys * 128, 1024, sm100::kSwizzle128);
       auto issue_pv = [&](int u) {  // O += P_u V_u, P_u in TMEM columns [0, kKeys / 2)
-        wait(bar_p, u & 1);
+        // V_u landed long before P_u: only the MMAs follow P_u's arrival
         wait(&bar_v[u % kStages], (u / kStages) & 1);
+        wait(bar_p, u & 1);
         if (*verr) return;
         sm100::tc_fence_after();
         const uint64_t vdesc = vdesc0 + (uint64_t)(((u % kStages) * L::V_SLOT) >> 4);
@@ -267,9 +268,9 @@ outlier_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
       for (int t = 0; t < kStages && t < n; ++t) load_kv(t);
       wait(bar_q, 0);
       for (int t = 0; t < n; ++t) {
-        if (t >= 1) issue_pv(t - 1);
         const int s = t % kStages;
         wait(&bar_k[s], (t / kStages) & 1);
+        if (t >= 1) issue_pv(t - 1);
         if (!*verr) {
           sm100::tc_fence_after();
           const uint64_t kdesc = kdesc0 + (uint64_t)((s * L::K_SLOT) >> 4);
