@@ -194,24 +194,30 @@ __device__ __forceinline__ void finish(const DecodeParams& p, int s, int b, int 
   if (p.split_k == 1) {
     fin_acc = part_acc; fin_l = cta_l; fin_y = part_y;
   } else if constexpr (CLUSTER) {
-    // every split CTA writes its partial into rank 0's sm_all[rank] through
-    // distributed shared memory and arrives (release, cluster scope) on rank
-    // 0's comb_bar, then exits; rank 0 waits once and combines locally.
+    // every other split CTA sends its partial into rank 0's sm_all[rank] with
+    // st.async stores whose bytes complete on rank 0's comb_bar (rank 0
+    // expects (split_k - 1) partials' bytes from kernel start), then exits
+    // without waiting; rank 0 adds its own arrival and waits once.
     cg::cluster_group cluster = cg::this_cluster();
     const uint32_t rank = cluster.block_rank();
-    const bool leader = rank == 0;
-    sm100::cluster_wait();  // every CTA of the cluster has initialised comb_bar
-    float* slot = leader ? &sm_all[0][0] : cluster.map_shared_rank(&sm_all[rank][0], 0);
-    if (tid == 0) { slot[0] = cta_m; slot[1] = cta_l; }
-    if (d < D) { slot[4 + d] = part_acc; slot[4 + D + d] = part_y; }
-    __syncthreads();
-    if (!leader) {
+    sm100::cluster_wait();  // rank 0's comb_bar and its expected bytes are in place
+    if (rank != 0) {
+      const uint32_t rbar = sm100::mapa_shared(comb_bar, 0);
+      const uint32_t rslot = sm100::mapa_shared(&sm_all[rank][0], 0);
       if (tid == 0) {
-        sm100::fence_acq_rel_cluster();
-        sm100::mbar_arrive_remote(sm100::mapa_shared(comb_bar, 0));
+        sm100::st_async_f32(rslot, cta_m, rbar);
+        sm100::st_async_f32(rslot + 4, cta_l, rbar);
+      }
+      if (d < D) {
+        sm100::st_async_f32(rslot + 4 * (4 + d), part_acc, rbar);
+        sm100::st_async_f32(rslot + 4 * (4 + D + d), part_y, rbar);
       }
       return;
     }
+    if (tid == 0) { sm_all[0][0] = cta_m; sm_all[0][1] = cta_l; }
+    if (d < D) { sm_all[0][4 + d] = part_acc; sm_all[0][4 + D + d] = part_y; }
+    if (tid == 0) sm100::mbar_arrive(comb_bar);
+    __syncthreads();
     if (!sm100::mbar_wait_cluster(comb_bar, 0) && tid == 0) atomicOr(p.ws_status, 64);
     float M = -INFINITY;
     for (int q = 0; q < p.split_k; ++q) M = fmaxf(M, sm_all[q][0]);
@@ -479,6 +485,7 @@ decode_bulk_kernel(const DecodeParams p) {
   __shared__ __align__(16) float sm_all[CLUSTER ? kMaxClusterSplit : 1][4 + 2 * D];  // split partials (rank 0's)
   __shared__ __align__(8) uint64_t full_bar[kMaxStages], empty_bar[kMaxStages];
   __shared__ __align__(8) uint64_t comb_bar;
+  __shared__ float sm_ep[D + 1];   // norm_w[h, :] and the blend weight, for the epilogue
   // PREP: [1] log decay, [2] mix, [4..6) new-token score partials, [8..12) / [12..16)
   // gate / mix dot partials, [16, 16+D) v, [16+D, 16+2D) q, [16+2D, 16+3D) k
   __shared__ __align__(16) float sm_pre[PREP ? 16 + 3 * D : 1];
@@ -508,7 +515,10 @@ decode_bulk_kernel(const DecodeParams p) {
       sm100::mbar_init(&full_bar[i], 1);
       sm100::mbar_init(&empty_bar[i], 1);
     }
-    if (CLUSTER) sm100::mbar_init(&comb_bar, p.split_k > 1 ? p.split_k - 1 : 1);
+    if (CLUSTER) {
+      sm100::mbar_init(&comb_bar, 1);   // rank 0's own arrival, plus the peers' partial bytes
+      if (s == 0 && p.split_k > 1) sm100::mbar_expect_tx(&comb_bar, (uint32_t)((p.split_k - 1) * (4 * (2 + 2 * D))));
+    }
     sm_err = 0;
     sm100::fence_mbar_init();
   }
@@ -536,10 +546,10 @@ decode_bulk_kernel(const DecodeParams p) {
   int t_begin, t_end;
   split_range(seq_len, t_begin, t_end);
   const int nchunks = t_end > t_begin ? (t_end - t_begin + kBulkChunk - 1) / kBulkChunk : 0;
-  const EpiloguePrefetch ep = prefetch_epilogue<D>(p, b, h, tid);
   __syncthreads();  // barriers initialised; the producer starts streaming at once
-  // cluster combine: arrive now, wait just before the first remote access
-  if (CLUSTER && p.split_k > 1) sm100::cluster_arrive_relaxed();
+  // cluster combine: arrive now (releasing rank 0's barrier set-up), wait just
+  // before the first remote access
+  if (CLUSTER && p.split_k > 1) sm100::cluster_arrive();
 
   float m_run = -INFINITY, l_run = 0.f;
   float acc[8];
@@ -565,6 +575,10 @@ decode_bulk_kernel(const DecodeParams p) {
     }
   } else if (warp == NW + 1) {
     // ---------------- GLA warp: state rows and y_I, beside the streaming ---
+    // the epilogue's norm_w row and blend weight go to shared memory first,
+    // so that their global round trip is over long before the epilogue
+    for (int d = lane; d < D; d += 32) sm_ep[d] = ld_any(p.norm_w, p.dt_nw, h * p.snw[0] + d * p.snw[1]);
+    if (lane == 0 && !p.fused_prep) sm_ep[D] = ld_any(p.mix_g, p.dt_mg, b * p.smg[0] + h * p.smg[1]);
     if constexpr (PREP) {
       asm volatile("bar.sync 2, %0;" ::"n"(NW * 32 + 32) : "memory");  // the log decay is in sm_pre[1]
       gla_rows<T, D, ALPHA, 32>(p, s, b, h, lane, sm_y, &sm_pre[1]);
@@ -621,6 +635,11 @@ decode_bulk_kernel(const DecodeParams p) {
   }
   __syncthreads();
   if (tid == 0 && sm_err) atomicOr(p.ws_status, 4 * sm_err);
+  EpiloguePrefetch ep;
+  if (tid < D) {
+    ep.nw = sm_ep[tid];
+    ep.mix = sm_ep[D];
+  }
   finish<T, D, CLUSTER, NW, RSUB>(p, s, b, h, tid, lane, warp, NW + 2, sh, sm_acc, sm_y, sm_all, &comb_bar, ep,
                                   PREP ? sm_pre : nullptr);
 }

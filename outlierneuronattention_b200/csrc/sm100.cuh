@@ -112,6 +112,19 @@ __device__ __forceinline__ uint32_t mapa_shared(const void* smem, uint32_t rank)
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(smem)), "r"(rank));
   return r;
 }
+// Cluster-wide barrier arrive with release semantics (pairs with cluster_wait).
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.aligned;" ::: "memory"); }
+// Raise the transaction count of the current phase by `bytes` (no arrival).
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+// Asynchronous 4-byte store into another CTA's shared memory (shared::cluster
+// address); its bytes complete on the mbarrier at `cluster_bar` in that CTA.
+__device__ __forceinline__ void st_async_f32(uint32_t cluster_addr, float v, uint32_t cluster_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.f32 [%0], %1, [%2];" ::"r"(cluster_addr), "f"(v),
+               "r"(cluster_bar)
+               : "memory");
+}
 // Arrive (release, cluster scope) on an mbarrier in another CTA of the cluster.
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
