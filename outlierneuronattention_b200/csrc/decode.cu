@@ -119,24 +119,42 @@ __device__ __forceinline__ void gla_rows(const DecodeParams& p, int s, int b, in
     const float gam_h = expf(lg);
     const float* sin_ = p.state_in + b * p.sst[0] + h * p.sst[1];
     float* sout = p.state_out + b * p.sso[0] + h * p.sso[1];
-#pragma unroll 4
-    for (int row = r0 + rsub; row < r1; row += RSUB) {
-      const float kr = to_f(kp[(int64_t)(R + row) * p.sk[2]]);
-      const float qr = to_f(qp[(int64_t)(R + row) * p.sq[2]]);
-      float gam = gam_h;
-      if constexpr (ALPHA)
-        gam = expf(lg * expf(ld_any(p.log_alpha, p.dt_la, b * p.sla[0] + h * p.sla[1] + row * p.sla[2])));
-      const float4 s4 = __ldg(reinterpret_cast<const float4*>(sin_ + (int64_t)row * p.sst[2] + 4 * c4));
-      float4 n4;
-      n4.x = fmaf(gam, s4.x, kr * v4[0]);
-      n4.y = fmaf(gam, s4.y, kr * v4[1]);
-      n4.z = fmaf(gam, s4.z, kr * v4[2]);
-      n4.w = fmaf(gam, s4.w, kr * v4[3]);
-      *reinterpret_cast<float4*>(sout + (int64_t)row * p.sso[2] + 4 * c4) = n4;
-      ya[0] = fmaf(qr, n4.x, ya[0]);
-      ya[1] = fmaf(qr, n4.y, ya[1]);
-      ya[2] = fmaf(qr, n4.z, ya[2]);
-      ya[3] = fmaf(qr, n4.w, ya[3]);
+    // Batches of up to four rows per thread: every load of a batch is issued
+    // before its first store (a store to state_out could alias a later
+    // state_in load as far as the compiler knows, which would otherwise
+    // serialise one memory round trip per row).
+    constexpr int BAT = 4;
+    for (int base = r0 + rsub; base < r1; base += BAT * RSUB) {
+      float kr[BAT], qr[BAT], la[BAT];
+      float4 s4[BAT];
+#pragma unroll
+      for (int u = 0; u < BAT; ++u) {
+        const int row = base + u * RSUB;
+        if (row < r1) {
+          kr[u] = to_f(kp[(int64_t)(R + row) * p.sk[2]]);
+          qr[u] = to_f(qp[(int64_t)(R + row) * p.sq[2]]);
+          s4[u] = __ldg(reinterpret_cast<const float4*>(sin_ + (int64_t)row * p.sst[2] + 4 * c4));
+          if constexpr (ALPHA) la[u] = ld_any(p.log_alpha, p.dt_la, b * p.sla[0] + h * p.sla[1] + row * p.sla[2]);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < BAT; ++u) {
+        const int row = base + u * RSUB;
+        if (row < r1) {
+          float gam = gam_h;
+          if constexpr (ALPHA) gam = expf(lg * expf(la[u]));
+          float4 n4;
+          n4.x = fmaf(gam, s4[u].x, kr[u] * v4[0]);
+          n4.y = fmaf(gam, s4[u].y, kr[u] * v4[1]);
+          n4.z = fmaf(gam, s4[u].z, kr[u] * v4[2]);
+          n4.w = fmaf(gam, s4[u].w, kr[u] * v4[3]);
+          *reinterpret_cast<float4*>(sout + (int64_t)row * p.sso[2] + 4 * c4) = n4;
+          ya[0] = fmaf(qr[u], n4.x, ya[0]);
+          ya[1] = fmaf(qr[u], n4.y, ya[1]);
+          ya[2] = fmaf(qr[u], n4.z, ya[2]);
+          ya[3] = fmaf(qr[u], n4.w, ya[3]);
+        }
+      }
     }
   }
 #pragma unroll
