@@ -1,5 +1,8 @@
-// Gates + RoPE + cache export: one thread per (token, head) with 16-byte row
-// accesses (prep_vec_kernel), or one warp per (token, head) for any strides.
+// Gates + RoPE + cache export: one warp per token over all heads when each
+// token's heads are adjacent in memory (prep_tok_kernel: a token's q, k, v
+// rows are then contiguous blocks, read with coalesced 16-byte loads), one
+// thread per (token, head) with 16-byte row accesses otherwise
+// (prep_vec_kernel), or one warp per (token, head) for any strides.
 //
 // Replaces the layer's elementwise glue around the attention core
 // (src/HybridOutlierFactorizedAttention.py):
@@ -12,12 +15,20 @@
 //     :365-375; src/modules/modules.py:33-45);
 //   * the outlier cache rows: cache_k[.., pos, :R] = rotated k,
 //     cache_v[.., pos, :] = v (:196-198 prefill export, :382-384 decode append).
+#include <algorithm>
+#include <cstdlib>
+
 #include "common.cuh"
 #include "kernels.h"
 
 namespace hofa {
 
 namespace {
+
+bool getenv_flag_prep(const char* name) {
+  const char* v = getenv(name);
+  return v != nullptr && v[0] != '\0' && v[0] != '0';
+}
 
 constexpr int kPrepWarps = 8;
 
@@ -227,9 +238,214 @@ prep_vec_kernel(const PrepParams p) {
   }
 }
 
+// Token-major variant: one warp per token, all heads at once.  When every
+// head's row of a token lies next to the previous head's (q, k, v views of a
+// [.., T, H, D] or [.., T, 3, H, D] projection output), a token's q (and k, v)
+// is one contiguous block of H*D elements, read with fully coalesced 16-byte
+// loads: lane L holds 16-byte slot i = L + 32 j, i.e. channels [8g, 8g + 8)
+// (g = i % (D/8)) of head i / (D/8), so each head is a group of D/8 adjacent
+// lanes.  The gate and blend dot products reduce within a group; rotate-half
+// RoPE exchanges the partner channels of [0, R) with one shuffle (in-lane for
+// R = 8); the cache rows of a head are written by its group.  The heads'
+// gate / blend weights are staged in shared memory once per CTA, and each
+// warp walks tokens with a grid stride.
+constexpr int kTokWarps = 8;
+constexpr int kTokMaxElems = 1024;  // H * D: at most four 16-byte slots per lane (registers)
+
+template <typename T, int D, int RMAX, int NJ>   // NJ >= ceil(H * D / 256) 16-byte slots per lane
+__global__ void __launch_bounds__(kTokWarps * 32, 2)
+prep_tok_kernel(const PrepParams p) {
+  constexpr int GL = D / 8;                 // lanes per head
+  // Weights in shared memory, per head a row of 2D gate values then 2D blend
+  // values; every 32 values are followed by 4 pad words, so that the 16-byte
+  // reads of the 8 lanes of a quarter warp (channels 8g .. 8g + 7) hit
+  // distinct banks.
+  constexpr int PADROW = 2 * D + 2 * D / 8;  // one weight vector of 2D values, padded
+  extern __shared__ float w_sm[];            // [H][2][PADROW]
+  auto widx = [](int c) { return c + 4 * (c >> 5); };
+  const int H = p.H;
+  const int slots = H * GL;                 // 16-byte slots of a token's row block
+  const bool has_mix = p.mix_w != nullptr;
+  for (int i = threadIdx.x; i < H * 2 * D; i += blockDim.x) {
+    const int hh = i / (2 * D), c = i % (2 * D);
+    w_sm[(2 * hh) * PADROW + widx(c)] = ld_any(p.gate_w, p.dt_gw, hh * p.sgw[0] + c * p.sgw[1]);
+    w_sm[(2 * hh + 1) * PADROW + widx(c)] = has_mix ? ld_any(p.mix_w, p.dt_mw, hh * p.smw[0] + c * p.smw[1]) : 0.f;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31;
+  const int g = lane % GL;                  // channel group of this lane within its head
+  const int64_t total = (int64_t)p.B * p.N;
+  const int64_t nwarps = (int64_t)gridDim.x * kTokWarps;
+  const int pbase = p.pos0_dev != nullptr ? *p.pos0_dev + p.pos0_dev_bias : p.pos0;
+  for (int64_t tok = (int64_t)blockIdx.x * kTokWarps + (threadIdx.x >> 5); tok < total; tok += nwarps) {
+    const int b = (int)(tok / p.N), n = (int)(tok % p.N);
+    T* qrow = reinterpret_cast<T*>(p.q) + b * p.sq[0] + (int64_t)n * p.sq[2];
+    T* krow = reinterpret_cast<T*>(p.k) + b * p.sk[0] + (int64_t)n * p.sk[2];
+    const T* vrow = reinterpret_cast<const T*>(p.v) + b * p.sv[0] + (int64_t)n * p.sv[2];
+    const int pos = pbase + n;
+    const int prow = pos < 0 ? 0 : (pos < p.P ? pos : p.P - 1);
+    // this lane's channels are the same for every head: one table row read per token
+    float csv[RMAX > 0 ? 8 : 1], snv[RMAX > 0 ? 8 : 1];
+    if constexpr (RMAX > 0) {
+      if (p.rope && g < RMAX / 8) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          csv[e] = ld_any(p.cos, p.dt_cs, (int64_t)prow * p.scos[0] + (8 * g + e) * p.scos[1]);
+          snv[e] = ld_any(p.sin, p.dt_cs, (int64_t)prow * p.ssin[0] + (8 * g + e) * p.ssin[1]);
+        }
+      }
+    }
+    // every 16-byte slot of the token is requested before any is processed
+    uint4 aq[NJ], ak[NJ], av[NJ];
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+      const int i = lane + 32 * j;
+      aq[j] = ak[j] = av[j] = make_uint4(0, 0, 0, 0);
+      if (i < slots) {
+        aq[j] = *reinterpret_cast<const uint4*>(qrow + 8 * i);
+        ak[j] = *reinterpret_cast<const uint4*>(krow + 8 * i);
+        if (p.cache_v != nullptr) av[j] = *reinterpret_cast<const uint4*>(vrow + 8 * i);
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+      // keeps the weight reads of one slot from being hoisted above another's
+      asm volatile("" ::: "memory");
+      const int i = lane + 32 * j;
+      const bool live = i < slots;
+      const int hh = live ? i / GL : 0;
+      uint4 uk = ak[j];
+      const uint4 uv = av[j];
+      Vec8<T> vq, vk;
+      vq.w[0] = aq[j];
+      vk.w[0] = uk;
+      float fq[8], fk[8];
+      vec8_to_f(vq, fq);
+      vec8_to_f(vk, fk);
+      // gate / blend partial dots of channels [8g, 8g + 8) on the un-rotated q, k
+      const float* wg = w_sm + (2 * hh) * PADROW;
+      const float* wm = wg + PADROW;
+      float w[4][8];   // gate-q, gate-k, blend-q, blend-k weights of these channels
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        const float* src = (v < 2 ? wg : wm) + widx((v & 1) * D + 8 * g);   // 8 values, 16-byte aligned
+        const float4 a = *reinterpret_cast<const float4*>(src);
+        const float4 c4 = *reinterpret_cast<const float4*>(src + 4);
+        w[v][0] = a.x; w[v][1] = a.y; w[v][2] = a.z; w[v][3] = a.w;
+        w[v][4] = c4.x; w[v][5] = c4.y; w[v][6] = c4.z; w[v][7] = c4.w;
+      }
+      float gs = 0.f, ms = 0.f;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        gs = fmaf(fq[e], w[0][e], gs);
+        gs = fmaf(fk[e], w[1][e], gs);
+        ms = fmaf(fq[e], w[2][e], ms);
+        ms = fmaf(fk[e], w[3][e], ms);
+      }
+#pragma unroll
+      for (int o = 1; o < GL; o <<= 1) {
+        gs += __shfl_xor_sync(0xffffffffu, gs, o);
+        ms += __shfl_xor_sync(0xffffffffu, ms, o);
+      }
+      if (live && g == 0) {
+        const float gt = gs + ld_any(p.gate_b, p.dt_gb, hh * p.sgb);
+        st_any(p.log_gamma, p.dt_lg, b * p.slg[0] + hh * p.slg[1] + (int64_t)n * p.slg[2],
+               -(fmaxf(gt, 0.f) + log1pf(expf(-fabsf(gt)))));
+        if (p.mix_out != nullptr) {
+          const float mlog = has_mix ? ms + ld_any(p.mix_b, p.dt_mb, hh * p.smb) : ld_any(p.fixed_mix, p.dt_fm, hh * p.sfm);
+          st_any(p.mix_out, p.dt_mo, b * p.smo[0] + hh * p.smo[1] + (int64_t)n * p.smo[2], 1.f / (1.f + expf(-mlog)));
+        }
+      }
+      // rotate-half RoPE of channels [0, R): the partner of channel c is c +- R/2
+      if constexpr (RMAX > 0) {
+        float pq[8], pk[8];
+        if constexpr (RMAX >= 16) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            pq[e] = __shfl_xor_sync(0xffffffffu, fq[e], RMAX / 16);
+            pk[e] = __shfl_xor_sync(0xffffffffu, fk[e], RMAX / 16);
+          }
+        }
+        const bool in_r = live && g < RMAX / 8;
+        if (in_r) {
+          if (p.rope) {
+            float rq[8], rk[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+              const int c = 8 * g + e;
+              const float cs = csv[e], sn = snv[e];
+              float hq, hk;
+              if constexpr (RMAX >= 16) {
+                const bool lower = c < RMAX / 2;
+                hq = lower ? -pq[e] : pq[e];
+                hk = lower ? -pk[e] : pk[e];
+              } else {   // R = 8: the partner is in this lane
+                hq = e < 4 ? -fq[e + 4] : fq[e - 4];
+                hk = e < 4 ? -fk[e + 4] : fk[e - 4];
+              }
+              rq[e] = fq[e] * cs + hq * sn;
+              rk[e] = fk[e] * cs + hk * sn;
+            }
+            T tq[8], tk[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) { tq[e] = from_f<T>(rq[e]); tk[e] = from_f<T>(rk[e]); }
+            *reinterpret_cast<uint4*>(qrow + 8 * i) = *reinterpret_cast<const uint4*>(tq);
+            *reinterpret_cast<uint4*>(krow + 8 * i) = *reinterpret_cast<const uint4*>(tk);
+            uk = *reinterpret_cast<const uint4*>(tk);
+          }
+          if (p.cache_k != nullptr && pos >= 0 && pos < p.L) {
+            T* ck = reinterpret_cast<T*>(p.cache_k) + b * p.sck[0] + hh * p.sck[1] + (int64_t)pos * p.sck[2];
+            *reinterpret_cast<uint4*>(ck + 8 * g) = uk;
+          }
+        }
+      }
+      if (live && p.cache_v != nullptr && pos >= 0 && pos < p.L) {
+        T* cv = reinterpret_cast<T*>(p.cache_v) + b * p.scv[0] + hh * p.scv[1] + (int64_t)pos * p.scv[2];
+        *reinterpret_cast<uint4*>(cv + 8 * g) = uv;
+      }
+    }
+  }
+}
+
 template <typename T>
 cudaError_t launch_t(const PrepParams& p, cudaStream_t st) {
   if constexpr (sizeof(T) == 2) {
+    // token-major kernel: each token's heads are adjacent (head stride D) in q, k and v
+    const bool tok = p.vec && p.sq[1] == p.D && p.sk[1] == p.D && (p.cache_v == nullptr || p.sv[1] == p.D) &&
+                     p.H * p.D <= kTokMaxElems && (p.R == 0 || p.R == 8 || p.R == 16 || p.R == 32 || p.R == 64);
+    if (tok && !getenv_flag_prep("HOFA_PREP_NO_TOKEN_MAJOR")) {
+      const size_t smem = (size_t)p.H * 2 * (2 * p.D + 2 * p.D / 8) * sizeof(float);
+      int sms = 148;
+      {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      }
+      const int64_t warps_needed = (int64_t)p.B * p.N;
+      const int64_t blocks = std::min<int64_t>((warps_needed + kTokWarps - 1) / kTokWarps, (int64_t)sms * 6);
+      bool launched = true;
+      const int nj = (p.H * p.D / 8 + 31) / 32;
+#define HOFA_PREP_TOK_NJ(DD, RR, NJJ)                                                                          \
+  {                                                                                                            \
+    auto kk = prep_tok_kernel<T, DD, RR, NJJ>;                                                                 \
+    if (smem > 48 * 1024) cudaFuncSetAttribute(kk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);    \
+    kk<<<(unsigned)blocks, kTokWarps * 32, smem, st>>>(p);                                                     \
+  }
+#define HOFA_PREP_TOK(DD, RR)                                                                                  \
+  else if (p.D == DD && p.R == RR) {                                                                           \
+    if (nj <= 1) HOFA_PREP_TOK_NJ(DD, RR, 1)                                                                   \
+    else if (nj <= 2) HOFA_PREP_TOK_NJ(DD, RR, 2)                                                              \
+    else HOFA_PREP_TOK_NJ(DD, RR, 4)                                                                           \
+  }
+      if (false) {}
+      HOFA_PREP_TOK(64, 0) HOFA_PREP_TOK(64, 8) HOFA_PREP_TOK(64, 16) HOFA_PREP_TOK(64, 32) HOFA_PREP_TOK(64, 64)
+      HOFA_PREP_TOK(128, 0) HOFA_PREP_TOK(128, 16) HOFA_PREP_TOK(128, 32) HOFA_PREP_TOK(128, 64)
+      HOFA_PREP_TOK(32, 0) HOFA_PREP_TOK(32, 8) HOFA_PREP_TOK(32, 16) HOFA_PREP_TOK(32, 32)
+      else launched = false;
+#undef HOFA_PREP_TOK
+#undef HOFA_PREP_TOK_NJ
+      if (launched) return cudaGetLastError();
+    }
     if (p.vec) {
       const dim3 grid((unsigned)((p.N + kVecThreads - 1) / kVecThreads), p.H, p.B);
       const int r = p.R;  // the outlier channels: rotated when p.rope, copied to cache_k either way
