@@ -231,7 +231,7 @@ outlier_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
   auto wait = [&](uint64_t* bar, uint32_t parity) {
     if (sm100::mbar_try_wait(bar, parity)) return;
     if (*verr) return;
-    if (!sm100::mbar_wait_sleep(bar, parity)) atomicOr(err_flag, 1);
+    if (!sm100::mbar_wait(bar, parity)) atomicOr(err_flag, 1);
   };
 
   if (warp == kSoftmaxWarps) {
@@ -514,14 +514,16 @@ cudaError_t launch_dr(const OutlierParams& p, cudaStream_t st, bool* taken) {
   if (!make_map(&mk, p.k, bf16, R, p.Tk, p.H, p.B, sk, R, kKeys, qk_swz)) return cudaSuccess;
   if (!make_map(&mv, p.v, bf16, D, p.Tk, p.H, p.B, sv, 64, kKeys, CU_TENSOR_MAP_SWIZZLE_128B)) return cudaSuccess;
   dim3 grid((unsigned)((p.Tq + kRows - 1) / kRows) * p.H * p.B);
-  // HOFA_OUTLIER_EMU (0, 2, 3) overrides how many of every 8 exp2 pairs of a
+  // HOFA_OUTLIER_EMU (0..4) overrides how many of every 8 exp2 pairs of a
   // full tile run as the FMA-pipe polynomial (bf16, head dim 64, r = 16)
   if constexpr (std::is_same<T, __nv_bfloat16>::value && D == 64 && R == 16) {
     const char* emu = getenv("HOFA_OUTLIER_EMU");
     const int e = emu != nullptr && emu[0] != '\0' ? atoi(emu) : kEmuDefault;
     if (e == 0) return launch_kernel<T, D, R, 0>(mq, mk, mv, p, grid, st, taken);
-    if (e == 3) return launch_kernel<T, D, R, 3>(mq, mk, mv, p, grid, st, taken);
+    if (e == 1) return launch_kernel<T, D, R, 1>(mq, mk, mv, p, grid, st, taken);
     if (e == 2) return launch_kernel<T, D, R, 2>(mq, mk, mv, p, grid, st, taken);
+    if (e == 3) return launch_kernel<T, D, R, 3>(mq, mk, mv, p, grid, st, taken);
+    if (e == 4) return launch_kernel<T, D, R, 4>(mq, mk, mv, p, grid, st, taken);
   }
   return launch_kernel<T, D, R, kEmuDefault>(mq, mk, mv, p, grid, st, taken);
 }
