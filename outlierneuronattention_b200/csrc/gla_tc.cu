@@ -16,7 +16,8 @@
 //   B  gla_tc_scan_kernel    (one thread per state element of a head)
 //        S_0 = state_init or 0;  start_c = S before chunk c;  S <- exp(G_C) S + dS_c
 //        start_c overwrites dS_c in the workspace; the last S goes to state_out
-//   C  gla_tc_out_kernel     (one CTA per chunk c)
+//   C  gla_tc_out_kernel     (one CTA per chunk c; at D = 64 Y2 and then Y1 reuse A's
+//                             upper TMEM columns once P is formed: 128 columns, 3 CTAs/SM)
 //        A   = Q_I K_I^T            tcgen05.mma M=128, N=128, K=J (A/B K-major)
 //        Y2  = Q_I start_c          tcgen05.mma M=128, N=D,   K=J (start_c as a bf16
 //                                   MN-major operand)
@@ -55,10 +56,14 @@ struct Geo {
   static constexpr uint32_t OP = NB * kTile;             // one operand tile (128 tokens x D)
   static constexpr uint32_t LBO = NB > 1 ? kTile : 16;   // byte distance of the column blocks
   static constexpr int STATE_M = D == 64 ? 64 : 128;     // MMA M of the state kernel
-  static constexpr uint32_t OUT_COLS = D == 64 ? 256 : 512;  // A (128) + Y1 (D) + Y2 (D), power of two
+  // output kernel TMEM: D = 64 keeps A (128 columns) and lets Y2 then Y1 use A's
+  // upper half once P is formed (128 columns, three CTAs per SM); D = 128 holds
+  // A, Y1 and Y2 side by side (512 columns, one CTA per SM)
+  static constexpr bool SHARE = D == 64;
+  static constexpr uint32_t OUT_COLS = SHARE ? 128 : 512;
   static constexpr size_t STATE_SMEM = 2 * OP + 1024 + 256;
   // D = 64: 80 KB keeps <= 2 CTAs (2 x 256 TMEM columns) per SM; D = 128: one CTA
-  static constexpr size_t OUT_SMEM = D == 64 ? 80 * 1024 : 4 * OP + 1024 + 4096;
+  static constexpr size_t OUT_SMEM = 4 * OP + 1024 + 4096;
 };
 
 __device__ __forceinline__ uint32_t pack2(float a, float b, bool bf16) {
@@ -241,7 +246,7 @@ __global__ void __launch_bounds__(256) gla_tc_scan_kernel(const GlaParams p) {
 // C: per-chunk output
 // ---------------------------------------------------------------------------
 template <typename T, int D>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, D == 64 ? 3 : 1)
 gla_tc_out_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                   const __grid_constant__ CUtensorMap tv, const GlaParams p) {
   using Gm = Geo<D>;
@@ -280,7 +285,8 @@ gla_tc_out_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
   __syncthreads();
   sm100::tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tA = tmem, tY1 = tmem + 128, tY2 = tmem + 128 + D;
+  const uint32_t tA = tmem;
+  const uint32_t tY1 = Gm::SHARE ? tmem + 64 : tmem + 128, tY2 = Gm::SHARE ? tmem + 64 : tmem + 128 + D;
   const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
   if (tid == 0) {
     sm100::mbar_arrive_expect_tx(&bars[0], 3 * Gm::OP);
@@ -331,8 +337,9 @@ gla_tc_out_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
     // K-major steps of 16 channels: 4 per 128-byte block (32 B each), blocks kTile apart
     auto kstep = [](int ks) { return (uint64_t)(((ks >> 2) * kTile + (ks & 3) * 32) >> 4); };
     for (int ks = 0; ks < KS; ++ks) sm100::mma_ss(tA, qdesc + kstep(ks), kdesc + kstep(ks), IDESC_A, ks > 0);
-    for (int ks = 0; ks < KS; ++ks)
-      sm100::mma_ss(tY2, qdesc + kstep(ks), sdesc + (uint64_t)(ks * 2048 >> 4), IDESC_Y, ks > 0);
+    if (!Gm::SHARE)
+      for (int ks = 0; ks < KS; ++ks)
+        sm100::mma_ss(tY2, qdesc + kstep(ks), sdesc + (uint64_t)(ks * 2048 >> 4), IDESC_Y, ks > 0);
     sm100::mma_commit(&bars[1]);
   }
   if (!*verr && !sm100::mbar_wait(&bars[1], 0)) atomicOr(err, 1);
@@ -361,6 +368,32 @@ gla_tc_out_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
   sm100::tc_wait_st();
   sm100::tc_fence_before();
   __syncthreads();
+  // SHARE: Y2 = Q_I start_c into A's upper half (consumed above), read into
+  // registers, then Y1 = P V into the same columns
+  float y2r[Gm::SHARE ? D : 1];
+  if constexpr (Gm::SHARE) {
+    if (tid == 0 && !*verr) {
+      sm100::tc_fence_after();
+      const uint64_t qdesc = sm100::smem_desc(sQ, 16, 1024, sm100::kSwizzle128);
+      const uint64_t sdesc = sm100::smem_desc(sS, Gm::LBO, 1024, sm100::kSwizzle128);
+      auto kstep = [](int ks) { return (uint64_t)(((ks >> 2) * kTile + (ks & 3) * 32) >> 4); };
+      for (int ks = 0; ks < KS; ++ks)
+        sm100::mma_ss(tY2, qdesc + kstep(ks), sdesc + (uint64_t)(ks * 2048 >> 4), IDESC_Y, ks > 0);
+      sm100::mma_commit(&bars[1]);
+    }
+    if (!*verr && !sm100::mbar_wait(&bars[1], 1)) atomicOr(err, 1);
+    sm100::tc_fence_after();
+#pragma unroll
+    for (int cc = 0; cc < D; cc += 32) {
+      uint32_t a[32];
+      sm100::tmem_ld32(tY2 + lane_off + cc, a);
+      sm100::tc_wait_ld();
+#pragma unroll
+      for (int u = 0; u < 32; ++u) y2r[cc + u] = __uint_as_float(a[u]);
+    }
+    sm100::tc_fence_before();
+    __syncthreads();
+  }
   if (tid == 0 && !*verr) {
     sm100::tc_fence_after();
     const uint64_t vdesc = sm100::smem_desc(sV, Gm::LBO, 1024, sm100::kSwizzle128);
@@ -369,7 +402,7 @@ gla_tc_out_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
       sm100::mma_ts(tY1, tA + kk * 8, vdesc + (uint64_t)(kk * 2048 >> 4), IDESC_Y, kk > 0);
     sm100::mma_commit(&bars[1]);
   }
-  if (!*verr && !sm100::mbar_wait(&bars[1], 1)) atomicOr(err, 1);
+  if (!*verr && !sm100::mbar_wait(&bars[1], Gm::SHARE ? 0 : 1)) atomicOr(err, 1);
   sm100::tc_fence_after();
 
   // epilogue: y = Y1 + exp(G_i) Y2, fused (1 - mix) * gla_scale * RMSNorm(y); two passes over
@@ -382,11 +415,12 @@ gla_tc_out_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
     for (int cc = 0; cc < D; cc += 32) {
       uint32_t a[32], bb[32];
       sm100::tmem_ld32(tY1 + lane_off + cc, a);
-      sm100::tmem_ld32(tY2 + lane_off + cc, bb);
+      if (!Gm::SHARE) sm100::tmem_ld32(tY2 + lane_off + cc, bb);
       sm100::tc_wait_ld();
 #pragma unroll
       for (int u = 0; u < 32; ++u) {
-        const float y = fmaf(eg, __uint_as_float(bb[u]), __uint_as_float(a[u]));
+        const float y2 = Gm::SHARE ? y2r[cc + u] : __uint_as_float(bb[u]);
+        const float y = fmaf(eg, y2, __uint_as_float(a[u]));
         ss = fmaf(y, y, ss);
       }
     }
@@ -399,12 +433,13 @@ gla_tc_out_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
   for (int cc = 0; cc < D; cc += 32) {
     uint32_t a[32], bb[32];
     sm100::tmem_ld32(tY1 + lane_off + cc, a);  // warp-collective: every lane executes it
-    sm100::tmem_ld32(tY2 + lane_off + cc, bb);
+    if (!Gm::SHARE) sm100::tmem_ld32(tY2 + lane_off + cc, bb);
     sm100::tc_wait_ld();
     if (store) {
       float y[32];
 #pragma unroll
-      for (int u = 0; u < 32; ++u) y[u] = fmaf(eg, __uint_as_float(bb[u]), __uint_as_float(a[u])) * scale * sGS[cc + u];
+      for (int u = 0; u < 32; ++u)
+        y[u] = fmaf(eg, Gm::SHARE ? y2r[cc + u] : __uint_as_float(bb[u]), __uint_as_float(a[u])) * scale * sGS[cc + u];
       if (vec) {
 #pragma unroll
         for (int d = 0; d < 32; d += 8) {
