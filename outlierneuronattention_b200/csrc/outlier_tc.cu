@@ -31,9 +31,10 @@
 // its exponentials against the running max at once and only takes the row max
 // when a row's sum shows a growth past 2^64.
 //
-// Exponentials: a share of the exp2 evaluations of each full (unmasked) half
-// can run on the FMA pipe as a cubic polynomial (exp2_pair_poly), the rest on
-// the MUFU unit (HOFA_OUTLIER_EMU; MUFU only by default).
+// Exponentials: one of every eight exp2 pairs of each full (unmasked) half
+// runs on the FMA pipe as a cubic polynomial (exp2_pair_poly), the rest on the
+// MUFU unit, so that neither unit alone bounds the softmax (HOFA_OUTLIER_EMU
+// selects 0-4 of 8 at bf16, head dim 64, r = 16; one measured fastest).
 //
 // Every mbarrier wait is bounded; on a timeout the CTA records an error in
 // g_outlier_tc_status, skips the rest of its work, frees its TMEM and exits.
@@ -58,7 +59,7 @@ constexpr int kHalf = 32;          // the softmax takes a tile in two halves of 
 constexpr int kSoftmaxWarps = 4;
 constexpr int kThreads = 32 * (kSoftmaxWarps + 1);
 constexpr int kStages = 4;         // K and V ring depth
-constexpr int kEmuDefault = 0;     // of every 8 exp2 pairs of a full half-tile, this many run on the FMA pipe
+constexpr int kEmuDefault = 1;     // of every 8 exp2 pairs of a full half-tile, this many run on the FMA pipe (measured best)
 
 // TMEM columns: the S/P buffer in [0, kKeys), O in [kKeys, kKeys + D), rounded up to a power of two
 template <int D>
