@@ -221,13 +221,24 @@ __global__ void __launch_bounds__(256) gla_tc_scan_kernel(const GlaParams p) {
   const float* gc = p.ws_decay + bh * p.nseg;
   const int64_t cs = (int64_t)p.J * p.D;
   // 16 chunk contributions per round trip: their loads are independent, only
-  // the fmaf chain is sequential
+  // the fmaf chain is sequential.  The next batch is requested before this
+  // batch's start states are stored (the compiler cannot move those loads
+  // above the stores, which it must assume may alias), so round trips overlap.
   constexpr int kU = 16;
-  int c = 0;
-  for (; c + kU <= p.nseg; c += kU) {
-    float dS[kU], g[kU];
+  const int full = p.nseg / kU * kU;
+  float dS[kU], g[kU], dSn[kU], gn[kU];
+  if (full > 0) {
 #pragma unroll
-    for (int u = 0; u < kU; ++u) { dS[u] = ws[(c + u) * cs]; g[u] = gc[c + u]; }
+    for (int u = 0; u < kU; ++u) { dSn[u] = ws[u * cs]; gn[u] = gc[u]; }
+  }
+  int c = 0;
+  for (; c < full; c += kU) {
+#pragma unroll
+    for (int u = 0; u < kU; ++u) { dS[u] = dSn[u]; g[u] = gn[u]; }
+    if (c + kU < full) {
+#pragma unroll
+      for (int u = 0; u < kU; ++u) { dSn[u] = ws[(c + kU + u) * cs]; gn[u] = gc[c + kU + u]; }
+    }
 #pragma unroll
     for (int u = 0; u < kU; ++u) {
       ws[(c + u) * cs] = S;
