@@ -359,6 +359,7 @@ def run_ours(args):
     if not args.no_config4 and world == 1:
         out["config4"] = measure_config4(dev)
         out["layer_step"] = [measure_layer_step(dev, B=1), measure_layer_step(dev, B=4)]
+        out["decode_batches"] = [measure_decode_batch(dev, 1), measure_decode_batch(dev, 64, steps=50)]
     if not args.no_config4 and world > 1:
         out["config4_seqpar"] = measure_seqpar(dev, world)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -437,6 +438,58 @@ def measure_prefill(dev, B=4, T=8192, steps=5, warmup=3, name="config2"):
             "roofline_outlier_kernel": {"bound": "tensor", "achieved": round(ach, 2), "peak": bf16_peak,
                                         "unit": "TFLOP/s", "frac": round(ach / bf16_peak, 4),
                                         "peak_source": "measured bf16_tflops (burst)"}}
+
+
+def measure_decode_batch(dev, B, steps=200, reps=3):
+    """Config-1 decode (L=4096, H=16, d_h=64, r=16, bf16) at another batch size:
+    `hofa_decode_fwd` steps replayed from a CUDA graph over rotating cache
+    sets of at least 3 x L2 (every step streams its cache from HBM), timed
+    with CUDA events; tokens/s and the HBM roofline of the step."""
+    from outlierneuronattention_b200 import _capi
+    from outlierneuronattention_b200.hofa_decode import decode_args, decode_workspace
+    per_set = algorithmic_bytes(B)
+    nsets = max(2, math.ceil(3 * 126 * 2 ** 20 / per_set))
+    inp = make_step_inputs(B, "cpu", seed=5000 + B)
+    q, k, v = (inp[n].to(dev) for n in ("q", "k", "v"))
+    lg, mix, nw = inp["log_gamma"].to(dev), inp["mix"].to(dev), inp["norm_w"].to(dev)
+    sets = [make_cache(B, dev, seed=100 * B + i) for i in range(nsets)]
+    outs = [torch.empty(B, H, J, D, device=dev) for _ in range(nsets)]
+    y = torch.empty_like(q)
+    ws = decode_workspace(dev, B, H, D)
+    fmt = _capi.FORMATS[_capi.DecodeArgs]
+    bufs = [fmt.pack(*decode_args(q, k, v, ck, cv, st, outs[i], lg, mix, nw, R, L, 2.0, y, workspace=ws))
+            for i, (ck, cv, st) in enumerate(sets)]
+    fn = _capi.lib().hofa_decode_fwd
+    stream = torch.cuda.Stream(dev)
+
+    def launch(n):
+        for i in range(n):
+            if fn(bufs[i % nsets], stream.cuda_stream) != 0:
+                raise RuntimeError(_capi.lib().hofa_last_error().decode())
+
+    with torch.cuda.stream(stream):
+        launch(nsets)
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            launch(steps)
+        graph.replay()
+        stream.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+        stream.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * steps)
+    del graph
+    peak, kind = peaks()
+    ach = per_set / (us / 1e6) / 1e9
+    split = int(_capi.lib().hofa_decode_choose_split(B, H, L, torch.cuda.get_device_properties(dev).multi_processor_count))
+    return {"workload": f"config1-decode-B{B}-L{L}", "us_per_step": round(us, 3), "tokens_per_s": round(B / (us / 1e6), 1),
+            "algorithmic_bytes_per_step": per_set, "split_k": split, "rotating_sets": nsets,
+            "roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(ach / peak, 4), "peak_source": f"{kind} hbm_gbs"}}
 
 
 def measure_config4(dev, steps=64, reps=3):
