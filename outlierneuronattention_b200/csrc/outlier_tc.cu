@@ -31,10 +31,10 @@
 // its exponentials against the running max at once and only takes the row max
 // when a row's sum shows a growth past 2^64.
 //
-// Exponentials: one of every eight exp2 pairs of each full (unmasked) half
+// Exponentials: two of every sixteen exp2 pairs of each full (unmasked) half
 // runs on the FMA pipe as a cubic polynomial (exp2_pair_poly), the rest on the
 // MUFU unit, so that neither unit alone bounds the softmax (HOFA_OUTLIER_EMU
-// selects 0-4 of 8 at bf16, head dim 64, r = 16; one measured fastest).
+// selects 0-4 of 16 at bf16, head dim 64, r = 16; two measured fastest).
 //
 // Every mbarrier wait is bounded; on a timeout the CTA records an error in
 // g_outlier_tc_status, skips the rest of its work, frees its TMEM and exits.
@@ -59,7 +59,7 @@ constexpr int kHalf = 32;          // the softmax takes a tile in two halves of 
 constexpr int kSoftmaxWarps = 4;
 constexpr int kThreads = 32 * (kSoftmaxWarps + 1);
 constexpr int kStages = 4;         // K and V ring depth
-constexpr int kEmuDefault = 1;     // of every 8 exp2 pairs of a full half-tile, this many run on the FMA pipe (measured best)
+constexpr int kEmuDefault = 2;     // of the 16 exp2 pairs of a full half-tile, this many run on the FMA pipe (measured best)
 
 // TMEM columns: the S/P buffer in [0, kKeys), O in [kKeys, kKeys + D), rounded up to a power of two
 template <int D>
@@ -124,8 +124,9 @@ __device__ __forceinline__ void exp2_pair_poly(uint64_t x2, float& e0, float& e1
 }
 
 // Row of 32 scores -> 32 probabilities packed as 16-bit pairs in pk[16]
-// (pair i = columns 2i, 2i+1); returns the row sum in fp32.  E of every 8
-// pairs use the polynomial, the rest the MUFU unit.
+// (pair i = columns 2i, 2i+1); returns the row sum in fp32.  E of the 16
+// pairs, spread evenly (pair i when i*E mod 16 < E), use the polynomial, the
+// rest the MUFU unit.
 template <bool BF16, int E>
 __device__ __forceinline__ float row_exp(const uint32_t (&r)[32], float scale, float m, uint32_t (&pk)[16]) {
   const uint64_t sc2 = sm100::f2_pack(scale, scale);
@@ -138,7 +139,7 @@ __device__ __forceinline__ float row_exp(const uint32_t (&r)[32], float scale, f
     const uint64_t x =
         sm100::f2_fma(sm100::f2_pack(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1])), sc2, nm2);
     float e0, e1;
-    if ((i & 7) < E) {
+    if ((i * E) % 16 < E) {
       exp2_pair_poly(x, e0, e1);
     } else {
       float x0, x1;
@@ -318,7 +319,7 @@ outlier_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
           // exponentials against the running max straight away; a row whose max
           // grew by more than 2^kRaise shows in its sum (>= 2^kRaise, inf or
           // NaN), and only then does the warp redo the half with the row max
-          ls = row_exp<BF16, (EMU > 8 ? 0 : EMU)>(r, scale, m_used, pk);
+          ls = row_exp<BF16, (EMU > 16 ? 0 : EMU)>(r, scale, m_used, pk);
           slow = __any_sync(0xffffffffu, !(ls < 1.8446744e19f));  // 2^64
         }
         if (slow) {
@@ -369,7 +370,7 @@ outlier_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
             }
           }
           ls = masked ? row_exp<BF16, 0>(r, scale, m_used, pk)   // exact zeros where masked
-                      : row_exp<BF16, (EMU > 8 ? 0 : EMU)>(r, scale, m_used, pk);
+                      : row_exp<BF16, (EMU > 16 ? 0 : EMU)>(r, scale, m_used, pk);
         }
         l_sum = l_sum * factor + ls;
         // P of this half as 16-bit pairs over columns [16 hf, 16 hf + 16), which
@@ -515,8 +516,8 @@ cudaError_t launch_dr(const OutlierParams& p, cudaStream_t st, bool* taken) {
   if (!make_map(&mk, p.k, bf16, R, p.Tk, p.H, p.B, sk, R, kKeys, qk_swz)) return cudaSuccess;
   if (!make_map(&mv, p.v, bf16, D, p.Tk, p.H, p.B, sv, 64, kKeys, CU_TENSOR_MAP_SWIZZLE_128B)) return cudaSuccess;
   dim3 grid((unsigned)((p.Tq + kRows - 1) / kRows) * p.H * p.B);
-  // HOFA_OUTLIER_EMU (0..4) overrides how many of every 8 exp2 pairs of a
-  // full tile run as the FMA-pipe polynomial (bf16, head dim 64, r = 16)
+  // HOFA_OUTLIER_EMU (0..4) overrides how many of the 16 exp2 pairs of a
+  // full half-tile run as the FMA-pipe polynomial (bf16, head dim 64, r = 16)
   if constexpr (std::is_same<T, __nv_bfloat16>::value && D == 64 && R == 16) {
     const char* emu = getenv("HOFA_OUTLIER_EMU");
     const int e = emu != nullptr && emu[0] != '\0' ? atoi(emu) : kEmuDefault;
