@@ -255,10 +255,11 @@ int decode_setup(const hofa_decode_args* a, hofa::DecodeParams& p, int& path, bo
   p.consumer_warps = 4;
   p.stages = es == 4 ? 4 : 8;
   if (const char* v = getenv("HOFA_DECODE_WARPS")) p.consumer_warps = atoi(v) == 8 ? 8 : 4;
-  // L2 prefetch before the grid dependency only while the step's cache rows fit
-  // well inside L2 (larger steps would evict prefetched rows before use)
+  // L2 prefetch before the grid dependency only for small steps (up to 24 MB
+  // of cache rows: measured faster at B = 1 and 2 of the 4096-token config,
+  // slower at B = 4, whose 42 MB step keeps HBM busy without it)
   p.no_l2_prefetch = getenv_flag("HOFA_DECODE_NO_L2_PREFETCH") ||
-                     (double)B * H * (a->seq_len_dev ? L : a->seq_len) * (R + D) * es > 48e6;
+                     (double)B * H * (a->seq_len_dev ? L : a->seq_len) * (R + D) * es > 24e6;
   if (const char* v = getenv("HOFA_DECODE_STAGES")) {
     const int n = atoi(v);
     if (n >= 2 && n <= 16) p.stages = n;
