@@ -254,6 +254,16 @@ int decode_setup(const hofa_decode_args* a, hofa::DecodeParams& p, int& path, bo
   // which requires stages % consumer_warps == 0
   p.consumer_warps = 4;
   p.stages = es == 4 ? 4 : 8;
+  // A grid that does not fit at once with the 8-slot ring (80 KB at r=16,
+  // d_h=64: two CTAs per SM) runs in waves; then the 4-slot ring, which keeps
+  // more CTAs resident per SM, streams faster (measured at config 1: B=32
+  // 90 -> 94 % and B=64 90 -> 97 % of the HBM roofline; one-wave grids such
+  // as B=4, 8 and 16 are faster with 8 slots).
+  if (es != 4) {
+    const size_t ring8 = (size_t)8 * 64 * (R + D) * es;
+    const int64_t per_sm8 = (int64_t)(228 * 1024 / (ring8 + 12 * 1024));
+    if ((int64_t)B * H * split > (per_sm8 > 0 ? per_sm8 : 1) * (int64_t)sms) p.stages = 4;
+  }
   if (const char* v = getenv("HOFA_DECODE_WARPS")) p.consumer_warps = atoi(v) == 8 ? 8 : 4;
   // L2 prefetch before the grid dependency only for small steps (up to 24 MB
   // of cache rows: measured faster at B = 1 and 2 of the 4096-token config,
