@@ -22,6 +22,8 @@
 //                    consumed (P of the tile ends in columns [0, 32)), arrive.
 //   While a CTA's softmax waits for its next S, the warps of the other CTAs
 //   on the SM keep the exponential unit busy.
+//   The 1-D grid launches the row blocks with the most keys first, across
+//   all heads, so that the CTAs finishing last are short ones.
 //
 // The running max is raised only when a row's max grows by more than 2^64
 // (bf16; 2^8 for f16, whose largest value is 65504) -- then the row of O (and
@@ -31,8 +33,8 @@
 // its exponentials against the running max at once and only takes the row max
 // when a row's sum shows a growth past 2^64.
 //
-// Exponentials: two of every sixteen exp2 pairs of each full (unmasked) half
-// runs on the FMA pipe as a cubic polynomial (exp2_pair_poly), the rest on the
+// Exponentials: two of the sixteen exp2 pairs of each full (unmasked) half
+// run on the FMA pipe as a cubic polynomial (exp2_pair_poly), the rest on the
 // MUFU unit, so that neither unit alone bounds the softmax (HOFA_OUTLIER_EMU
 // selects 0-4 of 16 at bf16, head dim 64, r = 16; two measured fastest).
 //
