@@ -61,3 +61,44 @@ def test_prep_matches_reference_formulas(dtype, strided, D, r):
         assert (ck[:, :, pos0:pos0 + N, :r].double().cpu() - ref_k[..., :r]).abs().max().item() <= tol * 4
         assert ck[:, :, :pos0].abs().max().item() == 0 and ck[:, :, pos0 + N:].abs().max().item() == 0
     assert torch.equal(cv[:, :, pos0:pos0 + N].cpu(), vd.cpu())
+
+
+@pytest.mark.parametrize("layout", ["token_major", "head_major"])
+@pytest.mark.parametrize("D,r", [(32, 8), (32, 32), (64, 8), (64, 16), (64, 64), (128, 16), (128, 64)])
+def test_prep_row_layouts(layout, D, r):
+    """Both 16-byte-row kernels: token_major views of one [B, N, 3, H, D]
+    projection output (a token's heads adjacent: the warp-per-token kernel)
+    and head_major separate [B, H, N, D] tensors (the thread-per-row kernel).
+    H = 5 leaves part of a warp's 16-byte slots without a head."""
+    from outlierneuronattention_b200.modules import RotaryEmbedding
+    from outlierneuronattention_b200.prep import prep
+    dtype = torch.bfloat16
+    g = torch.Generator().manual_seed(7 * D + r)
+    B, H, N, L, pos0 = 2, 5, 70, 100, 9
+    x = torch.randn(B, N, 3, H, D, generator=g).to(dtype)
+    if layout == "token_major":
+        xd = x.cuda()
+        qd, kd, vd = (xd[:, :, i].transpose(1, 2) for i in range(3))
+        assert qd.stride(1) == D
+    else:
+        qd, kd, vd = (x[:, :, i].transpose(1, 2).contiguous().cuda() for i in range(3))
+        assert qd.stride(1) == N * D
+    gw, mw = torch.randn(H, 2 * D, generator=g) * 0.3, torch.randn(H, 2 * D, generator=g) * 0.3
+    gb, mb = torch.randn(H, generator=g), torch.randn(H, generator=g)
+    ref_lg, ref_mix, ref_q, ref_k = reference(qd.cpu(), kd.cpu(), vd.cpu(), gw, gb, mw, mb, r, pos0)
+    lg = torch.empty(B, H, N, device="cuda")
+    mix = torch.empty(B, H, N, device="cuda", dtype=dtype)
+    ck = torch.zeros(B, H, L, r, device="cuda", dtype=dtype)
+    cv = torch.zeros(B, H, L, D, device="cuda", dtype=dtype)
+    rope = RotaryEmbedding(r).cuda()
+    prep(qd, kd, vd, gw.cuda(), gb.cuda(), lg, mix_w=mw.cuda(), mix_b=mb.cuda(), mix_out=mix,
+         cos=rope.cos_cached, sin=rope.sin_cached, R=r, pos0=pos0, cache_k=ck, cache_v=cv, use_rope=True)
+    torch.cuda.synchronize()
+    tol = 2e-2
+    assert (lg.double().cpu() - ref_lg).abs().max().item() <= tol
+    assert (mix.double().cpu() - ref_mix).abs().max().item() <= tol
+    assert (qd.double().cpu() - ref_q).abs().max().item() <= tol * 4
+    assert (kd.double().cpu() - ref_k).abs().max().item() <= tol * 4
+    assert (ck[:, :, pos0:pos0 + N].double().cpu() - ref_k[..., :r]).abs().max().item() <= tol * 4
+    assert ck[:, :, :pos0].abs().max().item() == 0 and ck[:, :, pos0 + N:].abs().max().item() == 0
+    assert torch.equal(cv[:, :, pos0:pos0 + N].cpu(), vd.cpu())
