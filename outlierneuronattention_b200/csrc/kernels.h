@@ -108,6 +108,7 @@ struct PrepParams {
   int64_t sck[4], scv[4];
   int dt_gw, dt_gb, dt_mw, dt_mb, dt_fm, dt_cs, dt_lg, dt_mo;
   bool vec;                    // unit channel strides and 16-byte aligned rows everywhere
+  uint32_t zero;               // 0, set by the launcher (an operand the compiler cannot fold)
 };
 
 cudaError_t launch_prep(const PrepParams& p, int dtype, cudaStream_t st);

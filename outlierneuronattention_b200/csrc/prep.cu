@@ -248,9 +248,23 @@ prep_vec_kernel(const PrepParams p) {
 // RoPE exchanges the partner channels of [0, R) with one shuffle (in-lane for
 // R = 8); the cache rows of a head are written by its group.  The heads'
 // gate / blend weights are staged in shared memory once per CTA, and each
-// warp walks tokens with a grid stride.
+// warp walks tokens with a grid stride over a grid of resident CTAs.  Each
+// lane copies its slots of the warp's NEXT token (and that token's cos/sin
+// channels when the tables are contiguous fp32) into its own part of a
+// shared-memory stage with cp.async while the current token is computed, so
+// a warp always has one token's reads in flight.
 constexpr int kTokWarps = 8;
 constexpr int kTokMaxElems = 1024;  // H * D: at most four 16-byte slots per lane (registers)
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gmem_src) {
+  const uint32_t d = static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(d), "l"(gmem_src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Bytes of one warp's stage: q, k, v slots of a token, then cos lo/hi, sin lo/hi.
+template <int NJ, int RMAX>
+__host__ __device__ constexpr int tok_stage_bytes() { return (3 * NJ + (RMAX > 0 ? 4 : 0)) * 32 * 16; }
 
 template <typename T, int D, int RMAX, int NJ>   // NJ >= ceil(H * D / 256) 16-byte slots per lane
 __global__ void __launch_bounds__(kTokWarps * 32, 2)
@@ -261,52 +275,119 @@ prep_tok_kernel(const PrepParams p) {
   // reads of the 8 lanes of a quarter warp (channels 8g .. 8g + 7) hit
   // distinct banks.
   constexpr int PADROW = 2 * D + 2 * D / 8;  // one weight vector of 2D values, padded
-  extern __shared__ float w_sm[];            // [H][2][PADROW]
+  extern __shared__ __align__(16) float w_sm[];   // [H][2][PADROW], then kTokWarps stages
   auto widx = [](int c) { return c + 4 * (c >> 5); };
   const int H = p.H;
   const int slots = H * GL;                 // 16-byte slots of a token's row block
   const bool has_mix = p.mix_w != nullptr;
+  const int lane = threadIdx.x & 31;
+  const int g = lane % GL;                  // channel group of this lane within its head
+  const int64_t total = (int64_t)p.B * p.N;
+  const int64_t nwarps = (int64_t)gridDim.x * kTokWarps;
+  const int pbase = p.pos0_dev != nullptr ? *p.pos0_dev + p.pos0_dev_bias : p.pos0;
+  // this lane's stage entries: data slot (t, j) at stg[(t * NJ + j) * 32], table row q at stg[(3 NJ + q) * 32]
+  uint4* stg = reinterpret_cast<uint4*>(w_sm + H * 2 * PADROW) + (threadIdx.x >> 5) * (tok_stage_bytes<NJ, RMAX>() / 16) + lane;
+  const bool tab_async = RMAX > 0 && p.rope && p.dt_cs == HOFA_DTYPE_F32 && p.scos[1] == 1 && p.ssin[1] == 1 &&
+                         (p.scos[0] & 3) == 0 && (p.ssin[0] & 3) == 0 &&
+                         ((reinterpret_cast<uintptr_t>(p.cos) | reinterpret_cast<uintptr_t>(p.sin)) & 15) == 0;
+  // Copies token t's slots into the stage.  `z` is zero, computed from the
+  // values this lane last read from the stage, so that the copies cannot be
+  // issued before those reads have returned.
+  auto prefetch = [&](int b_, int n_, uint32_t z) {
+    const T* q_ = reinterpret_cast<const T*>(p.q) + b_ * p.sq[0] + (int64_t)n_ * p.sq[2];
+    const T* k_ = reinterpret_cast<const T*>(p.k) + b_ * p.sk[0] + (int64_t)n_ * p.sk[2];
+    const T* v_ = reinterpret_cast<const T*>(p.v) + b_ * p.sv[0] + (int64_t)n_ * p.sv[2];
+    uint4* d = stg + z;
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+      const int i = lane + 32 * j;
+      if (i < slots) {
+        cp_async16(d + (0 * NJ + j) * 32, q_ + 8 * i);
+        cp_async16(d + (1 * NJ + j) * 32, k_ + 8 * i);
+        if (p.cache_v != nullptr) cp_async16(d + (2 * NJ + j) * 32, v_ + 8 * i);
+      }
+    }
+    if (RMAX > 0 && tab_async && g < RMAX / 8) {
+      const int pos_ = pbase + n_;
+      const int64_t pr = pos_ < 0 ? 0 : (pos_ < p.P ? pos_ : p.P - 1);
+      const float* c_ = reinterpret_cast<const float*>(p.cos) + pr * p.scos[0] + 8 * g;
+      const float* s_ = reinterpret_cast<const float*>(p.sin) + pr * p.ssin[0] + 8 * g;
+      cp_async16(d + (3 * NJ + 0) * 32, c_);
+      cp_async16(d + (3 * NJ + 1) * 32, c_ + 4);
+      cp_async16(d + (3 * NJ + 2) * 32, s_);
+      cp_async16(d + (3 * NJ + 3) * 32, s_ + 4);
+    }
+  };
+  // tokens advance by nwarps: (b, n) are carried instead of divided per token
+  const int64_t tok0 = (int64_t)blockIdx.x * kTokWarps + (threadIdx.x >> 5);
+  const int step_b = (int)(nwarps / p.N), step_n = (int)(nwarps % p.N);
+  int nb = (int)(tok0 / p.N), nn = (int)(tok0 % p.N);
+  if (tok0 < total) prefetch(nb, nn, 0u);   // overlaps the weight staging below
+  // The gate and blend of head fin_h are finalized by this lane once per
+  // token: slot j = g of the token (g < NJ) belongs to that head.
+  const int fin_i = lane + 32 * g;
+  const bool fin_live = g < NJ && fin_i < slots;
+  const int fin_h = fin_live ? fin_i / GL : 0;
+  const float fin_gb = fin_live ? ld_any(p.gate_b, p.dt_gb, fin_h * p.sgb) : 0.f;
+  const float fin_mb = !fin_live || p.mix_out == nullptr ? 0.f
+                       : has_mix ? ld_any(p.mix_b, p.dt_mb, fin_h * p.smb) : ld_any(p.fixed_mix, p.dt_fm, fin_h * p.sfm);
   for (int i = threadIdx.x; i < H * 2 * D; i += blockDim.x) {
     const int hh = i / (2 * D), c = i % (2 * D);
     w_sm[(2 * hh) * PADROW + widx(c)] = ld_any(p.gate_w, p.dt_gw, hh * p.sgw[0] + c * p.sgw[1]);
     w_sm[(2 * hh + 1) * PADROW + widx(c)] = has_mix ? ld_any(p.mix_w, p.dt_mw, hh * p.smw[0] + c * p.smw[1]) : 0.f;
   }
   __syncthreads();
-  const int lane = threadIdx.x & 31;
-  const int g = lane % GL;                  // channel group of this lane within its head
-  const int64_t total = (int64_t)p.B * p.N;
-  const int64_t nwarps = (int64_t)gridDim.x * kTokWarps;
-  const int pbase = p.pos0_dev != nullptr ? *p.pos0_dev + p.pos0_dev_bias : p.pos0;
-  for (int64_t tok = (int64_t)blockIdx.x * kTokWarps + (threadIdx.x >> 5); tok < total; tok += nwarps) {
-    const int b = (int)(tok / p.N), n = (int)(tok % p.N);
+  for (int64_t tok = tok0; tok < total; tok += nwarps) {
+    const int b = nb, n = nn;
+    nn += step_n;
+    nb += step_b;
+    if (nn >= p.N) { nn -= p.N; ++nb; }
     T* qrow = reinterpret_cast<T*>(p.q) + b * p.sq[0] + (int64_t)n * p.sq[2];
     T* krow = reinterpret_cast<T*>(p.k) + b * p.sk[0] + (int64_t)n * p.sk[2];
-    const T* vrow = reinterpret_cast<const T*>(p.v) + b * p.sv[0] + (int64_t)n * p.sv[2];
     const int pos = pbase + n;
     const int prow = pos < 0 ? 0 : (pos < p.P ? pos : p.P - 1);
-    // this lane's channels are the same for every head: one table row read per token
+    cp_async_wait_all();   // this lane's copies of the token have landed
+    // this lane's channels are the same for every head: one table row per token
     float csv[RMAX > 0 ? 8 : 1], snv[RMAX > 0 ? 8 : 1];
+    uint32_t seen = 0;
     if constexpr (RMAX > 0) {
       if (p.rope && g < RMAX / 8) {
+        if (tab_async) {
+          const float4 c0 = *reinterpret_cast<const float4*>(stg + (3 * NJ + 0) * 32);
+          const float4 c1 = *reinterpret_cast<const float4*>(stg + (3 * NJ + 1) * 32);
+          const float4 s0 = *reinterpret_cast<const float4*>(stg + (3 * NJ + 2) * 32);
+          const float4 s1 = *reinterpret_cast<const float4*>(stg + (3 * NJ + 3) * 32);
+          csv[0] = c0.x; csv[1] = c0.y; csv[2] = c0.z; csv[3] = c0.w;
+          csv[4] = c1.x; csv[5] = c1.y; csv[6] = c1.z; csv[7] = c1.w;
+          snv[0] = s0.x; snv[1] = s0.y; snv[2] = s0.z; snv[3] = s0.w;
+          snv[4] = s1.x; snv[5] = s1.y; snv[6] = s1.z; snv[7] = s1.w;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          csv[e] = ld_any(p.cos, p.dt_cs, (int64_t)prow * p.scos[0] + (8 * g + e) * p.scos[1]);
-          snv[e] = ld_any(p.sin, p.dt_cs, (int64_t)prow * p.ssin[0] + (8 * g + e) * p.ssin[1]);
+          for (int e = 0; e < 8; ++e) seen ^= __float_as_uint(csv[e]) ^ __float_as_uint(snv[e]);
+        } else {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            csv[e] = ld_any(p.cos, p.dt_cs, (int64_t)prow * p.scos[0] + (8 * g + e) * p.scos[1]);
+            snv[e] = ld_any(p.sin, p.dt_cs, (int64_t)prow * p.ssin[0] + (8 * g + e) * p.ssin[1]);
+          }
         }
       }
     }
-    // every 16-byte slot of the token is requested before any is processed
     uint4 aq[NJ], ak[NJ], av[NJ];
 #pragma unroll
     for (int j = 0; j < NJ; ++j) {
       const int i = lane + 32 * j;
       aq[j] = ak[j] = av[j] = make_uint4(0, 0, 0, 0);
       if (i < slots) {
-        aq[j] = *reinterpret_cast<const uint4*>(qrow + 8 * i);
-        ak[j] = *reinterpret_cast<const uint4*>(krow + 8 * i);
-        if (p.cache_v != nullptr) av[j] = *reinterpret_cast<const uint4*>(vrow + 8 * i);
+        aq[j] = stg[(0 * NJ + j) * 32];
+        ak[j] = stg[(1 * NJ + j) * 32];
+        if (p.cache_v != nullptr) av[j] = stg[(2 * NJ + j) * 32];
       }
+      seen ^= aq[j].x ^ aq[j].y ^ aq[j].z ^ aq[j].w ^ ak[j].x ^ ak[j].y ^ ak[j].z ^ ak[j].w ^
+              av[j].x ^ av[j].y ^ av[j].z ^ av[j].w;
     }
+    // the next token's reads overwrite the stage only once every read above has returned
+    if (tok + nwarps < total) prefetch(nb, nn, seen & p.zero);
+    float fin_gs = 0.f, fin_ms = 0.f;
 #pragma unroll
     for (int j = 0; j < NJ; ++j) {
       // keeps the weight reads of one slot from being hoisted above another's
@@ -347,15 +428,7 @@ prep_tok_kernel(const PrepParams p) {
         gs += __shfl_xor_sync(0xffffffffu, gs, o);
         ms += __shfl_xor_sync(0xffffffffu, ms, o);
       }
-      if (live && g == 0) {
-        const float gt = gs + ld_any(p.gate_b, p.dt_gb, hh * p.sgb);
-        st_any(p.log_gamma, p.dt_lg, b * p.slg[0] + hh * p.slg[1] + (int64_t)n * p.slg[2],
-               -(fmaxf(gt, 0.f) + log1pf(expf(-fabsf(gt)))));
-        if (p.mix_out != nullptr) {
-          const float mlog = has_mix ? ms + ld_any(p.mix_b, p.dt_mb, hh * p.smb) : ld_any(p.fixed_mix, p.dt_fm, hh * p.sfm);
-          st_any(p.mix_out, p.dt_mo, b * p.smo[0] + hh * p.smo[1] + (int64_t)n * p.smo[2], 1.f / (1.f + expf(-mlog)));
-        }
-      }
+      if (g == j) { fin_gs = gs; fin_ms = ms; }   // every lane of the group holds the sums
       // rotate-half RoPE of channels [0, R): the partner of channel c is c +- R/2
       if constexpr (RMAX > 0) {
         float pq[8], pk[8];
@@ -404,6 +477,15 @@ prep_tok_kernel(const PrepParams p) {
         *reinterpret_cast<uint4*>(cv + 8 * g) = uv;
       }
     }
+    if (fin_live) {
+      const float gt = fin_gs + fin_gb;
+      st_any(p.log_gamma, p.dt_lg, b * p.slg[0] + fin_h * p.slg[1] + (int64_t)n * p.slg[2],
+             -(fmaxf(gt, 0.f) + log1pf(expf(-fabsf(gt)))));
+      if (p.mix_out != nullptr) {
+        const float mlog = (has_mix ? fin_ms : 0.f) + fin_mb;
+        st_any(p.mix_out, p.dt_mo, b * p.smo[0] + fin_h * p.smo[1] + (int64_t)n * p.smo[2], 1.f / (1.f + expf(-mlog)));
+      }
+    }
   }
 }
 
@@ -414,22 +496,26 @@ cudaError_t launch_t(const PrepParams& p, cudaStream_t st) {
     const bool tok = p.vec && p.sq[1] == p.D && p.sk[1] == p.D && (p.cache_v == nullptr || p.sv[1] == p.D) &&
                      p.H * p.D <= kTokMaxElems && (p.R == 0 || p.R == 8 || p.R == 16 || p.R == 32 || p.R == 64);
     if (tok && !getenv_flag_prep("HOFA_PREP_NO_TOKEN_MAJOR")) {
-      const size_t smem = (size_t)p.H * 2 * (2 * p.D + 2 * p.D / 8) * sizeof(float);
+      const size_t wbytes = (size_t)p.H * 2 * (2 * p.D + 2 * p.D / 8) * sizeof(float);
       int sms = 148;
       {
         int dev = 0;
         cudaGetDevice(&dev);
         cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
       }
+      // resident CTAs only (two per SM: registers), each walking its tokens with a grid stride
       const int64_t warps_needed = (int64_t)p.B * p.N;
-      const int64_t blocks = std::min<int64_t>((warps_needed + kTokWarps - 1) / kTokWarps, (int64_t)sms * 6);
+      const int64_t blocks = std::min<int64_t>((warps_needed + kTokWarps - 1) / kTokWarps, (int64_t)sms * 2);
+      PrepParams pk = p;
+      pk.zero = 0;
       bool launched = true;
       const int nj = (p.H * p.D / 8 + 31) / 32;
 #define HOFA_PREP_TOK_NJ(DD, RR, NJJ)                                                                          \
   {                                                                                                            \
     auto kk = prep_tok_kernel<T, DD, RR, NJJ>;                                                                 \
+    const size_t smem = wbytes + (size_t)kTokWarps * tok_stage_bytes<NJJ, RR>();                              \
     if (smem > 48 * 1024) cudaFuncSetAttribute(kk, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);    \
-    kk<<<(unsigned)blocks, kTokWarps * 32, smem, st>>>(p);                                                     \
+    kk<<<(unsigned)blocks, kTokWarps * 32, smem, st>>>(pk);                                                    \
   }
 #define HOFA_PREP_TOK(DD, RR)                                                                                  \
   else if (p.D == DD && p.R == RR) {                                                                           \
