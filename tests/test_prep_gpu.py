@@ -102,3 +102,49 @@ def test_prep_row_layouts(layout, D, r):
     assert (ck[:, :, pos0:pos0 + N].double().cpu() - ref_k[..., :r]).abs().max().item() <= tol * 4
     assert ck[:, :, :pos0].abs().max().item() == 0 and ck[:, :, pos0 + N:].abs().max().item() == 0
     assert torch.equal(cv[:, :, pos0:pos0 + N].cpu(), vd.cpu())
+
+
+@pytest.mark.parametrize("table", ["f32", "bf16", "strided"])
+def test_prep_token_major_many_tokens(table):
+    """More tokens than the token-major kernel has resident warps, so each warp
+    walks several tokens with its (b, n) carried across batch boundaries (N is
+    not a multiple of the warp count), and the RoPE tables either copied into
+    the shared-memory stage with the token (contiguous float32) or read
+    directly (bfloat16; float32 with channel stride 2)."""
+    from outlierneuronattention_b200.modules import RotaryEmbedding
+    from outlierneuronattention_b200.prep import prep
+    dtype = torch.bfloat16
+    g = torch.Generator().manual_seed(11)
+    B, H, D, r, N, pos0 = 3, 16, 64, 16, 3001, 13
+    L = N + pos0 + 7
+    x = torch.randn(B, N, 3, H, D, generator=g).to(dtype)
+    xd = x.cuda()
+    qd, kd, vd = (xd[:, :, i].transpose(1, 2) for i in range(3))
+    gw, mw = torch.randn(H, 2 * D, generator=g) * 0.3, torch.randn(H, 2 * D, generator=g) * 0.3
+    gb, mb = torch.randn(H, generator=g), torch.randn(H, generator=g)
+    ref_lg, ref_mix, ref_q, ref_k = reference(qd.cpu(), kd.cpu(), vd.cpu(), gw, gb, mw, mb, r, pos0)
+    rope = RotaryEmbedding(r, max_seq_len=L).cuda()
+    cos, sin = rope.cos_cached, rope.sin_cached
+    if table == "bf16":
+        cos, sin = cos.to(dtype), sin.to(dtype)
+    elif table == "strided":
+        wide_c = torch.zeros(cos.shape[0], 2 * r, device="cuda")
+        wide_s = torch.zeros_like(wide_c)
+        wide_c[:, ::2], wide_s[:, ::2] = cos, sin
+        cos, sin = wide_c[:, ::2], wide_s[:, ::2]
+        assert cos.stride(1) == 2
+    lg = torch.empty(B, H, N, device="cuda")
+    mix = torch.empty(B, H, N, device="cuda", dtype=dtype)
+    ck = torch.zeros(B, H, L, r, device="cuda", dtype=dtype)
+    cv = torch.zeros(B, H, L, D, device="cuda", dtype=dtype)
+    prep(qd, kd, vd, gw.cuda(), gb.cuda(), lg, mix_w=mw.cuda(), mix_b=mb.cuda(), mix_out=mix,
+         cos=cos, sin=sin, R=r, pos0=pos0, cache_k=ck, cache_v=cv, use_rope=True)
+    torch.cuda.synchronize()
+    tol = 2e-2
+    assert (lg.double().cpu() - ref_lg).abs().max().item() <= tol
+    assert (mix.double().cpu() - ref_mix).abs().max().item() <= tol
+    assert (qd.double().cpu() - ref_q).abs().max().item() <= tol * 4
+    assert (kd.double().cpu() - ref_k).abs().max().item() <= tol * 4
+    assert (ck[:, :, pos0:pos0 + N].double().cpu() - ref_k[..., :r]).abs().max().item() <= tol * 4
+    assert ck[:, :, :pos0].abs().max().item() == 0 and ck[:, :, pos0 + N:].abs().max().item() == 0
+    assert torch.equal(cv[:, :, pos0:pos0 + N].cpu(), vd.cpu())
