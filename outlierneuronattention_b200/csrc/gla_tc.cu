@@ -308,33 +308,41 @@ gla_tc_out_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
       sm100::tma_load_4d(sV + nb * kTile, &tv, 64 * nb, t0, h, b, &bars[0]);
     }
   }
-  // start state of this chunk -> bf16 MN-major operand (row j = 128 bytes per block, 128B swizzle)
+  // Every global read of the prologue is issued before the first shared-memory
+  // store: the stores go through generic pointers that the compiler cannot
+  // tell apart from the global sources, so a load placed after one waits for
+  // the round trips before it.
+  static_assert(D <= kThreads, "one gla_scale value per thread");
+  const int t = t0 + tid;
+  const float g = t < p.T ? ld_any(p.log_gamma, p.dt_lg, b * p.slg[0] + h * p.slg[1] + (int64_t)t * p.slg[2]) : 0.f;
+  float mix = 0.f;
+  if (p.fuse && t < p.T) mix = ld_any(p.mix_g, p.dt_mg, b * p.smg[0] + h * p.smg[1] + (int64_t)t * p.smg[2]);
+  const float gsv = tid < D && p.fuse ? ld_any(p.gla_scale, p.dt_gs, h * p.sgs[0] + tid * p.sgs[1]) : 1.f;
+  // start state of this chunk -> bf16 MN-major operand (row j = 128 bytes per block, 128B swizzle);
+  // each 64-channel block of the row is read into registers at once, then packed
   if (tid < 16 * KS) {
     const int j = tid;
     const float* src = p.ws_state + (((int64_t)bh * p.nseg + c) * J + j) * D;
 #pragma unroll
     for (int nb = 0; nb < Gm::NB; ++nb) {
+      float4 f[16];
+#pragma unroll
+      for (int q = 0; q < 16; ++q)
+        f[q] = j < J ? reinterpret_cast<const float4*>(src + nb * 64)[q] : make_float4(0.f, 0.f, 0.f, 0.f);
       uint4* row = reinterpret_cast<uint4*>(sS + nb * kTile + j * 128);
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
-        uint4 u = make_uint4(0, 0, 0, 0);
-        if (j < J) {
-          const float4 a = *reinterpret_cast<const float4*>(src + nb * 64 + q * 8);
-          const float4 bq = *reinterpret_cast<const float4*>(src + nb * 64 + q * 8 + 4);
-          u.x = pack2(a.x, a.y, BF16); u.y = pack2(a.z, a.w, BF16);
-          u.z = pack2(bq.x, bq.y, BF16); u.w = pack2(bq.z, bq.w, BF16);
-        }
+        const float4 a = f[2 * q], bq = f[2 * q + 1];
+        uint4 u;
+        u.x = pack2(a.x, a.y, BF16); u.y = pack2(a.z, a.w, BF16);
+        u.z = pack2(bq.x, bq.y, BF16); u.w = pack2(bq.z, bq.w, BF16);
         row[q ^ (j & 7)] = u;
       }
     }
   }
-  const int t = t0 + tid;
-  const float g = t < p.T ? ld_any(p.log_gamma, p.dt_lg, b * p.slg[0] + h * p.slg[1] + (int64_t)t * p.slg[2]) : 0.f;
   const float G = block_scan128(g, sm_warp, tid) * kLog2e;   // log2 units from here on
   sG[tid] = G;
-  for (int d = tid; d < D; d += kThreads) sGS[d] = p.fuse ? ld_any(p.gla_scale, p.dt_gs, h * p.sgs[0] + d * p.sgs[1]) : 1.f;
-  float mix = 0.f;
-  if (p.fuse && t < p.T) mix = ld_any(p.mix_g, p.dt_mg, b * p.smg[0] + h * p.smg[1] + (int64_t)t * p.smg[2]);
+  if (tid < D) sGS[tid] = gsv;
   fence_async_smem();
   volatile int* verr = err;
   if (!sm100::mbar_wait(&bars[0], 0)) atomicOr(err, 1);
