@@ -389,10 +389,17 @@ outlier_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
 
     // ---- epilogue: out = (accumulate ? out : 0) + mix * O / l --------------
     const bool store = row < p.Tq && !*verr;
-    const float mix = store ? ld_any(p.mix_g, p.dt_mg, b * p.smg[0] + h * p.smg[1] + (int64_t)row * p.smg[2]) : 0.f;
-    const float inv = l_sum > 0.f ? mix / l_sum : 0.f;
     T* og = reinterpret_cast<T*>(p.out) + b * p.so[0] + h * p.so[1] + (int64_t)(store ? row : 0) * p.so[2];
     const bool vec = p.so[3] == 1 && (reinterpret_cast<uintptr_t>(og) & 15u) == 0;
+    // the row's global reads in one round trip: its blend and, when accumulating,
+    // its current output (read per column chunk, each read would wait for the
+    // previous chunk's TMEM load and stores)
+    const float mix = store ? ld_any(p.mix_g, p.dt_mg, b * p.smg[0] + h * p.smg[1] + (int64_t)row * p.smg[2]) : 0.f;
+    uint4 oldv[D / 8];
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i)
+      oldv[i] = store && vec && p.accumulate ? reinterpret_cast<const uint4*>(og)[i] : make_uint4(0, 0, 0, 0);
+    const float inv = l_sum > 0.f ? mix / l_sum : 0.f;
 #pragma unroll
     for (int c = 0; c < D; c += 16) {
       uint32_t o[16];
@@ -401,11 +408,7 @@ outlier_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
       if (store && vec) {
         uint4* dst = reinterpret_cast<uint4*>(og + c);
         uint32_t w[8];
-        uint4 old[2] = {make_uint4(0, 0, 0, 0), make_uint4(0, 0, 0, 0)};
-        if (p.accumulate) {
-          old[0] = dst[0];
-          old[1] = dst[1];
-        }
+        const uint4 old[2] = {oldv[c / 8], oldv[c / 8 + 1]};   // zeros unless accumulating
         const uint32_t* ow = reinterpret_cast<const uint32_t*>(old);
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
