@@ -110,12 +110,21 @@ int hofa_decode_read_status(void* workspace, void* stream, int32_t* status_out);
  * args->workspace_bytes are ignored: the scratch is a 2 MiB array built into
  * the library (held on every GPU that loads it until exit), and calls needing
  * more (hofa_decode_workspace_size of their B, H, D and split count) fail with
- * HOFA_ERR_WORKSPACE.  All calls share that array, so calls that overlap on the
- * GPU race and must be serialised by the caller.  The first call on a device
- * looks up the array's address; make it before any stream capture.  Each call
- * clears the array's ticket and status words on `stream` before the kernel;
- * it never allocates. */
+ * HOFA_ERR_WORKSPACE.  All arguments are validated, and the split count
+ * chosen, exactly as hofa_decode_fwd does before anything is issued.  All
+ * calls share that array, so calls that overlap on the GPU race and must be
+ * serialised by the caller.  The first call on a device looks up the array's
+ * address; make it before any stream capture.  Each call clears the array's
+ * combine tickets on `stream` before the kernel; the status word keeps the
+ * bits of every call until hofa_decode_noalloc_read_status reads it.  It never
+ * allocates. */
 int hofa_decode_fwd_noalloc(const hofa_decode_args* args, void* stream);
+
+/* The status word of hofa_decode_fwd_noalloc's built-in scratch on the current
+ * device (the bits of hofa_decode_read_status, collected over every call since
+ * the last read), then clears it.  No counterpart in the reference.
+ * Synchronises `stream`; not for use inside graph capture. */
+int hofa_decode_noalloc_read_status(void* stream, int32_t* status_out);
 
 /* ------------------------------------------------------------------------ */
 /* Prefill, inlier path: chunked gated linear attention.                      */

@@ -130,10 +130,16 @@ int num_sms() {
   return g_num_sms[dev];
 }
 
-bool getenv_flag(const char* name) {
+// Tuning overrides for sweeps of the decode kernel, read once when the
+// library is loaded (never per launch).  Unset: the measured defaults below.
+int env_int(const char* name, int dflt) {
   const char* v = getenv(name);
-  return v != nullptr && v[0] != '\0' && v[0] != '0';
+  return (v != nullptr && v[0] != '\0') ? atoi(v) : dflt;
 }
+const bool kDecodeNoBulk = env_int("HOFA_DECODE_NO_BULK", 0) != 0;
+const int kDecodeWarps = env_int("HOFA_DECODE_WARPS", 4) == 8 ? 8 : 4;
+const bool kDecodeNoL2Prefetch = env_int("HOFA_DECODE_NO_L2_PREFETCH", 0) != 0;
+const int kDecodeStages = env_int("HOFA_DECODE_STAGES", 0);  // 0: choose by shape
 
 bool supported_d(int64_t D) { return D == 32 || D == 64 || D == 128; }
 
@@ -149,8 +155,11 @@ size_t round256(size_t x) { return (x + 255) & ~size_t(255); }
 namespace {
 
 // Validation of hofa_decode_args and the kernel parameters (shared by
-// hofa_decode_fwd and hofa_decode_step_fwd).
-int decode_setup(const hofa_decode_args* a, hofa::DecodeParams& p, int& path, bool& alpha, int& dt) {
+// hofa_decode_fwd, hofa_decode_step_fwd and the no-allocation entry point).
+// With check_ws == false the workspace fields are not looked at (p.split_k
+// and the size the workspace would need still come out).
+int decode_setup(const hofa_decode_args* a, hofa::DecodeParams& p, int& path, bool& alpha, int& dt,
+                 bool check_ws = true, size_t* ws_need = nullptr) {
   if (a == nullptr) return fail(HOFA_ERR_INVALID_ARGUMENT, "args is NULL");
   const int64_t B = a->q.shape[0], H = a->q.shape[1], D = a->q.shape[3];
   CHECK(a->q, "q", 4, -1, -1, 1, -1);
@@ -210,9 +219,12 @@ int decode_setup(const hofa_decode_args* a, hofa::DecodeParams& p, int& path, bo
   if (split > kMaxSplit) return fail(HOFA_ERR_INVALID_ARGUMENT, "split_k=%d above %d", split, kMaxSplit);
   if (R == 0) split = 1;
   const size_t need = hofa_decode_workspace_size((int)B, (int)H, (int)D, split);
-  if (a->workspace == nullptr || a->workspace_bytes < need)
-    return fail(HOFA_ERR_WORKSPACE, "decode workspace needs %zu bytes, got %zu", need, a->workspace_bytes);
-  if (!aligned16(a->workspace)) return fail(HOFA_ERR_MISALIGNED, "workspace must be 16-byte aligned");
+  if (ws_need != nullptr) *ws_need = need;
+  if (check_ws) {
+    if (a->workspace == nullptr || a->workspace_bytes < need)
+      return fail(HOFA_ERR_WORKSPACE, "decode workspace needs %zu bytes, got %zu", need, a->workspace_bytes);
+    if (!aligned16(a->workspace)) return fail(HOFA_ERR_MISALIGNED, "workspace must be 16-byte aligned");
+  }
 
   p.q = a->q.data; p.k = a->k.data; p.v = a->v.data;
   p.cache_k = a->cache_k.data; p.cache_v = a->cache_v.data;
@@ -248,7 +260,7 @@ int decode_setup(const hofa_decode_args* a, hofa::DecodeParams& p, int& path, bo
     }
   }
   // TMA bulk path: additionally, every (b,h) slab of cache rows is contiguous
-  const bool bulk = vec && a->cache_k.stride[2] == R && a->cache_v.stride[2] == D && !getenv_flag("HOFA_DECODE_NO_BULK");
+  const bool bulk = vec && a->cache_k.stride[2] == R && a->cache_v.stride[2] == D && !kDecodeNoBulk;
   path = bulk ? 2 : (vec ? 1 : 0);
   // bulk ring: 64-token slots; a slot is always consumed by the same warp,
   // which requires stages % consumer_warps == 0
@@ -264,22 +276,22 @@ int decode_setup(const hofa_decode_args* a, hofa::DecodeParams& p, int& path, bo
     const int64_t per_sm8 = (int64_t)(228 * 1024 / (ring8 + 12 * 1024));
     if ((int64_t)B * H * split > (per_sm8 > 0 ? per_sm8 : 1) * (int64_t)sms) p.stages = 4;
   }
-  if (const char* v = getenv("HOFA_DECODE_WARPS")) p.consumer_warps = atoi(v) == 8 ? 8 : 4;
+  p.consumer_warps = kDecodeWarps;
   // L2 prefetch before the grid dependency only for small steps (up to 24 MB
   // of cache rows: measured faster at B = 1 and 2 of the 4096-token config,
   // slower at B = 4, whose 42 MB step keeps HBM busy without it)
-  p.no_l2_prefetch = getenv_flag("HOFA_DECODE_NO_L2_PREFETCH") ||
-                     (double)B * H * (a->seq_len_dev ? L : a->seq_len) * (R + D) * es > 24e6;
-  if (const char* v = getenv("HOFA_DECODE_STAGES")) {
-    const int n = atoi(v);
-    if (n >= 2 && n <= 16) p.stages = n;
-  }
+  p.no_l2_prefetch = kDecodeNoL2Prefetch || (double)B * H * (a->seq_len_dev ? L : a->seq_len) * (R + D) * es > 24e6;
+  if (kDecodeStages >= 2 && kDecodeStages <= 16) p.stages = kDecodeStages;
   p.stages = ((p.stages + p.consumer_warps - 1) / p.consumer_warps) * p.consumer_warps;
-  while (p.stages > p.consumer_warps && (size_t)p.stages * 64 * (R + D) * es > 200 * 1024) p.stages -= p.consumer_warps;
-  if (p.stages > 16 || (size_t)p.stages * 64 * (R + D) * es > 200 * 1024) {
+  const size_t ring_budget = 200 * 1024;  // dynamic shared memory of the ring (the kernel adds ~12 KB static)
+  while (p.stages > p.consumer_warps && (size_t)p.stages * 64 * (R + D) * es > ring_budget) p.stages -= p.consumer_warps;
+  if (p.stages > 16 || (size_t)p.stages * 64 * (R + D) * es > ring_budget) {
     p.consumer_warps = 4;
     p.stages = 4;
   }
+  // rows too wide for even a 4-slot ring (float32 with large R at d_h = 128):
+  // stream with 16-byte register loads instead
+  if (path == 2 && (size_t)p.stages * 64 * (R + D) * es > ring_budget) path = 1;
   return HOFA_OK;
 }
 
@@ -393,6 +405,20 @@ namespace hofa {
 int set_last_error(int code, const char* message) {
   g_err = message;
   return code;
+}
+
+// Validates `a` exactly as hofa_decode_fwd does, except for the workspace
+// fields, and returns the split count hofa_decode_fwd will launch with and
+// the workspace bytes that split needs (for the no-allocation entry point,
+// which sizes its built-in scratch with this before touching the device).
+int decode_plan(const hofa_decode_args* a, int32_t* split, size_t* ws_need) {
+  DecodeParams p;
+  int path = 0, dt = 0;
+  bool alpha = false;
+  const int st = decode_setup(a, p, path, alpha, dt, /*check_ws=*/false, ws_need);
+  if (st != HOFA_OK) return st;
+  *split = p.split_k;
+  return HOFA_OK;
 }
 }  // namespace hofa
 
@@ -696,7 +722,7 @@ int hofa_decode_step_fwd(const hofa_decode_args* d, const hofa_prep_args* pr, vo
   st = decode_setup(&da, dp, path, alpha, dt);
   if (st != HOFA_OK) return st;
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  const bool fuse = path == 2 && dp.R > 0 && pdt == dt && !getenv_flag("HOFA_DECODE_STEP_UNFUSED");
+  const bool fuse = path == 2 && dp.R > 0 && pdt == dt;
   if (!fuse) {  // the same computation as two launches
     cudaError_t e = hofa::launch_prep(pp, pdt, s);
     if (e != cudaSuccess) return cuda_fail(e, "hofa_decode_step_fwd prep launch");

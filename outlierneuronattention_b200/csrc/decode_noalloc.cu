@@ -13,18 +13,25 @@
 // Limits and behaviour:
 //   * the scratch is kNoAllocScratchBytes (2 MiB) of static device memory;
 //     every GPU that loads the library holds it until the process exits;
-//   * calls whose shapes need more scratch (hofa_decode_workspace_size() of
-//     B, H, D and the split count in use) are rejected with
-//     HOFA_ERR_WORKSPACE and a message naming both sizes;
+//   * the arguments are validated exactly as hofa_decode_fwd validates them,
+//     and the split count is the one hofa_decode_fwd will launch with
+//     (hofa::decode_plan), before anything is issued on the device; calls
+//     whose shapes need more scratch (hofa_decode_workspace_size() of B, H,
+//     D and that split count) are rejected with HOFA_ERR_WORKSPACE and a
+//     message naming both sizes;
 //   * all calls share the one array: calls that overlap on the GPU (two
 //     streams, or two host threads) race on it and must be serialised by the
 //     caller;
 //   * the first call on a device looks up the array's device address with
 //     cudaGetSymbolAddress (with that device current) and caches it; make that
 //     first call before any stream capture;
-//   * the ticket and status words must start at zero; every call clears them
-//     (an asynchronous memset on the caller's stream) before the kernel runs,
-//     so nothing left by an earlier call can leak into the next one;
+//   * the per-head tickets of the combine must start at zero; every call
+//     clears them (an asynchronous memset on the caller's stream) before the
+//     kernel runs, so a ticket left by an interrupted earlier call cannot leak
+//     into the next one;
+//   * the status word (device-side faults: a clamped seq_len_dev, a ring or
+//     combine wait that ran out) collects the bits of every call since it was
+//     last read; hofa_decode_noalloc_read_status() returns and clears it;
 //   * no cudaMalloc, cudaFree or other allocating routine is called.
 #include <cuda_runtime.h>
 
@@ -34,12 +41,14 @@
 #include "../../include/hofa.h"
 
 namespace hofa {
-int set_last_error(int code, const char* message);  // capi.cu
+int set_last_error(int code, const char* message);                            // capi.cu
+int decode_plan(const hofa_decode_args* a, int32_t* split, size_t* ws_need);  // capi.cu
 }
 
 namespace {
 
 constexpr size_t kNoAllocScratchBytes = 2u << 20;
+constexpr size_t kTicketOffset = 256;  // the status word sits at offset 0, tickets from here
 
 static __device__ __align__(256) unsigned char g_decode_scratch[kNoAllocScratchBytes];
 
@@ -68,39 +77,39 @@ int scratch_address(void** out) {
 }  // namespace
 
 extern "C" int hofa_decode_fwd_noalloc(const hofa_decode_args* args, void* stream) {
-  if (args == nullptr) return hofa_decode_fwd(args, stream);
-  hofa_decode_args a = *args;
-  const int64_t B = a.q.shape[0], H = a.q.shape[1], D = a.q.shape[3];
-  size_t zero_bytes = 256;
-  if (a.q.ndim == 4 && B > 0 && H > 0 && D > 0) {
-    // the split this call will use, chosen exactly as hofa_decode_fwd chooses it
-    int split = a.split_k;
-    if (split <= 0) {
-      int dev = 0, sms = 148;
-      if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-      const int len_hint = a.seq_len_dev != nullptr && a.cache_k.ndim == 4 ? (int)a.cache_k.shape[2] : a.seq_len;
-      split = hofa_decode_choose_split((int32_t)B, (int32_t)H, len_hint, sms);
-    }
-    if (a.R == 0) split = 1;
-    const size_t need = (B * H > ((int64_t)1 << 24)) ? (size_t)-1
-                                                     : hofa_decode_workspace_size((int32_t)B, (int32_t)H, (int32_t)D, split);
-    if (need > kNoAllocScratchBytes) {
-      char msg[256];
-      snprintf(msg, sizeof(msg),
-               "hofa_decode_fwd_noalloc: this call needs %zu bytes of scratch (B=%lld, H=%lld, D=%lld, split_k=%d) "
-               "but the built-in array holds %zu; pass a workspace to hofa_decode_fwd instead",
-               need, (long long)B, (long long)H, (long long)D, split, kNoAllocScratchBytes);
-      return hofa::set_last_error(HOFA_ERR_WORKSPACE, msg);
-    }
-    a.split_k = split;
-    zero_bytes = 256 + (((size_t)B * (size_t)H * sizeof(int) + 255) & ~size_t(255));  // status word + tickets
+  if (args == nullptr) return hofa::set_last_error(HOFA_ERR_INVALID_ARGUMENT, "args is NULL");
+  int32_t split = 0;
+  size_t need = 0;
+  int st = hofa::decode_plan(args, &split, &need);  // all argument checks, nothing issued yet
+  if (st != HOFA_OK) return st;
+  if (need > kNoAllocScratchBytes) {
+    char msg[256];
+    snprintf(msg, sizeof(msg),
+             "hofa_decode_fwd_noalloc: this call needs %zu bytes of scratch (B=%lld, H=%lld, D=%lld, split_k=%d) "
+             "but the built-in array holds %zu; pass a workspace to hofa_decode_fwd instead",
+             need, (long long)args->q.shape[0], (long long)args->q.shape[1], (long long)args->q.shape[3], split,
+             kNoAllocScratchBytes);
+    return hofa::set_last_error(HOFA_ERR_WORKSPACE, msg);
   }
   void* scratch = nullptr;
-  const int st = scratch_address(&scratch);
+  st = scratch_address(&scratch);
   if (st != HOFA_OK) return st;
-  const cudaError_t e = cudaMemsetAsync(scratch, 0, zero_bytes, reinterpret_cast<cudaStream_t>(stream));
+  const size_t heads = (size_t)args->q.shape[0] * (size_t)args->q.shape[1];
+  const size_t ticket_bytes = (heads * sizeof(int) + 255) & ~size_t(255);
+  const cudaError_t e = cudaMemsetAsync(static_cast<char*>(scratch) + kTicketOffset, 0, ticket_bytes,
+                                        reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return hofa::set_last_error(HOFA_ERR_CUDA, cudaGetErrorString(e));
+  hofa_decode_args a = *args;
+  a.split_k = split;  // the split the scratch was sized for
   a.workspace = scratch;
   a.workspace_bytes = kNoAllocScratchBytes;
   return hofa_decode_fwd(&a, stream);
+}
+
+extern "C" int hofa_decode_noalloc_read_status(void* stream, int32_t* status_out) {
+  if (status_out == nullptr) return hofa::set_last_error(HOFA_ERR_INVALID_ARGUMENT, "status_out is NULL");
+  void* scratch = nullptr;
+  const int st = scratch_address(&scratch);
+  if (st != HOFA_OK) return st;
+  return hofa_decode_read_status(scratch, stream, status_out);
 }

@@ -62,6 +62,10 @@ constexpr int kSoftmaxWarps = 4;
 constexpr int kThreads = 32 * (kSoftmaxWarps + 1);
 constexpr int kStages = 4;         // K and V ring depth
 constexpr int kEmuDefault = 2;     // of the 16 exp2 pairs of a full half-tile, this many run on the FMA pipe (measured best)
+const int kEmuSetting = [] {
+  const char* v = getenv("HOFA_OUTLIER_EMU");
+  return v != nullptr && v[0] != '\0' ? atoi(v) : kEmuDefault;
+}();
 
 // TMEM columns: the S/P buffer in [0, kKeys), O in [kKeys, kKeys + D), rounded up to a power of two
 template <int D>
@@ -521,11 +525,11 @@ cudaError_t launch_dr(const OutlierParams& p, cudaStream_t st, bool* taken) {
   if (!make_map(&mk, p.k, bf16, R, p.Tk, p.H, p.B, sk, R, kKeys, qk_swz)) return cudaSuccess;
   if (!make_map(&mv, p.v, bf16, D, p.Tk, p.H, p.B, sv, 64, kKeys, CU_TENSOR_MAP_SWIZZLE_128B)) return cudaSuccess;
   dim3 grid((unsigned)((p.Tq + kRows - 1) / kRows) * p.H * p.B);
-  // HOFA_OUTLIER_EMU (0..4) overrides how many of the 16 exp2 pairs of a
-  // full half-tile run as the FMA-pipe polynomial (bf16, head dim 64, r = 16)
+  // HOFA_OUTLIER_EMU (0..4, read once at library load) overrides how many of
+  // the 16 exp2 pairs of a full half-tile run as the FMA-pipe polynomial
+  // (bf16, head dim 64, r = 16)
   if constexpr (std::is_same<T, __nv_bfloat16>::value && D == 64 && R == 16) {
-    const char* emu = getenv("HOFA_OUTLIER_EMU");
-    const int e = emu != nullptr && emu[0] != '\0' ? atoi(emu) : kEmuDefault;
+    const int e = kEmuSetting;
     if (e == 0) return launch_kernel<T, D, R, 0>(mq, mk, mv, p, grid, st, taken);
     if (e == 1) return launch_kernel<T, D, R, 1>(mq, mk, mv, p, grid, st, taken);
     if (e == 2) return launch_kernel<T, D, R, 2>(mq, mk, mv, p, grid, st, taken);

@@ -25,9 +25,23 @@ namespace hofa {
 
 namespace {
 
-bool getenv_flag_prep(const char* name) {
-  const char* v = getenv(name);
+// HOFA_PREP_NO_TOKEN_MAJOR (read once at library load) turns the token-major
+// kernel off, for comparisons.
+const bool kPrepNoTokenMajor = [] {
+  const char* v = getenv("HOFA_PREP_NO_TOKEN_MAJOR");
   return v != nullptr && v[0] != '\0' && v[0] != '0';
+}();
+
+int sm_count() {
+  static int cached[64] = {};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
+  if (cached[dev] == 0) {
+    int n = 0;
+    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+    cached[dev] = n;
+  }
+  return cached[dev];
 }
 
 constexpr int kPrepWarps = 8;
@@ -495,14 +509,9 @@ cudaError_t launch_t(const PrepParams& p, cudaStream_t st) {
     // token-major kernel: each token's heads are adjacent (head stride D) in q, k and v
     const bool tok = p.vec && p.sq[1] == p.D && p.sk[1] == p.D && (p.cache_v == nullptr || p.sv[1] == p.D) &&
                      p.H * p.D <= kTokMaxElems && (p.R == 0 || p.R == 8 || p.R == 16 || p.R == 32 || p.R == 64);
-    if (tok && !getenv_flag_prep("HOFA_PREP_NO_TOKEN_MAJOR")) {
+    if (tok && !kPrepNoTokenMajor) {
       const size_t wbytes = (size_t)p.H * 2 * (2 * p.D + 2 * p.D / 8) * sizeof(float);
-      int sms = 148;
-      {
-        int dev = 0;
-        cudaGetDevice(&dev);
-        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-      }
+      const int sms = sm_count();
       // resident CTAs only (two per SM: registers), each walking its tokens with a grid stride
       const int64_t warps_needed = (int64_t)p.B * p.N;
       const int64_t blocks = std::min<int64_t>((warps_needed + kTokWarps - 1) / kTokWarps, (int64_t)sms * 2);

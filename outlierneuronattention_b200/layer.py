@@ -79,24 +79,6 @@ class HybridOutlierFactorizedAttention(nn.Module):
         self.gla_scale = nn.Parameter(torch.ones(1, self.num_heads, 1, self.d_head))
 
     # ------------------------------------------------------------------ helpers
-    def _compute_gates_optimized(self, Q, K):
-        """Gate logits and mix gate from the un-rotated Q, K (reference :67-95),
-        in PyTorch; the hybrid paths compute the same inside ``hofa_prep_fwd``."""
-        W_g = self.gate_proj.weight
-        W_g_q, W_g_k = W_g.chunk(2, dim=1)
-        bias = self.gate_proj.bias.view(1, self.num_heads, 1).to(Q.dtype)
-        gate_logits = torch.einsum("bhnf,hf->bhn", Q, W_g_q) + torch.einsum("bhnf,hf->bhn", K, W_g_k) + bias
-        if hasattr(self, "mix_proj"):
-            W_m_q, W_m_k = self.mix_proj.weight.chunk(2, dim=1)
-            bias_m = self.mix_proj.bias.view(1, self.num_heads, 1).to(Q.dtype)
-            mix_logits = torch.einsum("bhnf,hf->bhn", Q, W_m_q) + torch.einsum("bhnf,hf->bhn", K, W_m_k) + bias_m
-            mix_g = torch.sigmoid(mix_logits).to(Q.dtype).unsqueeze(-1)
-        elif hasattr(self, "fixed_mix"):
-            mix_g = torch.sigmoid(self.fixed_mix).to(Q.dtype).expand(Q.shape[0], -1, Q.shape[2], -1)
-        else:
-            mix_g = None
-        return gate_logits.unsqueeze(-1), mix_g
-
     def _qkv_weight(self):
         """[W_q / d_h^(1/4); W_k / d_h^(1/4); W_v] as one [3*H*d_h, d_model]
         weight (the reference's scaling, :100-104, folded in fp32), rebuilt

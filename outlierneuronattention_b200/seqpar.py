@@ -1,6 +1,6 @@
 """Sequence-sharded prefill of the HOFA attention core (long contexts over N GPUs).
 
-A long prompt (B=1, T=65536) is cut into 2N equal blocks
+A long prompt (e.g. B=1, T=65536 tokens) is cut into 2N equal blocks
 and rank r owns blocks r and 2N-1-r ("zig-zag"), so that every rank gets the
 same amount of causal attention work.  One exchange step per layer, one
 process per GPU over ``torch.distributed`` (NCCL on GPUs):

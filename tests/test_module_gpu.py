@@ -23,7 +23,8 @@ def make_layer(g, dtype=torch.float32):
     c = g["config"]
     cfg = ModelConfig(d_model=c["d_model"], num_heads=c["num_heads"], num_layers=1, r=c["r"],
                       chunk_size=c["chunk_size"], use_rope=c["use_rope"], rope_base=c["rope_base"],
-                      learnable_alpha=c["learnable_alpha"], fixed_blend_weight=c["fixed_blend_weight"])
+                      learnable_alpha=c["learnable_alpha"], fixed_blend_weight=c["fixed_blend_weight"],
+                      mha_heads_for_width_split=c.get("mha_heads_for_width_split", 0))
     m = HybridOutlierFactorizedAttention(cfg)
     missing, unexpected = m.load_state_dict(g["state_dict"], strict=True), None
     return m.to(device="cuda", dtype=dtype).eval()
@@ -60,6 +61,45 @@ def test_prefill_then_preallocated_decode_fp32(name):
         if r > 0:
             assert err(cache[0], g["cache_k"]) <= 1e-4
             assert err(cache[1], g["cache_v"]) <= 1e-4
+
+
+@pytest.mark.parametrize("name", ["mha_r_eq_dh", "width_split"])
+@pytest.mark.parametrize("mode", ["preallocated", "concat", "from_empty"])
+def test_ablation_branches_fp32(name, mode):
+    """The reference's ablation branches against its own outputs: r == d_head
+    (plain causal softmax attention, src/HybridOutlierFactorizedAttention.py:161-171,
+    :333-356) and the width split (softmax heads beside GLA heads, :106-143,
+    :234-296); prefill of 50 tokens then decode in each cache mode (or decode
+    from no cache at all)."""
+    g = load_golden(name)
+    m = make_layer(g)
+    x = g["x"].cuda()
+    B, T, _ = x.shape
+    T0 = 0 if mode == "from_empty" else 50
+    cache, state, ys = None, None, []
+    with torch.no_grad():
+        if T0:
+            y0, cache, state = m(x[:, :T0], return_state=True)
+            assert err(y0, g["y"][:, :T0]) <= 1e-4
+            if g["states"]:
+                assert err(state[0], g["states"][T0]) <= 1e-4
+            else:
+                assert state is None
+            ys.append(y0)
+            if mode == "preallocated":
+                Kc = torch.zeros(B, cache[0].shape[1], T, cache[0].shape[3], device="cuda")
+                Vc = torch.zeros(B, cache[1].shape[1], T, cache[1].shape[3], device="cuda")
+                Kc[:, :, :T0], Vc[:, :, :T0] = cache
+                cache = (Kc, Vc)
+        for t in range(T0, T):
+            y, cache, state = m.forward_step(x[:, t:t + 1], cache, state,
+                                             cache_seq_len=t if mode == "preallocated" else None)
+            ys.append(y)
+    assert err(torch.cat(ys, 1), g["y"]) <= 1e-4
+    assert err(cache[0][:, :, :T], g["cache_k"]) <= 1e-4
+    assert err(cache[1][:, :, :T], g["cache_v"]) <= 1e-4
+    if g["states"]:
+        assert err(state[0], g["states"][T]) <= 1e-4
 
 
 @pytest.mark.parametrize("name", ["hofa_r16", "hofa_r16_alpha", "gla_r0"])
