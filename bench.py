@@ -258,6 +258,10 @@ def run_ours(args):
         torch.cuda.synchronize()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         t_timed0 = time.time()
+        # an untimed lead-in replay keeps the GPU busy while e0 and the timed
+        # graph launches are enqueued, so no host launch latency falls between
+        # e0 and the first timed step
+        run(chunk)
         e0.record(stream)
         run(args.steps)
         e1.record(stream)
@@ -269,9 +273,12 @@ def run_ours(args):
     clocks = sampler.stop(t_timed0 if t_timed1 - t_timed0 > 0.15 else t_load0, t_timed1)
     ms = e0.elapsed_time(e1)
     ms_t = torch.tensor([ms], device=dev)
+    per_rank = [ms]
     if world > 1:
-        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
-    ms_max = ms_t.item()
+        all_ms = torch.empty(world, device=dev)
+        dist.all_gather_into_tensor(all_ms, ms_t)
+        per_rank = all_ms.tolist()
+    ms_max = max(per_rank)
     ms_step = ms_max / args.steps
     value = B * world * args.steps / (ms_max / 1e3)
 
@@ -375,7 +382,8 @@ def run_ours(args):
                    "api": "C ABI hofa_decode_fwd with pre-packed hofa_decode_args (ctypes), one staged H2D copy "
                           "and the D2H copy of Y by cudaMemcpyAsync, cudaStreamSynchronize and a host read of Y every "
                           "step; rotating cache sets (no L2 reuse)"},
-           "gpu_launches": args.steps, "clocks": clocks}
+           "gpu_launches": args.steps, "clocks": clocks,
+           "per_rank_us_per_step": [round(1e3 * m / args.steps, 3) for m in per_rank]}
     if not args.no_prefill:
         out["prefill"] = measure_prefill(dev)
     if not args.no_config4 and world == 1:
@@ -383,7 +391,10 @@ def run_ours(args):
         out["layer_step"] = [measure_layer_step(dev, B=1), measure_layer_step(dev, B=4)]
         out["decode_batches"] = [measure_decode_batch(dev, 1), measure_decode_batch(dev, 64, steps=50)]
     if not args.no_config4 and world > 1:
-        out["config4_seqpar"] = measure_seqpar(dev, world)
+        sp = measure_seqpar(dev, world)
+        out["config4_seqpar"] = sp.pop("summary")
+        out["decode_head_sharded"] = [measure_decode_head_sharded(dev, world, B=1),
+                                      measure_config4_decode_head_sharded(dev, world, sp)]
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(B, args.cpu_seconds)
     if world > 1:
@@ -569,50 +580,224 @@ def measure_config4(dev, steps=64, reps=3):
 
 def measure_seqpar(dev, world, steps=3, warmup=2):
     """BASELINE config 4 prefill of the attention core (B=1, T=65536)
-    sequence-sharded over the ranks (zig-zag blocks; two GLA passes around
-    the block-state exchange, outlier attention against the all-gathered key
-    prefix).  Each rank draws its own tokens; the time per prefill is the max
-    over ranks of CUDA-event times around the whole sharded core, exchange
-    included."""
+    sequence-sharded over the ranks (zig-zag blocks; two batched GLA passes
+    around the block-state exchange, outlier attention against the key prefix
+    that NCCL point-to-point transfers fill in during the GLA passes).  Every
+    rank draws the same whole-sequence inputs and takes its two blocks; the
+    time per prefill is the max over ranks of CUDA-event times around the
+    whole sharded core, exchange included, with a per-phase breakdown (median
+    over the timed runs, max over ranks).  After timing, each rank checks its
+    output rows and the final GLA state against a one-GPU run of the same
+    operators over the whole sequence (``parity_maxabs``, max over ranks)."""
     import torch.distributed as dist
     from outlierneuronattention_b200 import seqpar
+    from outlierneuronattention_b200.chunk_gla_inlier import gla_forward
+    from outlierneuronattention_b200.exact_attention import exact_attention_triton
     B4, T4 = 1, 65536
     rank = dist.get_rank()
-    g = torch.Generator(device=dev).manual_seed(21 + rank)
-    Tl = T4 // world
-    x3 = torch.randn(B4, Tl, 3, H, D, device=dev, generator=g).to(torch.bfloat16)
-    q, k, v = (x3[:, :, i].transpose(1, 2) for i in range(3))
-    lg = torch.nn.functional.logsigmoid(torch.randn(B4, H, Tl, device=dev, generator=g)) / 16
-    mix = torch.sigmoid(torch.randn(B4, H, Tl, device=dev, generator=g)).to(torch.bfloat16)
+    g = torch.Generator(device=dev).manual_seed(21)
+    x3 = torch.randn(B4, T4, 3, H, D, device=dev, generator=g).to(torch.bfloat16)
+    qf, kf, vf = (x3[:, :, i].transpose(1, 2) for i in range(3))
+    lgf = torch.nn.functional.logsigmoid(torch.randn(B4, H, T4, device=dev, generator=g) + 2.0) / 16
+    mixf = torch.sigmoid(torch.randn(B4, H, T4, device=dev, generator=g)).to(torch.bfloat16)
+    take = lambda x: seqpar.shard_tokens(x, world, rank, dim=2).contiguous()
+    q, k, v, lg, mix = take(qf), take(kf), take(vf), take(lgf), take(mixf)
     gs = torch.ones(1, H, 1, D, device=dev)
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    times = []
+    times, phases = [], []
     for it in range(warmup + steps):
         dist.barrier()
         torch.cuda.synchronize()
+        timer = seqpar.PhaseTimer()
         e0.record()
-        seqpar.sharded_attention_core(q, k, v, lg, mix, R, 2.0, gs, T4)
+        Y, S_end = seqpar.sharded_attention_core(q, k, v, lg, mix, R, 2.0, gs, T4, timer=timer)
         e1.record()
         torch.cuda.synchronize()
         if it >= warmup:
             times.append(e0.elapsed_time(e1))
-    t = torch.tensor([statistics.median(times)], device=dev)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = t.item()
-    return {"workload": f"config4-prefill-seqpar-B{B4}-T{T4}", "ranks": world, "ms": round(ms, 4),
-            "tokens_per_s": round(B4 * T4 / (ms / 1e3), 1),
-            "sharding": f"zig-zag: {2 * world} blocks of {T4 // (2 * world)} tokens, rank r owns r and {2 * world - 1}-r",
-            "exchange": "NCCL all_gather of K_O/V (async, overlaps the first GLA pass) and of GLA block states",
-            "timed": "gla (2 passes) + exchange + outlier attention, max over ranks"}
+            phases.append(timer.ms())
+    names = list(phases[0].keys())
+    ph = torch.tensor([statistics.median(p[n] for p in phases) for n in names] + [statistics.median(times)],
+                      device=dev)
+    dist.all_reduce(ph, op=dist.ReduceOp.MAX)
+    ms = ph[-1].item()
+    # parity against the one-GPU path over the whole sequence
+    Yf = torch.empty(B4, H, T4, D, device=dev, dtype=torch.bfloat16)
+    Sf = torch.empty(B4, H, J, D, device=dev)
+    gla_forward(qf, kf, vf, lgf, R, mix_g=mixf, gla_scale=gs, y=Yf, state_out=Sf)
+    exact_attention_triton(qf, kf, vf, R, 2.0, mixf, out=Yf)
+    err = torch.tensor([(Y.float() - take(Yf).float()).abs().max().item(), (S_end - Sf).abs().max().item()],
+                       device=dev)
+    dist.all_reduce(err, op=dist.ReduceOp.MAX)
+    summary = {"workload": f"config4-prefill-seqpar-B{B4}-T{T4}", "ranks": world, "ms": round(ms, 4),
+               "tokens_per_s": round(B4 * T4 / (ms / 1e3), 1),
+               "phase_ms_max_over_ranks": {n: round(ph[i].item(), 4) for i, n in enumerate(names)},
+               "parity_maxabs": {"y": err[0].item(), "final_state": err[1].item(),
+                                 "against": "one GPU, same operators, whole sequence"},
+               "sharding": f"zig-zag: {2 * world} blocks of {T4 // (2 * world)} tokens, rank r owns r and {2 * world - 1}-r",
+               "exchange": "NCCL isend/irecv of K_O/V blocks into token-major full-sequence buffers (overlaps the "
+                           "GLA passes); all_gather of the GLA block states",
+               "timed": "pack + GLA (2 batched passes) + exchange + outlier attention (2 streams), max over ranks"}
+    del x3, Yf
+    return {"summary": summary, "q": q, "k": k, "v": v, "S_end": S_end, "kf": kf, "vf": vf, "T": T4}
+
+
+def _decode_graph_time(launch, nsteps, reps, stream):
+    """CUDA-event time per step of `nsteps` launches captured in one graph,
+    replayed `reps` times behind an untimed lead-in replay."""
+    with torch.cuda.stream(stream):
+        launch()
+        stream.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            launch()
+        graph.replay()
+        stream.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        graph.replay()
+        e0.record(stream)
+        for _ in range(reps):
+            graph.replay()
+        e1.record(stream)
+        stream.synchronize()
+    us = e0.elapsed_time(e1) * 1e3 / (reps * nsteps)
+    del graph
+    return us
+
+
+def measure_decode_head_sharded(dev, world, B=1, steps=200, reps=3):
+    """Config-1 decode (L=4096) with the heads split over the ranks: rank g
+    runs the attention core of heads [16g/N, 16(g+1)/N) for all B sequences
+    (no collective).  One decode step of the B sequences uses all N GPUs, so
+    tokens/s = B / (max over ranks of the step time); each rank streams the
+    caches of its heads from HBM (rotating sets larger than 3 x L2)."""
+    import torch.distributed as dist
+    from outlierneuronattention_b200 import _capi
+    from outlierneuronattention_b200.hofa_decode import decode_args, decode_workspace
+    from outlierneuronattention_b200.seqpar import head_range
+    rank = dist.get_rank()
+    h0, h1 = head_range(H, world, rank)
+    Hg = h1 - h0
+    per_set = B * Hg * (L * (R + D) * 2 + J * D * 4 * 2)
+    nsets = max(2, math.ceil(3 * 126 * 2 ** 20 / per_set))
+    inp = make_step_inputs(B, "cpu", seed=6000 + B)
+    q, k, v = (inp[n][:, h0:h1].contiguous().to(dev) for n in ("q", "k", "v"))
+    lg, mix = inp["log_gamma"][:, h0:h1].contiguous().to(dev), inp["mix"][:, h0:h1].contiguous().to(dev)
+    nw = inp["norm_w"][h0:h1].contiguous().to(dev)
+    sets = [[t[:, h0:h1].contiguous() for t in make_cache(B, dev, seed=300 + i)] for i in range(nsets)]
+    outs = [torch.empty(B, Hg, J, D, device=dev) for _ in range(nsets)]
+    y = torch.empty_like(q)
+    ws = decode_workspace(dev, B, Hg, D)
+    fmt = _capi.FORMATS[_capi.DecodeArgs]
+    bufs = [fmt.pack(*decode_args(q, k, v, ck, cv, st, outs[i], lg, mix, nw, R, L, 2.0, y, workspace=ws))
+            for i, (ck, cv, st) in enumerate(sets)]
+    fn = _capi.lib().hofa_decode_fwd
+    stream = torch.cuda.Stream(dev)
+
+    def launch():
+        for i in range(steps):
+            if fn(bufs[i % nsets], stream.cuda_stream) != 0:
+                raise RuntimeError(_capi.lib().hofa_last_error().decode())
+
+    dist.barrier()
+    us = _decode_graph_time(launch, steps, reps, stream)
+    t = torch.tensor([us], device=dev)
+    all_us = torch.empty(world, device=dev)
+    dist.all_gather_into_tensor(all_us, t)
+    us_max = all_us.max().item()
+    peak, kind = peaks()
+    ach = per_set / (us_max / 1e6) / 1e9
+    split = int(_capi.lib().hofa_decode_choose_split(B, Hg, L, torch.cuda.get_device_properties(dev).multi_processor_count))
+    return {"workload": f"config1-decode-B{B}-L{L}-head-sharded", "ranks": world, "heads_per_rank": Hg,
+            "us_per_step": round(us_max, 3), "per_rank_us_per_step": [round(x, 3) for x in all_us.tolist()],
+            "tokens_per_s": round(B / (us_max / 1e6), 1), "split_k": split,
+            "per_rank_bytes_per_step": per_set,
+            "per_rank_roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
+                                  "frac": round(ach / peak, 4), "peak_source": f"{kind} hbm_gbs"}}
+
+
+def measure_config4_decode_head_sharded(dev, world, sp, nsteps=128, reps=3):
+    """Config 4 after the sequence-sharded prefill: the outlier caches and GLA
+    state are re-laid out from sequence shards to head shards (one
+    all_to_all_single, timed), then 128 split-K decode steps over the 64k
+    cache (rows T .. T+127 attended as the steps advance) run head-sharded,
+    replayed from a CUDA graph.  Parity: each rank's first decode step against
+    the same step over all heads with the whole-sequence caches."""
+    import torch.distributed as dist
+    from outlierneuronattention_b200 import _capi, fused_hofa_decode
+    from outlierneuronattention_b200.seqpar import head_range, relayout_seq_to_head
+    rank = dist.get_rank()
+    T4 = sp["T"]
+    cap = T4 + nsteps
+    h0, h1 = head_range(H, world, rank)
+    Hg = h1 - h0
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    ck, cv, st0 = relayout_seq_to_head(sp["k"][..., :R], sp["v"], sp["S_end"], T4, cap)
+    e1.record()
+    torch.cuda.synchronize()
+    relayout_ms = torch.tensor([e0.elapsed_time(e1)], device=dev)
+    dist.all_reduce(relayout_ms, op=dist.ReduceOp.MAX)
+    g = torch.Generator(device=dev).manual_seed(31)
+    newk = torch.randn(1, H, nsteps, R, device=dev, generator=g).to(torch.bfloat16)
+    newv = torch.randn(1, H, nsteps, D, device=dev, generator=g).to(torch.bfloat16)
+    ck[:, :, T4:] = newk[:, h0:h1]
+    cv[:, :, T4:] = newv[:, h0:h1]
+    inp = make_step_inputs(1, "cpu", seed=4100)
+    q, k, v = (inp[n].to(dev) for n in ("q", "k", "v"))
+    lg, mix, nw = inp["log_gamma"].to(dev), inp["mix"].to(dev), inp["norm_w"].to(dev)
+    sl = lambda t: t[:, h0:h1].contiguous()
+    qg, kg, vg, lgg, mixg, nwg = sl(q), sl(k), sl(v), sl(lg), sl(mix), nw[h0:h1].contiguous()
+    st = [st0.clone(), torch.empty_like(st0)]
+    ys = [torch.empty_like(qg) for _ in range(nsteps)]
+    # parity: step 0 (T4 + 1 rows) over the head shard vs all heads with the whole-sequence caches
+    y0 = fused_hofa_decode(qg, kg, vg, ck, cv, st[0], st[1], lgg, mixg, nwg, R, T4 + 1, 2.0)
+    ckf = torch.cat([sp["kf"][..., :R], newk[:, :, :1]], dim=2).contiguous()
+    cvf = torch.cat([sp["vf"], newv[:, :, :1]], dim=2).contiguous()
+    sf = torch.empty(1, H, J, D, device=dev)
+    S_full = torch.empty_like(sf)
+    # the whole-sequence state of every head: gather the head shards (every rank has all of S_end anyway)
+    S_full.copy_(sp["S_end"])
+    yf = fused_hofa_decode(q, k, v, ckf, cvf, S_full, sf, lg, mix, nw, R, T4 + 1, 2.0)
+    torch.cuda.synchronize()
+    perr = torch.tensor([(y0.float() - yf[:, h0:h1].float()).abs().max().item(),
+                         (st[1] - sf[:, h0:h1]).abs().max().item()], device=dev)
+    dist.all_reduce(perr, op=dist.ReduceOp.MAX)
+    del ckf, cvf
+
+    def launch():
+        for i in range(nsteps):
+            fused_hofa_decode(qg, kg, vg, ck, cv, st[i % 2], st[(i + 1) % 2], lgg, mixg, nwg, R, T4 + 1 + i, 2.0)
+
+    stream = torch.cuda.Stream(dev)
+    dist.barrier()
+    us = _decode_graph_time(launch, nsteps, reps, stream)
+    t = torch.tensor([us], device=dev)
+    all_us = torch.empty(world, device=dev)
+    dist.all_gather_into_tensor(all_us, t)
+    us_max = all_us.max().item()
+    per_rank_bytes = Hg * ((T4 + nsteps // 2) * (R + D) * 2 + J * D * 4 * 2)
+    peak, kind = peaks()
+    ach = per_rank_bytes / (us_max / 1e6) / 1e9
+    return {"workload": f"config4-decode-B1-L{T4}+{nsteps}-head-sharded", "ranks": world, "heads_per_rank": Hg,
+            "relayout_ms": round(relayout_ms.item(), 4),
+            "us_per_step": round(us_max, 3), "per_rank_us_per_step": [round(x, 3) for x in all_us.tolist()],
+            "tokens_per_s": round(1 / (us_max / 1e6), 1), "decode_steps": nsteps,
+            "parity_maxabs": {"y": perr[0].item(), "state": perr[1].item(),
+                              "against": "the same decode step over all heads with the whole-sequence caches"},
+            "per_rank_roofline": {"bound": "hbm", "achieved": round(ach, 1), "peak": peak, "unit": "GB/s",
+                                  "frac": round(ach / peak, 4), "peak_source": f"{kind} hbm_gbs",
+                                  "bytes_per_step": per_rank_bytes}}
 
 
 def measure_layer_step(dev, B=4, steps=64, reps=5):
     """Layer-level decode step (the drop-in module's forward_step with a
     pre-allocated cache of L=4096 rows, d_model=1024, H=16, r=16, bf16
-    weights): q/k/v projections, the fused decode step (hofa_decode_step_fwd:
+    weights): the QKV projection, the fused decode step (hofa_decode_step_fwd:
     gates, RoPE, cache append and the attention core in one launch) and the
-    output projection, replayed from a CUDA graph; also the same step with
-    the new token's prep as a separate launch."""
+    output projection, replayed from a CUDA graph."""
     from outlierneuronattention_b200 import HybridOutlierFactorizedAttention, ModelConfig
     torch.manual_seed(0)
     cfg = ModelConfig(d_model=1024, num_heads=H, num_layers=1, r=R, chunk_size=64)
@@ -623,34 +808,16 @@ def measure_layer_step(dev, B=4, steps=64, reps=5):
     caches = [((torch.randn(B, H, L, R, device=dev, generator=g) * KEY_STD).to(torch.bfloat16),
                (torch.randn(B, H, L, D, device=dev, generator=g) * VAL_STD).to(torch.bfloat16)) for _ in range(4)]
     st = (torch.randn(B, H, J, D, device=dev, generator=g) * 0.1, torch.empty(B, H, J, D, device=dev))
-    out = {}
-    for mode in ("fused", "two_launches"):
-        if mode == "two_launches":
-            os.environ["HOFA_DECODE_STEP_UNFUSED"] = "1"
-        stream = torch.cuda.Stream(dev)
-        with torch.no_grad(), torch.cuda.stream(stream):
-            for i in range(4):
-                m.forward_step(x, caches[i], st, cache_seq_len=L - 1)
-            stream.synchronize()
-            graph = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(graph, stream=stream):
-                for i in range(steps):
-                    m.forward_step(x, caches[i % 4], st, cache_seq_len=L - 1)
-            graph.replay()
-            stream.synchronize()
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            e0.record(stream)
-            for _ in range(reps):
-                graph.replay()
-            e1.record(stream)
-            stream.synchronize()
-        del graph
-        os.environ.pop("HOFA_DECODE_STEP_UNFUSED", None)
-        out[f"{mode}_us_per_step"] = round(e0.elapsed_time(e1) * 1e3 / (reps * steps), 3)
-    out.update({"workload": f"config1-layer-forward_step-B{B}-L{L}", "d_model": 1024,
-                "tokens_per_s": round(B / (out["fused_us_per_step"] / 1e6), 1),
-                "note": "projections (cuBLAS) + fused decode step + out_proj per step"})
-    return out
+
+    def launch():
+        for i in range(steps):
+            m.forward_step(x, caches[i % 4], st, cache_seq_len=L - 1)
+
+    with torch.no_grad():
+        us = _decode_graph_time(launch, steps, reps, torch.cuda.Stream(dev))
+    return {"workload": f"config1-layer-forward_step-B{B}-L{L}", "d_model": 1024, "us_per_step": round(us, 3),
+            "tokens_per_s": round(B / (us / 1e6), 1),
+            "note": "QKV projection (cuBLAS) + fused decode step + out_proj per step, CUDA graph"}
 
 
 # ----------------------------------------------------------------------------- CPU arm

@@ -11,7 +11,8 @@
 //        G   = inclusive cumsum of log_gamma over the chunk, G_C = its total
 //        Kd  = K_I * exp(G_C - G_t)        (rows of the K tile, in shared memory)
 //        dS  = Kd^T V                      tcgen05.mma, M = 64 or 128 (inlier rows,
-//                                          padded), N = D, K = 128 tokens, A and B MN-major
+//                                          padded), N = D, K = 128 tokens, A and B MN-major;
+//                                          Kd as hi + lo 16-bit terms, two MMAs
 //        -> workspace: dS_c [J x D] fp32 and G_C
 //   B  gla_tc_scan_kernel    (one thread per state element of a head)
 //        S_0 = state_init or 0;  start_c = S before chunk c;  S <- exp(G_C) S + dS_c
@@ -26,9 +27,11 @@
 //        y   = Y1 + exp(G_i) Y2, then (1 - mix) * gla_scale * RMSNorm(y)
 //
 // All decay factors are exponentials of non-positive differences of cumulative
-// log decays (no overflow).  Rounding points match the reference kernel: the
-// masked score matrix and the carried state enter the tensor core in the input
-// dtype, accumulation is fp32, the state carried between chunks stays fp32.
+// log decays (no overflow).  Rounding points: the masked score matrix and the
+// carried state enter the output kernel's tensor-core products in the input
+// dtype, as in the reference kernel; the decayed keys of the state update
+// enter as a hi + lo pair of 16-bit terms (the reference rounds them once),
+// accumulation is fp32 and the state carried between chunks stays fp32.
 // Waits are bounded (sm100::mbar_wait); a timeout is recorded in
 // g_gla_tc_status and the CTA skips its remaining issue, frees TMEM and exits.
 #include <cuda.h>
@@ -148,7 +151,15 @@ gla_tc_state_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
   if (!sm100::mbar_wait(&bars[0], 0)) atomicOr(err, 1);
   __syncthreads();
   const float gc = sm_gc;
-  // Kd: scale this thread's K row (every column block; swizzling only permutes chunks within a row)
+  // Kd = K * exp(G_C - G_t) enters the tensor core as two 16-bit terms,
+  // Kd = hi + lo (hi = Kd rounded, lo = the rounding remainder, rounded), so
+  // the fp32 state keeps about 16 significant bits of every key instead of
+  // the 8 of a single bf16 operand.  The reference rounds Kd once
+  // (src/chunk_gla_inlier.py:122-125); that alone puts about 2e-2 of absolute
+  // error into a state of magnitude 10 over 8192 tokens.  The two products
+  // accumulate into the same TMEM columns; hi goes first, lo waits in
+  // registers until the first MMA has read the shared-memory tile.
+  uint4 lo_regs[Gm::NB][8];
   {
     const float w = sm100::ex2_approx((gc - G) * kLog2e);
 #pragma unroll
@@ -158,31 +169,49 @@ gla_tc_state_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
       for (int q = 0; q < 8; ++q) {
         uint4 u = row[q];
         uint32_t* pu = reinterpret_cast<uint32_t*>(&u);
+        uint32_t* pl = reinterpret_cast<uint32_t*>(&lo_regs[nb][q]);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           float a, bb;
           if (BF16) bf16x2_to_f(pu[e], a, bb);
           else f16x2_to_f(pu[e], a, bb);
-          pu[e] = pack2(a * w, bb * w, BF16);
+          const float xa = a * w, xb = bb * w;
+          pu[e] = pack2(xa, xb, BF16);
+          float ha, hb;
+          if (BF16) bf16x2_to_f(pu[e], ha, hb);
+          else f16x2_to_f(pu[e], ha, hb);
+          pl[e] = pack2(xa - ha, xb - hb, BF16);
         }
         row[q] = u;
       }
     }
   }
-  fence_async_smem();
-  sm100::tc_fence_before();
-  __syncthreads();
-  if (tid == 0 && !*verr) {
-    sm100::tc_fence_after();
-    const uint64_t adesc = sm100::smem_desc(sK, Gm::LBO, 1024, sm100::kSwizzle128);
-    const uint64_t bdesc = sm100::smem_desc(sV, Gm::LBO, 1024, sm100::kSwizzle128);
+  const uint64_t adesc = sm100::smem_desc(sK, Gm::LBO, 1024, sm100::kSwizzle128);
+  const uint64_t bdesc = sm100::smem_desc(sV, Gm::LBO, 1024, sm100::kSwizzle128);
+#pragma unroll 1
+  for (int term = 0; term < 2; ++term) {
+    if (term == 1) {  // the hi product has completed: its operand tile may be overwritten with lo
 #pragma unroll
-    for (int ks = 0; ks < kC / 16; ++ks)
-      sm100::mma_ss(tmem, adesc + (uint64_t)(ks * 2048 >> 4), bdesc + (uint64_t)(ks * 2048 >> 4), IDESC, ks > 0);
-    sm100::mma_commit(&bars[1]);
+      for (int nb = 0; nb < Gm::NB; ++nb) {
+        uint4* row = reinterpret_cast<uint4*>(sK + nb * kTile + tid * 128);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) row[q] = lo_regs[nb][q];
+      }
+    }
+    fence_async_smem();
+    sm100::tc_fence_before();
+    __syncthreads();
+    if (tid == 0 && !*verr) {
+      sm100::tc_fence_after();
+#pragma unroll
+      for (int ks = 0; ks < kC / 16; ++ks)
+        sm100::mma_ss(tmem, adesc + (uint64_t)(ks * 2048 >> 4), bdesc + (uint64_t)(ks * 2048 >> 4), IDESC,
+                      term > 0 || ks > 0);
+      sm100::mma_commit(&bars[1]);
+    }
+    if (!*verr && !sm100::mbar_wait(&bars[1], term)) atomicOr(err, 1);
+    sm100::tc_fence_after();
   }
-  if (!*verr && !sm100::mbar_wait(&bars[1], 0)) atomicOr(err, 1);
-  sm100::tc_fence_after();
   // D (M = 64): row j lives in lane 32*(j/16) + j%16; (M = 128): row j in lane j
   const int j = Gm::STATE_M == 64 ? 16 * warp + lane : tid;
   const bool row_ok = (Gm::STATE_M == 64 ? lane < 16 : true) && j < p.J && !*verr;

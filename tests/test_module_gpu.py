@@ -127,7 +127,7 @@ def test_bf16_autocast_prefill_matches_reference(name, T0):
         y, cache, state = m(x[:, :T0].to(torch.bfloat16), return_state=True)
     assert y.dtype == torch.bfloat16
     assert err(y, g["y"][:, :T0]) <= 2e-2
-    assert err(state[0], g["states"][T0]) <= 2e-2 * max(1.0, g["states"][T0].abs().max().item())
+    assert err(state[0], g["states"][T0]) <= 2e-2
 
 
 def test_config0_fp32_against_oracle():
@@ -156,14 +156,14 @@ def test_config0_fp32_against_oracle():
     assert err(y, ref_y) <= 1e-4
     assert err(cache[0], ref_cache[0]) <= 1e-4
     assert err(cache[1], ref_cache[1]) <= 1e-4
-    assert err(state[0], ref_state) <= 1e-4 * max(1.0, ref_state.abs().max().item())
+    assert err(state[0], ref_state) <= 1e-4
     # one more token through forward_step == the oracle's decode step
     xs = torch.randn(2, 1, 512, generator=gen)
     with torch.no_grad():
         ys, _, st2 = m.forward_step(xs.cuda(), cache, state)
     oy, _, ost = oracle.forward_step(xs.double(), ref_cache, ref_state)
     assert err(ys, oy) <= 1e-4
-    assert err(st2[0], ost) <= 1e-4 * max(1.0, ost.abs().max().item())
+    assert err(st2[0], ost) <= 1e-4
 
 
 def test_module_has_reference_parameter_names():
@@ -203,7 +203,7 @@ def test_no_rope_layer_prefill_export_and_preallocated_decode_fp32():
             oy, oc, ost = oracle.forward_step(x[:, t:t + 1].double(), oc, ost)
             assert err(ys, oy) <= 1e-4
     assert err(cache[0], oc[0]) <= 1e-4 and err(cache[1], oc[1]) <= 1e-4
-    assert err(state[0], ost) <= 1e-4 * max(1.0, ost.abs().max().item())
+    assert err(state[0], ost) <= 1e-4
 
 
 def test_device_position_decode_loop_in_cuda_graph():
@@ -265,4 +265,4 @@ def test_device_position_decode_loop_in_cuda_graph():
         assert err(a, b) <= 1e-4
     assert int(pos.item()) == T0 + NS
     assert err(cache[0], ref_cache[0]) <= 1e-5 and err(cache[1], ref_cache[1]) <= 1e-5
-    assert err(sa, ref_state) <= 1e-4 * max(1.0, ref_state.abs().max().item())
+    assert err(sa, ref_state) <= 1e-4

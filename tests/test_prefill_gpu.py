@@ -6,10 +6,12 @@ inputs:
 * hofa_prefill_outlier_fwd (exact_attention_triton) vs
   ``outlier_attention_core`` (restating src/exact_attention.py:163-188).
 
-Tolerances: bf16/fp16 outputs <= 2e-2 max-abs on the normalised output
-(raw GLA output: 2e-2 relative to its max); float32 inputs <= 1e-4; final
-GLA state (float32) <= 1e-3 relative in bf16 runs of the CUDA-core kernel,
-<= 2e-2 relative for the tensor-core kernel (bf16 operands), 1e-5 in float32 runs.
+Tolerances (absolute, max over all elements): bf16/fp16 outputs <= 2e-2;
+float32 inputs <= 1e-4; the final float32 GLA state <= 2e-2 in bf16/fp16 runs
+and <= 1e-4 in float32 runs.  Raw (un-normalised) GLA outputs are checked on
+inputs scaled so that |y| stays below about 4, where a bf16 output's own
+rounding is below 1e-2.  The full-size tests print the achieved max-abs
+errors.
 """
 import math
 
@@ -47,9 +49,7 @@ def test_gla_fused_epilogue(dtype, T):
     assert st.shape == (B, H, 64, 64)
     tol = 1e-4 if dtype == torch.float32 else 2e-2
     assert maxabs(Y, Yr) <= tol
-    s = st[:, :, :D - r, :D]
-    rel = (s.double().cpu() - Sr).abs().max().item() / Sr.abs().max().item()
-    assert rel <= (1e-5 if dtype == torch.float32 else 2e-2)
+    assert maxabs(st[:, :, :D - r, :D], Sr) <= tol
     assert st[:, :, D - r:].abs().max().item() == 0
 
 
@@ -64,19 +64,19 @@ def test_gla_segments_and_initial_state(nseg):
                     state_out=st, initial_state=s0.cuda(), num_segments=nseg)
     Yr, Sr = chunk_gla_core(q, k, v, lg, r, 64, mix_g=mix, gla_scale=gs, eps=1e-5, state_init=s0)
     assert maxabs(Y, Yr) <= 1e-4
-    assert maxabs(st, Sr) <= 1e-4 * max(1.0, Sr.abs().max().item())
+    assert maxabs(st, Sr) <= 1e-4
 
 
 @pytest.mark.parametrize("D,r", [(128, 16), (128, 64), (32, 8), (64, 0), (64, 32)])
 def test_gla_shapes_raw_output(D, r):
     from outlierneuronattention_b200 import chunk_gla_inlier_fwd
     B, H, T = 2, 2, 300
-    q, k, v, lg, _, _ = rand_qkv(B, H, T, D, torch.bfloat16, seed=D * 7 + r)
+    q, k, v, lg, _, _ = rand_qkv(B, H, T, D, torch.bfloat16, seed=D * 7 + r, scale=0.3)
     Y, st = chunk_gla_inlier_fwd(q.cuda(), k.cuda(), v.cuda(), lg.cuda(), r, 64)
     Yr, Sr = chunk_gla_core(q, k, v, lg, r, 64)
-    assert maxabs(Y, Yr) <= 2e-2 * Yr.abs().max().item()
-    s = st[:, :, :D - r, :D]
-    assert (s.double().cpu() - Sr).abs().max().item() <= 2e-2 * Sr.abs().max().item()
+    assert Yr.abs().max().item() < 4.0  # keeps the bf16 output's own rounding below 1e-2
+    assert maxabs(Y, Yr) <= 2e-2
+    assert maxabs(st[:, :, :D - r, :D], Sr) <= 2e-2
 
 
 def test_gla_learnable_alpha_strong_decay():
@@ -94,7 +94,7 @@ def test_gla_learnable_alpha_strong_decay():
     # strong decay keeps the pre-norm output small and RMSNorm scales its fp32
     # rounding up with it: bound the error relative to the output's size
     assert maxabs(Y, Yr) <= 1e-4 * max(1.0, Yr.abs().max().item()), (maxabs(Y, Yr), Yr.abs().max().item())
-    assert maxabs(st[:, :, :D - r, :D], Sr) <= 1e-5 * max(1.0, Sr.abs().max().item())
+    assert maxabs(st[:, :, :D - r, :D], Sr) <= 1e-4
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32, torch.float16])
@@ -130,35 +130,81 @@ def test_outlier_attention_query_suffix_with_offset():
     assert maxabs(out, ref) <= 2e-2
 
 
-def test_config2_full_size_sampled_heads():
-    """BASELINE config 2 (B=4, T=8192, H=16, d_h=64, r=16) in bf16 on the GPU;
-    two heads are checked against the oracle (the full float64 oracle would
-    take minutes): all rows of the GLA, and the first/last 128 query rows of
-    the attention."""
+def _full_size_check(B, H, T, q, k, v, lg, mix, heads, row_blocks, label):
+    """Runs the GLA and the attention on the GPU at full size (as the layer
+    does: GLA writes Y, attention adds into it) and checks the sampled
+    (b, h) heads against the oracle: every GLA row and the final GLA state,
+    and the attention at 128-row blocks starting at ``row_blocks``.
+    Returns the achieved max-abs errors (also printed)."""
     from outlierneuronattention_b200 import chunk_gla_inlier_fwd, exact_attention_triton
-    B, H, T, D, r = 4, 16, 8192, 64, 16
-    g = torch.Generator(device="cuda").manual_seed(2)
-    q = torch.randn(B, H, T, D, device="cuda", generator=g).to(torch.bfloat16)
-    k = torch.randn(B, H, T, D, device="cuda", generator=g).to(torch.bfloat16)
-    v = torch.randn(B, H, T, D, device="cuda", generator=g).to(torch.bfloat16)
-    lg = F.logsigmoid(torch.randn(B, H, T, device="cuda", generator=g) + 2.0)
-    mix = torch.sigmoid(torch.randn(B, H, T, device="cuda", generator=g)).to(torch.bfloat16)
+    D, r = 64, 16
     gs = torch.ones(1, H, 1, D, device="cuda")
     Y, st = chunk_gla_inlier_fwd(q, k, v, lg, r, 64, mix_g=mix, gla_scale=gs)
     Y_gla = Y.clone()
     exact_attention_triton(q, k, v, r, 2.0, mix, out=Y)
     torch.cuda.synchronize()
-    assert torch.isfinite(Y).all()
-    for (b, h) in ((0, 0), (3, 15)):
+    assert torch.isfinite(Y.float()).all()
+    assert _prefill_status() == 0
+    e_gla = e_state = e_attn = 0.0
+    smax = 0.0
+    for (b, h) in heads:
         sl = lambda t: t[b:b + 1, h:h + 1].cpu()
-        Yr, Sr = chunk_gla_core(sl(q), sl(k), sl(v), sl(lg), r, 64, mix_g=sl(mix), gla_scale=gs[:, h:h + 1].cpu(), eps=1e-5)
-        assert maxabs(sl(Y_gla), Yr) <= 2e-2
-        assert (sl(st)[:, :, :D - r, :D].double() - Sr).abs().max().item() <= 2e-2 * Sr.abs().max().item()
-        for q0 in (0, T - 128):
-            qs = sl(q)[:, :, q0:q0 + 128]
-            ref = outlier_attention_core(qs, sl(k), sl(v), r, 2.0, sl(mix)[:, :, q0:q0 + 128],
+        Yr, Sr = chunk_gla_core(sl(q), sl(k), sl(v), sl(lg), r, 64, mix_g=sl(mix), gla_scale=gs[:, h:h + 1].cpu(),
+                                eps=1e-5)
+        e_gla = max(e_gla, maxabs(sl(Y_gla), Yr))
+        e_state = max(e_state, maxabs(sl(st)[:, :, :D - r, :D], Sr))
+        smax = max(smax, Sr.abs().max().item())
+        for q0 in row_blocks:
+            ref = outlier_attention_core(sl(q)[:, :, q0:q0 + 128], sl(k), sl(v), r, 2.0, sl(mix)[:, :, q0:q0 + 128],
                                          out=sl(Y_gla)[:, :, q0:q0 + 128], q_offset=q0)
-            assert maxabs(sl(Y)[:, :, q0:q0 + 128], ref) <= 2e-2
+            e_attn = max(e_attn, maxabs(sl(Y)[:, :, q0:q0 + 128], ref))
+    print(f"{label}: max-abs GLA output {e_gla:.3e}, GLA state {e_state:.3e} (|S| max {smax:.2f}), "
+          f"attention output {e_attn:.3e} over {len(heads)} heads x {len(row_blocks) * 128} attention rows")
+    assert e_gla <= 2e-2 and e_state <= 2e-2 and e_attn <= 2e-2, (e_gla, e_state, e_attn)
+    return e_gla, e_state, e_attn
+
+
+def test_config2_full_size_sampled_heads():
+    """BASELINE config 2 (B=4, T=8192, H=16, d_h=64, r=16) in bf16 on the GPU;
+    eight (b, h) heads spread over the batch are checked against the oracle:
+    every GLA row, the final GLA state, and 16 attention blocks of 128 query
+    rows spread evenly over the sequence (2,048 rows per head, first and last
+    block included)."""
+    B, H, T = 4, 16, 8192
+    g = torch.Generator(device="cuda").manual_seed(2)
+    q = torch.randn(B, H, T, 64, device="cuda", generator=g).to(torch.bfloat16)
+    k = torch.randn(B, H, T, 64, device="cuda", generator=g).to(torch.bfloat16)
+    v = torch.randn(B, H, T, 64, device="cuda", generator=g).to(torch.bfloat16)
+    lg = F.logsigmoid(torch.randn(B, H, T, device="cuda", generator=g) + 2.0)
+    mix = torch.sigmoid(torch.randn(B, H, T, device="cuda", generator=g)).to(torch.bfloat16)
+    heads = [(0, 0), (0, 9), (1, 3), (1, 14), (2, 6), (2, 11), (3, 1), (3, 15)]
+    rows = [i * (T - 128) // 15 // 128 * 128 for i in range(16)]
+    assert rows[0] == 0 and rows[-1] == T - 128
+    _full_size_check(B, H, T, q, k, v, lg, mix, heads, rows, "config 2")
+
+
+def test_config4_full_size_sampled_heads():
+    """BASELINE config 4 (B=1, T=65536, H=16, d_h=64, r=16) in bf16 on the GPU:
+    the attention kernel's 1,024-tile key loop and the GLA's 512-chunk scan at
+    full length.  Four heads against the oracle: every GLA row and the final
+    state, and attention blocks at the start, the middle and the end.  Heads
+    8-15 get keys whose outlier channel 0 grows along the sequence (logits rise
+    by about 150 log2 units from the first key to the last), so the running
+    max of late rows is raised far beyond the lazy-rescale threshold many
+    times deep into the key loop; heads 0-7 are N(0, 1)."""
+    B, H, T = 1, 16, 65536
+    g = torch.Generator(device="cuda").manual_seed(4)
+    q = torch.randn(B, H, T, 64, device="cuda", generator=g)
+    k = torch.randn(B, H, T, 64, device="cuda", generator=g)
+    v = torch.randn(B, H, T, 64, device="cuda", generator=g)
+    q[:, 8:, :, 0] = 1.0 + 0.1 * q[:, 8:, :, 0]
+    k[:, 8:, :, 0] = 0.8 * k[:, 8:, :, 0] + 52.0 * torch.arange(T, device="cuda") / T
+    q, k, v = (t.to(torch.bfloat16) for t in (q, k, v))
+    lg = F.logsigmoid(torch.randn(B, H, T, device="cuda", generator=g) + 2.0)
+    mix = torch.sigmoid(torch.randn(B, H, T, device="cuda", generator=g)).to(torch.bfloat16)
+    heads = [(0, 2), (0, 7), (0, 8), (0, 13)]
+    rows = [0, 128, 8192, 32768 - 128, 32768, 49152, T - 256, T - 128]
+    _full_size_check(B, H, T, q, k, v, lg, mix, heads, rows, "config 4")
 
 
 def _prefill_status():
@@ -209,10 +255,11 @@ def test_gla_tensor_core_path(monkeypatch, dtype, B, H, T, r, fuse, init, D):
     and the CUDA-core GLA agree with the oracle on the same inputs, including a
     seeded initial state; the tensor-core kernels' bounded waits never ran out."""
     from outlierneuronattention_b200.chunk_gla_inlier import gla_forward
-    q, k, v, lg, mix, gs = rand_qkv(B, H, T, D, dtype, seed=T + r)
+    q, k, v, lg, mix, gs = rand_qkv(B, H, T, D, dtype, seed=T + r, scale=0.3)
     s0 = torch.randn(B, H, D - r, D, generator=torch.Generator().manual_seed(T + r)) * 0.3 if init else None
     Yr, Sr = chunk_gla_core(q, k, v, lg, r, 64, mix_g=mix if fuse else None, gla_scale=gs if fuse else None,
                             eps=1e-5, state_init=s0)
+    assert fuse or Yr.abs().max().item() < 4.0  # raw outputs: the bf16 output's own rounding stays below 1e-2
     assert _prefill_status() == 0
     outs = {}
     for path in ("tc", "cuda_core"):
@@ -224,10 +271,8 @@ def test_gla_tensor_core_path(monkeypatch, dtype, B, H, T, r, fuse, init, D):
                         initial_state=None if s0 is None else s0.cuda())
         torch.cuda.synchronize()
         outs[path] = (Y, st)
-        scale = 1.0 if fuse else max(1.0, Yr.abs().max().item())
-        assert maxabs(Y, Yr) <= 2e-2 * scale, path
-        # bf16 runs: <= 2e-2 on the state (the decayed keys enter the tensor core in bf16, as in the reference)
-        assert (st.double().cpu() - Sr).abs().max().item() <= 2e-2 * max(1.0, Sr.abs().max().item()), path
+        assert maxabs(Y, Yr) <= 2e-2, path
+        assert maxabs(st, Sr) <= 2e-2, path
     monkeypatch.delenv("HOFA_GLA_NO_TC")
     assert _prefill_status() == 0
 
