@@ -395,6 +395,8 @@ def run_ours(args):
         out["config4_seqpar"] = sp.pop("summary")
         out["decode_head_sharded"] = [measure_decode_head_sharded(dev, world, B=1),
                                       measure_config4_decode_head_sharded(dev, world, sp)]
+    if not args.no_triton_reference and world == 1:
+        out["triton_reference"] = measure_triton_reference(dev)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(B, args.cpu_seconds)
     if world > 1:
@@ -820,6 +822,160 @@ def measure_layer_step(dev, B=4, steps=64, reps=5):
             "note": "QKV projection (cuBLAS) + fused decode step + out_proj per step, CUDA graph"}
 
 
+# ----------------------------------------------------------------------------- reference's Triton kernels
+REF_DIR = os.path.join(ROOT, "baseline", "_ref")
+
+
+def _event_ms(fn, n, flush=None):
+    """Mean CUDA-event time of `n` back-to-back calls (after a flush of L2)."""
+    if flush is not None:
+        flush.zero_()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(n):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / n
+
+
+def measure_triton_reference(dev):
+    """The reference's own GPU implementation of the hot path -- its Triton
+    kernels ``fused_hofa_decode`` (src/hofa_decode_triton.py:342),
+    ``chunk_gla_inlier_fwd`` (src/chunk_gla_inlier.py:153) and
+    ``exact_attention_triton`` (src/exact_attention.py:163), and its layer
+    ``HybridOutlierFactorizedAttention`` -- imported unmodified from
+    baseline/_ref (an install of the reference package) and run on this GPU
+    with the same inputs, shapes and timing method as this library's arm:
+    decode steps replayed from a CUDA graph over rotating cache sets larger
+    than L2, prefill operators over back-to-back calls after an L2 flush.
+    ``maxabs_vs_ours`` is the largest difference between the reference's
+    outputs and this library's on the same inputs."""
+    if not os.path.isdir(os.path.join(REF_DIR, "src")):
+        return {"unavailable": "baseline/_ref is not installed"}
+    sys.path.insert(0, REF_DIR)
+    try:
+        from src.chunk_gla_inlier import chunk_gla_inlier_fwd as ref_gla
+        from src.exact_attention import exact_attention_triton as ref_attn
+        from src.hofa_decode_triton import fused_hofa_decode as ref_decode
+        from src.HybridOutlierFactorizedAttention import HybridOutlierFactorizedAttention as RefLayer
+        from src.config import ModelConfig as RefConfig
+    except Exception as e:  # noqa: BLE001
+        sys.path.remove(REF_DIR)
+        return {"unavailable": f"import of the reference failed: {e!r}"}
+    from outlierneuronattention_b200 import (HybridOutlierFactorizedAttention, ModelConfig, exact_attention_triton,
+                                             fused_hofa_decode)
+    from outlierneuronattention_b200.chunk_gla_inlier import gla_forward
+    out = {"source": "baseline/_ref (reference package, unmodified), Triton " + __import__("triton").__version__}
+    try:
+        # ---- decode, config 1 (B = 1, 4, 64) and config 4 ------------------------------------
+        dec = []
+        for B, steps in ((1, 200), (4, 200), (64, 20)):
+            per_set = algorithmic_bytes(B)
+            nsets = max(2, math.ceil(3 * 126 * 2 ** 20 / per_set))
+            inp = make_step_inputs(B, "cpu", seed=7000 + B)
+            q, k, v = (inp[n].to(dev) for n in ("q", "k", "v"))
+            lg, mix, nw = inp["log_gamma"].to(dev), inp["mix"].to(dev), inp["norm_w"].to(dev)
+            sets = [make_cache(B, dev, seed=500 * B + i) for i in range(nsets)]
+            outs = [torch.empty(B, H, J, D, device=dev) for _ in range(nsets)]
+            row = {"workload": f"config1-decode-B{B}-L{L}"}
+            if B == 4:
+                ck, cv, st = sets[0]
+                s_ref, s_our = torch.empty_like(st), torch.empty_like(st)
+                y_ref = ref_decode(q, k, v, ck, cv, st, s_ref, lg, mix, nw, R, L, 2.0)
+                y_our = fused_hofa_decode(q, k, v, ck, cv, st, s_our, lg, mix, nw, R, L, 2.0)
+                torch.cuda.synchronize()
+                row["maxabs_vs_ours"] = {"y": (y_ref.float() - y_our.float()).abs().max().item(),
+                                         "state": (s_ref - s_our).abs().max().item()}
+
+            def launch(B=B, sets=sets, outs=outs, q=q, k=k, v=v, lg=lg, mix=mix, nw=nw, steps=steps, nsets=nsets):
+                for i in range(steps):
+                    ck, cv, st = sets[i % nsets]
+                    ref_decode(q, k, v, ck, cv, st, outs[i % nsets], lg, mix, nw, R, L, 2.0)
+
+            us = _decode_graph_time(launch, steps, 3, torch.cuda.Stream(dev))
+            row.update({"us_per_step": round(us, 3), "tokens_per_s": round(B / (us / 1e6), 1),
+                        "hbm_frac": round(per_set / (us / 1e6) / 1e9 / peaks()[0], 4)})
+            dec.append(row)
+            del sets, outs
+        out["decode"] = dec
+        # ---- prefill operators, config 2 and config 4 -----------------------------------------
+        flush = torch.empty(2 * 126 * 2 ** 20 // 4, device=dev)
+        pre = []
+        for B, T, n in ((4, 8192, 3), (1, 65536, 2)):
+            g = torch.Generator(device=dev).manual_seed(3)
+            x3 = torch.randn(B, T, 3, H, D, device=dev, generator=g).to(torch.bfloat16)
+            q, k, v = (x3[:, :, i].transpose(1, 2) for i in range(3))
+            lg = F.logsigmoid(torch.randn(B, H, T, device=dev, generator=g) + 2.0)
+            mix = torch.sigmoid(torch.randn(B, H, T, device=dev, generator=g)).to(torch.bfloat16)
+            gs = torch.ones(1, H, 1, D, device=dev)
+            y_ref, s_ref = ref_gla(q, k, v, lg, R, 64, mix_g=mix, gla_scale=gs)
+            y_our = torch.empty_like(y_ref)
+            s_our = torch.empty(B, H, J, D, device=dev)
+            gla_forward(q, k, v, lg, R, mix_g=mix, gla_scale=gs, y=y_our, state_out=s_our)
+            torch.cuda.synchronize()
+            gla_diff = (y_ref.float() - y_our.float()).abs().max().item()
+            state_diff = (s_ref[:, :, :J, :D] - s_our).abs().max().item()
+            ref_attn(q, k, v, R, 2.0, mix, out=y_ref)
+            exact_attention_triton(q, k, v, R, 2.0, mix, out=y_our)
+            torch.cuda.synchronize()
+            attn_diff = (y_ref.float() - y_our.float()).abs().max().item()
+            t_gla = _event_ms(lambda: ref_gla(q, k, v, lg, R, 64, mix_g=mix, gla_scale=gs, out=y_ref), n, flush)
+            t_attn = _event_ms(lambda: ref_attn(q, k, v, R, 2.0, mix, out=y_ref), n, flush)
+            flops = B * H * (R + D) * T * T
+            pre.append({"workload": f"prefill-B{B}-T{T}", "ms_by_kernel": {"gla": round(t_gla, 4),
+                                                                            "outlier": round(t_attn, 4)},
+                        "outlier_tflops": round(flops / (t_attn / 1e3) / 1e12, 1),
+                        "maxabs_vs_ours": {"gla_y": gla_diff, "gla_state": state_diff, "y_after_attention": attn_diff}})
+            del x3, y_ref, y_our
+        out["prefill"] = pre
+        # ---- the layer: forward at config 2, forward_step at config 1 (same weights as ours) -----
+        torch.manual_seed(0)
+        rcfg = RefConfig(d_model=1024, num_heads=H, num_layers=1, r=R, chunk_size=64)
+        ref_layer = RefLayer(rcfg).to(dev).eval()
+        with torch.no_grad():
+            for name, prm in ref_layer.named_parameters():
+                if "gate_proj.weight" in name or "mix_proj.weight" in name:
+                    prm.normal_(0, 0.02)
+        our_layer = HybridOutlierFactorizedAttention(ModelConfig(d_model=1024, num_heads=H, num_layers=1, r=R,
+                                                                 chunk_size=64)).to(dev).eval()
+        our_layer.load_state_dict(ref_layer.state_dict(), strict=True)
+        x = torch.randn(4, 8192, 1024, device=dev, generator=torch.Generator(device=dev).manual_seed(8)) * 0.5
+        lay = {}
+        with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
+            yr = ref_layer(x)
+            yo = our_layer(x)
+            torch.cuda.synchronize()
+            lay["forward_config2_maxabs_vs_ours"] = (yr.float() - yo.float()).abs().max().item()
+            lay["forward_config2_ms"] = round(_event_ms(lambda: ref_layer(x), 3, flush), 4)
+            lay["forward_config2_ms_ours"] = round(_event_ms(lambda: our_layer(x), 3, flush), 4)
+        del x, yr, yo
+        ref_bf = ref_layer.to(torch.bfloat16)
+        for B in (1, 4):
+            g = torch.Generator(device=dev).manual_seed(9)
+            xs = torch.randn(B, 1, 1024, device=dev, generator=g).to(torch.bfloat16)
+            caches = [((torch.randn(B, H, L, R, device=dev, generator=g) * KEY_STD).to(torch.bfloat16),
+                       (torch.randn(B, H, L, D, device=dev, generator=g) * VAL_STD).to(torch.bfloat16))
+                      for _ in range(4)]
+            st = (torch.randn(B, H, J, D, device=dev, generator=g) * 0.1, torch.empty(B, H, J, D, device=dev))
+
+            def launch(B=B, xs=xs, caches=caches, st=st):
+                for i in range(64):
+                    ref_bf.forward_step(xs, caches[i % 4], st, cache_seq_len=L - 1)
+
+            with torch.no_grad():
+                us = _decode_graph_time(launch, 64, 5, torch.cuda.Stream(dev))
+            lay[f"forward_step_B{B}_us"] = round(us, 3)
+        out["layer"] = lay
+    except Exception as e:  # noqa: BLE001
+        out["error"] = f"{type(e).__name__}: {e}"
+    finally:
+        if REF_DIR in sys.path:
+            sys.path.remove(REF_DIR)
+    return out
+
+
 # ----------------------------------------------------------------------------- CPU arm
 def cpu_baseline(B: int, seconds: float):
     """The reference's CPU computation of one decode step (oracle port of the
@@ -875,6 +1031,8 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-triton-reference", action="store_true",
+                    help="skip timing the reference's own Triton kernels (baseline/_ref)")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-2 prefill measurement")
     ap.add_argument("--no-config4", action="store_true",
                     help="skip the config-4 (B=1, T=65536) prefill and long-cache decode measurement")

@@ -114,6 +114,18 @@ class PhaseTimer:
         return out
 
 
+_SIDE_STREAMS: Dict[int, torch.cuda.Stream] = {}
+
+
+def _side_stream(dev: torch.device) -> torch.cuda.Stream:
+    """One extra stream per device for the concurrent attention launch."""
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    st = _SIDE_STREAMS.get(idx)
+    if st is None:
+        st = _SIDE_STREAMS[idx] = torch.cuda.Stream(torch.device("cuda", idx))
+    return st
+
+
 def _as_block_batch(x: torch.Tensor, bl: int) -> Optional[torch.Tensor]:
     """[B, H, 2*bl, ...] -> [2*B, H, bl, ...] as a view (block-major batch),
     or None when the strides do not allow a view."""
@@ -135,13 +147,10 @@ def _block_prefix_states(S_blocks: torch.Tensor, G_blocks: torch.Tensor, want: L
     c_{k+1}) S_k`` with ``c`` the exclusive prefix sum of G."""
     n = S_blocks.shape[0]
     c = torch.cat([torch.zeros_like(G_blocks[:1]), torch.cumsum(G_blocks, 0)], 0)     # [n+1, ...]
-    idx = torch.tensor(want, device=S_blocks.device)
-    ci = c.index_select(0, idx)                                                       # [w, ...]
-    diff = ci[:, None] - c[1:][None]                                                  # [w, n, ...]
-    k = torch.arange(n, device=S_blocks.device)
-    mask = (k[None, :] < idx[:, None]).view(len(want), n, *([1] * (diff.dim() - 2)))
-    w = torch.where(mask, torch.exp(torch.clamp(diff, max=0.0)), torch.zeros((), dtype=diff.dtype,
-                                                                             device=diff.device))
+    # weights [w, n, ...]: exp(c_i - c_{k+1}) for k < i, else 0 (built from host
+    # integers only: no host <-> device copy, so nothing here waits for the GPU)
+    k = torch.arange(n, device=S_blocks.device).view(n, *([1] * (G_blocks.dim() - 1)))
+    w = torch.stack([torch.where(k < i, torch.exp(torch.clamp(c[i] - c[1:], max=0.0)), 0.0) for i in want])
     if G_blocks.dim() == 3:                       # scalar decay per (b, h)
         return torch.einsum("wkbh,kbhjd->wbhjd", w, S_blocks)
     return torch.einsum("wkbhj,kbhjd->wbhjd", w, S_blocks)
@@ -229,7 +238,8 @@ def sharded_attention_core(Q, K, V, log_gamma, mix, r: int, sm_scale: float, gla
     order = [block_owner(i, world) for i in range(nb)]
     S_blocks = torch.stack([S_all[o][li * B:(li + 1) * B] for o, li in order])    # [nb, B, H, J, D]
     G_blocks = torch.stack([G_all[o][li * B:(li + 1) * B] for o, li in order])    # [nb, B, H(, J)]
-    starts = _block_prefix_states(S_blocks, G_blocks, [blocks[0][0] // bl, blocks[1][0] // bl, nb])
+    with torch.autocast(dev.type, enabled=False):                                # float32 state arithmetic
+        starts = _block_prefix_states(S_blocks, G_blocks, [blocks[0][0] // bl, blocks[1][0] // bl, nb])
     S_end = starts[2]
     mark("state_exchange")
 
@@ -253,7 +263,7 @@ def sharded_attention_core(Q, K, V, log_gamma, mix, r: int, sm_scale: float, gla
     Kv = KB.permute(1, 2, 0, 3)                     # [B, H, T, r] view
     Vv = VB.permute(1, 2, 0, 3)
     calls = [(Q[:, :, sl], e, a, sl) for (a, e), sl in zip(blocks, local)]
-    side = torch.cuda.Stream(dev) if Q.is_cuda else None
+    side = _side_stream(dev) if Q.is_cuda else None
     if side is not None:
         side.wait_stream(torch.cuda.current_stream(dev))
         with torch.cuda.stream(side):
