@@ -395,6 +395,8 @@ def run_ours(args):
         out["config4_seqpar"] = sp.pop("summary")
         out["decode_head_sharded"] = [measure_decode_head_sharded(dev, world, B=1),
                                       measure_config4_decode_head_sharded(dev, world, sp)]
+    if not args.no_config3:
+        out["config3"] = measure_config3(dev, world, rank)
     if not args.no_triton_reference and world == 1:
         out["triton_reference"] = measure_triton_reference(dev)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -822,6 +824,74 @@ def measure_layer_step(dev, B=4, steps=64, reps=5):
             "note": "QKV projection (cuBLAS) + fused decode step + out_proj per step, CUDA graph"}
 
 
+# ----------------------------------------------------------------------------- config 3: the 350M LM
+def measure_config3(dev, world, rank, batches=(1, 4, 64), prompt=16384, new=256):
+    """the 350M-shaped LM (24 layers, d_model 1024, 16
+    heads of 64, r = 16, SwiGLU 4096, RMSNorm, vocabulary 32000, tied
+    embedding, random init std 0.02, bf16) decodes `new` tokens greedily after
+    a `prompt`-token prompt of uniform random token ids (seed 1), from one
+    CUDA graph of two decode steps with the position and the sampling on the
+    device (``lm.DecodeEngine``).  A batch that splits evenly over the ranks
+    is batch-sharded (each rank prefills and decodes B/N sequences); smaller
+    ones run as independent replicas.  Device time of the whole generation
+    (CUDA events, max over ranks, after one untimed generation); the prompt's
+    prefill runs once per batch, outside the timed region.  Roofline: weights
+    plus every layer's outlier cache at the mean decode length, per step."""
+    import torch.distributed as dist
+    from outlierneuronattention_b200.lm import DecodeEngine, HofaLM, LMConfig
+    cfg = LMConfig()
+    torch.manual_seed(0)
+    model = HofaLM(cfg).to(device=dev, dtype=torch.bfloat16).eval()
+    nparam = model.num_parameters()
+    peak, kind = peaks()
+    rows = []
+    for Bg in batches:
+        shard = world > 1 and Bg >= world and Bg % world == 0
+        B = Bg // world if shard else Bg
+        g = torch.Generator().manual_seed(1 + (rank if (shard or world > 1) else 0))
+        idx = torch.randint(0, cfg.vocab_size, (B, prompt), generator=g).to(dev)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        logits0, caches, states = model.prefill(idx, prompt + new, batch_chunk=8)
+        torch.cuda.synchronize()
+        prefill_s = time.perf_counter() - t0
+        eng = DecodeEngine(model, caches, states, logits0, prompt)
+        eng.capture(new)
+        eng.generate(new)
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        toks = eng.generate(new)
+        e1.record()
+        torch.cuda.synchronize()
+        ms = torch.tensor([e0.elapsed_time(e1)], device=dev)
+        if world > 1:
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        ms = ms.item()
+        total = (Bg if shard else B * world) * new
+        per_step_bytes = nparam * 2 + B * cfg.num_layers * cfg.num_heads * (
+            (prompt + new // 2) * (cfg.r + 64) * 2 + (64 - cfg.r) * 64 * 4 * 2)
+        bound = B / (per_step_bytes / (peak * 1e9))
+        tps = total / (ms / 1e3)
+        rows.append({"batch": Bg, "mode": ("batch-sharded" if shard else ("replicas" if world > 1 else "one GPU")),
+                     "batch_per_rank": B, "tokens": total, "ms": round(ms, 3), "tokens_per_s": round(tps, 1),
+                     "us_per_step": round(1e3 * ms / new, 2), "prefill_s": round(prefill_s, 3),
+                     "hbm_bytes_per_step_per_rank": per_step_bytes,
+                     "roofline": {"bound": "hbm", "tokens_per_s_bound_per_rank": round(bound, 1),
+                                  "frac": round((tps / (total / new / B)) / bound, 4),
+                                  "peak_source": f"{kind} hbm_gbs"},
+                     "first_tokens": toks[0, :4].tolist()})
+        eng.release()
+        del eng, caches, states, logits0, toks
+        torch.cuda.empty_cache()
+    return {"workload": f"config3-350M-LM-decode-{new}-after-{prompt}", "params": nparam,
+            "model": "24 x (RMSNorm, HOFA layer, RMSNorm, SwiGLU 4096), vocab 32000, tied embedding, bf16, random init",
+            "sampling": "greedy, in the CUDA graph", "timing": "CUDA events around the graph replays, max over ranks",
+            "rows": rows}
+
+
 # ----------------------------------------------------------------------------- reference's Triton kernels
 REF_DIR = os.path.join(ROOT, "baseline", "_ref")
 
@@ -943,11 +1013,19 @@ def measure_triton_reference(dev):
         our_layer.load_state_dict(ref_layer.state_dict(), strict=True)
         x = torch.randn(4, 8192, 1024, device=dev, generator=torch.Generator(device=dev).manual_seed(8)) * 0.5
         lay = {}
+        with torch.no_grad():
+            # float32 (both libraries' float32 kernels): the layers agree to float32 rounding
+            xs32 = x[:1, :2048]
+            lay["forward_fp32_B1_T2048_maxabs_vs_ours"] = (ref_layer(xs32) - our_layer(xs32)).abs().max().item()
         with torch.no_grad(), torch.autocast("cuda", dtype=torch.bfloat16):
             yr = ref_layer(x)
             yo = our_layer(x)
             torch.cuda.synchronize()
+            # bf16: the two differ in where they round (the reference divides the bf16
+            # projection by d_h^(1/4), this library folds it into the weights; bf16 vs
+            # float32 gate arithmetic), so the difference is compared with the output's size
             lay["forward_config2_maxabs_vs_ours"] = (yr.float() - yo.float()).abs().max().item()
+            lay["forward_config2_max_abs_output"] = yr.float().abs().max().item()
             lay["forward_config2_ms"] = round(_event_ms(lambda: ref_layer(x), 3, flush), 4)
             lay["forward_config2_ms_ours"] = round(_event_ms(lambda: our_layer(x), 3, flush), 4)
         del x, yr, yo
@@ -1031,11 +1109,14 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-config3", action="store_true", help="skip the 350M-shaped LM decode (config 3)")
     ap.add_argument("--no-triton-reference", action="store_true",
                     help="skip timing the reference's own Triton kernels (baseline/_ref)")
     ap.add_argument("--no-prefill", action="store_true", help="skip the config-2 prefill measurement")
     ap.add_argument("--no-config4", action="store_true",
                     help="skip the config-4 (B=1, T=65536) prefill and long-cache decode measurement")
+    ap.add_argument("--profile-config3", action="store_true",
+                    help="only one graph replay of the 350M LM decode at --batch (for ncu captures)")
     ap.add_argument("--profile-prefill", action="store_true",
                     help="only the config-2 prefill kernels (for ncu captures); prints no bench line")
     ap.add_argument("--profile", action="store_true",
@@ -1045,6 +1126,24 @@ def main():
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args)
+    elif args.profile_config3:
+        # small, self-contained command for ncu: one graph replay (two decode steps) of the 350M LM at B=1
+        from outlierneuronattention_b200.lm import DecodeEngine, HofaLM, LMConfig
+        torch.cuda.set_device(0)
+        dev = torch.device("cuda", 0)
+        torch.manual_seed(0)
+        model = HofaLM(LMConfig()).to(device=dev, dtype=torch.bfloat16).eval()
+        idx = torch.randint(0, 32000, (args.batch, 16384), generator=torch.Generator().manual_seed(1)).to(dev)
+        logits0, caches, states = model.prefill(idx, 16384 + 8, batch_chunk=8)
+        eng = DecodeEngine(model, caches, states, logits0, 16384)
+        eng.capture(4)
+        eng.generate(2)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_push("decode")
+        eng.generate(2)
+        torch.cuda.synchronize()
+        torch.cuda.nvtx.range_pop()
+        print(json.dumps({"profile_config3": True, "batch": args.batch}))
     elif args.profile_prefill:
         # small, self-contained command for ncu: one warm-up and one timed prefill
         torch.cuda.set_device(0)
