@@ -228,6 +228,29 @@ int hofa_prep_fwd(const hofa_prep_args* args, void* stream);
 int hofa_decode_step_fwd(const hofa_decode_args* decode, const hofa_prep_args* prep, void* stream);
 
 /* ------------------------------------------------------------------------ */
+/* Decoder-LM harness: small-batch linear layer (decode steps).               */
+/* ------------------------------------------------------------------------ */
+typedef struct hofa_linear_args {
+  hofa_tensor x;           /* [M, K] input rows (M <= 8), or [M, 2K] = [gate | up] with input_mode 2 */
+  hofa_tensor weight;      /* [N, K] (nn.Linear layout), K % 8 == 0, K <= 4096 */
+  hofa_tensor norm_w;      /* [K] RMSNorm weight (input_mode 1) */
+  hofa_tensor residual;    /* optional [M, N], added to the product; may be y itself */
+  hofa_tensor y;           /* [M, N] output */
+  int32_t input_mode;      /* 0: x; 1: RMSNorm(x) * norm_w; 2: silu(gate) * up */
+  float eps;               /* RMSNorm epsilon */
+} hofa_linear_args;
+
+/* y = (residual +) transform(x) W^T for decode-sized batches, bf16 or f16:
+ * the projections and MLP of the decoder LM that surrounds the HOFA layer in
+ * the full-model decode benchmark (a SwiGLU / RMSNorm LM; the reference's own
+ * LM wrappers, src/HybridOutlierFactorizedAttention.py:425-513, run them as
+ * separate nn.Linear / LayerNorm / activation launches).  No counterpart
+ * operator in the reference.  The input transform (RMSNorm or the SwiGLU
+ * product, rounded to the activation dtype) and the residual add are fused
+ * into the weight-streaming kernel. */
+int hofa_lm_linear_fwd(const hofa_linear_args* args, void* stream);
+
+/* ------------------------------------------------------------------------ */
 const char* hofa_last_error(void);
 int32_t hofa_abi_version(void);
 

@@ -68,6 +68,10 @@ class PrepArgs(ctypes.Structure):
         ("R", c_int32), ("pos0", c_int32), ("pos0_dev", c_void_p), ("use_rope", c_int32)]
 
 
+class LinearArgs(ctypes.Structure):
+    _fields_ = _T("x", "weight", "norm_w", "residual", "y") + [("input_mode", c_int32), ("eps", c_float)]
+
+
 def _pack_format(cls) -> str:
     """struct format reproducing the C layout of ``cls`` (offsets from ctypes)."""
     fmt, pos = "<", 0
@@ -94,7 +98,7 @@ def _pack_format(cls) -> str:
     return fmt
 
 
-FORMATS = {cls: struct.Struct(_pack_format(cls)) for cls in (DecodeArgs, GlaArgs, OutlierArgs, PrepArgs)}
+FORMATS = {cls: struct.Struct(_pack_format(cls)) for cls in (DecodeArgs, GlaArgs, OutlierArgs, PrepArgs, LinearArgs)}
 
 ABSENT = (0, 0, 0, 1, 1, 1, 1, 0, 0, 0, 0)
 
@@ -134,7 +138,8 @@ def lib():
                     raise ImportError(f"{LIB_PATH} is missing: build it with "
                                       "`python -m outlierneuronattention_b200.build`")
                 L = ctypes.CDLL(LIB_PATH)
-                for fn in ("hofa_decode_fwd", "hofa_prefill_gla_fwd", "hofa_prefill_outlier_fwd", "hofa_prep_fwd"):
+                for fn in ("hofa_decode_fwd", "hofa_prefill_gla_fwd", "hofa_prefill_outlier_fwd", "hofa_prep_fwd",
+                           "hofa_lm_linear_fwd"):
                     getattr(L, fn).restype = ctypes.c_int
                     getattr(L, fn).argtypes = [c_void_p, c_void_p]
                 L.hofa_decode_step_fwd.restype = ctypes.c_int

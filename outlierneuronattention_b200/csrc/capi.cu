@@ -137,9 +137,19 @@ int env_int(const char* name, int dflt) {
   return (v != nullptr && v[0] != '\0') ? atoi(v) : dflt;
 }
 const bool kDecodeNoBulk = env_int("HOFA_DECODE_NO_BULK", 0) != 0;
-const int kDecodeWarps = env_int("HOFA_DECODE_WARPS", 4) == 8 ? 8 : 4;
+const int kDecodeWarps = [] {
+  const int w = env_int("HOFA_DECODE_WARPS", 4);
+  return (w == 6 || w == 8) ? w : 4;
+}();
 const bool kDecodeNoL2Prefetch = env_int("HOFA_DECODE_NO_L2_PREFETCH", 0) != 0;
 const int kDecodeStages = env_int("HOFA_DECODE_STAGES", 0);  // 0: choose by shape
+// Steps of up to this many MB of cache rows ask L2 to prefetch the first
+// window of their ring (the chunks loaded first) before the grid dependency.
+// Measured at the 4096-token config 1: B = 4 10.77 -> 10.49 us per step with
+// the windowed prefetch; prefetching a split's whole range instead was slower
+// above 24 MB (11.17 us at B = 4).
+const int kDecodePrefetchMaxMB = env_int("HOFA_DECODE_PREFETCH_MAX_MB", 100);
+const bool kDecodePrefetchWindow = env_int("HOFA_DECODE_PREFETCH_WINDOW", 1) != 0;
 
 bool supported_d(int64_t D) { return D == 32 || D == 64 || D == 128; }
 
@@ -277,10 +287,9 @@ int decode_setup(const hofa_decode_args* a, hofa::DecodeParams& p, int& path, bo
     if ((int64_t)B * H * split > (per_sm8 > 0 ? per_sm8 : 1) * (int64_t)sms) p.stages = 4;
   }
   p.consumer_warps = kDecodeWarps;
-  // L2 prefetch before the grid dependency only for small steps (up to 24 MB
-  // of cache rows: measured faster at B = 1 and 2 of the 4096-token config,
-  // slower at B = 4, whose 42 MB step keeps HBM busy without it)
-  p.no_l2_prefetch = kDecodeNoL2Prefetch || (double)B * H * (a->seq_len_dev ? L : a->seq_len) * (R + D) * es > 24e6;
+  p.no_l2_prefetch = kDecodeNoL2Prefetch ||
+                     (double)B * H * (a->seq_len_dev ? L : a->seq_len) * (R + D) * es > kDecodePrefetchMaxMB * 1e6;
+  p.prefetch_window = kDecodePrefetchWindow;
   if (kDecodeStages >= 2 && kDecodeStages <= 16) p.stages = kDecodeStages;
   p.stages = ((p.stages + p.consumer_warps - 1) / p.consumer_warps) * p.consumer_warps;
   const size_t ring_budget = 200 * 1024;  // dynamic shared memory of the ring (the kernel adds ~12 KB static)

@@ -26,6 +26,7 @@
 //       memory.
 //   decode_reg_kernel   -- any strides: 16-byte (or scalar) register loads.
 #include <float.h>
+#include <cstdlib>
 
 #include <cooperative_groups.h>
 
@@ -477,6 +478,7 @@ __device__ __forceinline__ void prep_new_token(const DecodeParams& p, int s, int
 }
 
 constexpr int kBulkChunk = 64;  // tokens per bulk chunk (two warp tiles)
+
 // Warps: NW consumers, then the TMA producer (warp NW), then the GLA warp
 // (warp NW + 1), which updates this split's GLA state rows and its part of
 // y_I while the consumers stream the cache.
@@ -551,6 +553,7 @@ decode_bulk_kernel(const DecodeParams p) {
   if (warp == NW && lane == 0 && p.seq_len_dev == nullptr && p.R > 0 && !p.no_l2_prefetch) {
     int tb, te;
     split_range(p.seq_len, tb, te);
+    if (p.prefetch_window) te = min(te, tb + NST * kBulkChunk);  // only the chunks the ring loads first
     if (te > tb) {
       const char* kg = reinterpret_cast<const char*>(p.cache_k) + (b * p.sck[0] + h * p.sck[1] + (int64_t)tb * R) * sizeof(T);
       const char* vg = reinterpret_cast<const char*>(p.cache_v) + (b * p.scv[0] + h * p.scv[1] + (int64_t)tb * D) * sizeof(T);
@@ -694,14 +697,25 @@ cudaError_t launch_bulk(const DecodeParams& p, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+// HOFA_DECODE_NO_CLUSTER (read once at library load): combine the splits of a
+// head through the workspace even when they would fit in one cluster.
+const bool kDecodeNoCluster = [] {
+  const char* v = getenv("HOFA_DECODE_NO_CLUSTER");
+  return v != nullptr && v[0] != '\0' && v[0] != '0';
+}();
+
 template <typename T, int D>
 cudaError_t launch_d(const DecodeParams& p, int path, bool alpha, cudaStream_t st) {
   dim3 grid(p.split_k, p.H, p.B);
   if (path == 2) {
-    const bool cluster = p.split_k > 1 && p.split_k <= kMaxClusterSplit;
+    const bool cluster = p.split_k > 1 && p.split_k <= kMaxClusterSplit && !kDecodeNoCluster;
     if (p.fused_prep) {  // decode step with the new token's prep (4 consumer warps)
       if (cluster) return alpha ? launch_bulk<T, D, true, true, 4, true>(p, st) : launch_bulk<T, D, false, true, 4, true>(p, st);
       return alpha ? launch_bulk<T, D, true, false, 4, true>(p, st) : launch_bulk<T, D, false, false, 4, true>(p, st);
+    }
+    if (p.consumer_warps == 6) {
+      if (cluster) return alpha ? launch_bulk<T, D, true, true, 6, false>(p, st) : launch_bulk<T, D, false, true, 6, false>(p, st);
+      return alpha ? launch_bulk<T, D, true, false, 6, false>(p, st) : launch_bulk<T, D, false, false, 6, false>(p, st);
     }
     if (p.consumer_warps == 8) {
       if (cluster) return alpha ? launch_bulk<T, D, true, true, 8, false>(p, st) : launch_bulk<T, D, false, true, 8, false>(p, st);

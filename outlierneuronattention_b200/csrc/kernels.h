@@ -31,8 +31,9 @@ struct DecodeParams {
   int* ws_count;
   int* ws_status;
   int stages;                 // bulk ring depth (64-token chunks)
-  int consumer_warps;         // bulk kernel consumer warps: 4 or 8
+  int consumer_warps;         // bulk kernel consumer warps: 4, 6 or 8
   bool no_l2_prefetch;        // bulk kernel: skip the L2 prefetch of the cache rows before the grid dependency
+  bool prefetch_window;       // bulk kernel: that prefetch covers only the ring's first window of chunks
   // hofa_decode_step_fwd (bulk kernel): the new token's gates, RoPE and cache
   // row are computed in the same launch.  q, k, v are then un-rotated; the
   // cache is streamed over rows [0, seq_len - 1) and the new token (row

@@ -28,8 +28,22 @@ import torch
 import torch.nn as nn
 import torch.nn.functional as F
 
+from . import _capi
+from ._capi import LinearArgs, flat, tview
 from .config import ModelConfig
+from .hofa_decode import fused_hofa_decode_step
 from .layer import HybridOutlierFactorizedAttention
+
+
+def lm_linear(x: torch.Tensor, weight: torch.Tensor, y: torch.Tensor, *, norm_w: Optional[torch.Tensor] = None,
+              residual: Optional[torch.Tensor] = None, mode: int = 0, eps: float = 1e-6) -> torch.Tensor:
+    """``y = (residual +) transform(x) @ weight.T`` for decode-sized batches
+    (``hofa_lm_linear_fwd``): x [M, K] (or [M, 2K] = [gate | up] with mode 2),
+    weight [N, K], y [M, N], M <= 8, bf16/f16.  mode 0: x; 1: RMSNorm(x) *
+    norm_w; 2: silu(gate) * up.  ``residual`` may be ``y`` itself."""
+    vals = flat(tview(x), tview(weight), tview(norm_w), tview(residual), tview(y), int(mode), float(eps))
+    _capi.call("hofa_lm_linear_fwd", LinearArgs, vals, _capi.stream_handle(x.device))
+    return y
 
 
 @dataclass
@@ -128,17 +142,53 @@ class HofaLM(nn.Module):
             last.append(self.logits(x[:, -1]))
         return torch.cat(last, 0), caches, states
 
-    def step(self, tok: torch.Tensor, caches, states, pos_dev: torch.Tensor, flip: bool):
+    def fused_step_ok(self, B: int) -> bool:
+        """Whether a decode step of B sequences runs on the fused small-batch path."""
+        return B <= 8 and self.embed.weight.dtype in (torch.bfloat16, torch.float16) and self.embed.weight.is_cuda
+
+    def step(self, tok: torch.Tensor, caches, states, pos_dev: torch.Tensor, flip: bool, fused: Optional[bool] = None):
         """One decode step for tokens ``tok`` [B, 1] at the device position
         ``pos_dev`` (int32 [1]: rows already in the caches).  ``flip`` selects
-        the direction of the GLA state ping-pong.  Returns logits [B, vocab]."""
-        x = self.embed(tok)
-        for blk, cache, (s0, s1) in zip(self.blocks, caches, states):
-            st = (s1, s0) if flip else (s0, s1)
-            y, _, _ = blk.attn.forward_step(blk.attn_norm(x), cache, st, cache_seq_len=pos_dev)
-            x = x + y
-            x = x + blk.mlp(blk.mlp_norm(x))
-        return self.logits(x[:, -1])
+        the direction of the GLA state ping-pong.  Returns logits [B, vocab].
+
+        Up to 8 sequences in bf16/f16 (``fused``, the default there) a layer is
+        five launches: RMSNorm + QKV projection, the layer's one-launch decode
+        step (gates, RoPE, cache append, attention core), out-projection +
+        residual, RMSNorm + gate/up projection, SwiGLU + down-projection +
+        residual (``hofa_lm_linear_fwd`` streams each weight once).  Otherwise
+        the modules run as written (the layer's ``forward_step``, nn.Linear)."""
+        B = tok.shape[0]
+        if fused is None:
+            fused = self.fused_step_ok(B)
+        if not fused:
+            x = self.embed(tok)
+            for blk, cache, (s0, s1) in zip(self.blocks, caches, states):
+                st = (s1, s0) if flip else (s0, s1)
+                y, _, _ = blk.attn.forward_step(blk.attn_norm(x), cache, st, cache_seq_len=pos_dev)
+                x = x + y
+                x = x + blk.mlp(blk.mlp_norm(x))
+            return self.logits(x[:, -1])
+        cfg = self.cfg
+        H, dh = cfg.num_heads, cfg.d_model // cfg.num_heads
+        x = self.embed(tok).view(B, cfg.d_model)
+        seq_len = pos_dev + 1                        # rows attended: the cached ones and the new one
+        qkv = torch.empty(B, 3 * cfg.d_model, device=x.device, dtype=x.dtype)
+        gu = torch.empty(B, 2 * cfg.d_mlp, device=x.device, dtype=x.dtype)
+        for blk, (ck, cv), (s0, s1) in zip(self.blocks, caches, states):
+            at = blk.attn
+            s_in, s_out = (s1, s0) if flip else (s0, s1)
+            lm_linear(x, at._qkv_weight(), qkv, norm_w=blk.attn_norm.weight, mode=1, eps=blk.attn_norm.eps)
+            q, k, v = (t.transpose(1, 2) for t in qkv.view(B, 1, 3, H, dh).unbind(2))
+            cos, sin = at._rope_tables(ck.shape[2])
+            y, _, _ = fused_hofa_decode_step(
+                q, k, v, ck, cv, s_in, s_out, at.gla_scale.view(H, dh), at.r, ck.shape[2], (dh / at.r) ** 0.5,
+                cos=cos, sin=sin, seq_len_dev=seq_len, log_alpha=at.log_alpha if at.learnable_alpha else None,
+                **at._gate_kwargs())
+            lm_linear(y.reshape(B, cfg.d_model), at.out_proj.weight, x, residual=x)
+            lm_linear(x, blk.mlp.gate_up.weight, gu, norm_w=blk.mlp_norm.weight, mode=1, eps=blk.mlp_norm.eps)
+            lm_linear(gu, blk.mlp.down.weight, x, residual=x, mode=2)
+        logits = torch.empty(B, cfg.vocab_size, device=x.device, dtype=x.dtype)
+        return lm_linear(x, self.embed.weight, logits, norm_w=self.norm.weight, mode=1, eps=self.norm.eps)
 
 
 def sample_tokens(logits: torch.Tensor, temperature: float, top_k: int) -> torch.Tensor:

@@ -42,6 +42,7 @@ STRUCTS = {
     "hofa_gla_args": (_capi.GlaArgs, [f for f, _ in _capi.GlaArgs._fields_]),
     "hofa_outlier_args": (_capi.OutlierArgs, [f for f, _ in _capi.OutlierArgs._fields_]),
     "hofa_prep_args": (_capi.PrepArgs, [f for f, _ in _capi.PrepArgs._fields_]),
+    "hofa_linear_args": (_capi.LinearArgs, [f for f, _ in _capi.LinearArgs._fields_]),
 }
 
 
