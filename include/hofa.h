@@ -247,7 +247,10 @@ typedef struct hofa_linear_args {
  * separate nn.Linear / LayerNorm / activation launches).  No counterpart
  * operator in the reference.  The input transform (RMSNorm or the SwiGLU
  * product, rounded to the activation dtype) and the residual add are fused
- * into the weight-streaming kernel. */
+ * into the weight-streaming kernel.  Launched as a programmatic dependent
+ * launch whose weight fetch starts before the previous kernel on the stream
+ * has finished: the weight and norm_w must not be written by the kernel
+ * immediately before this call on the stream (x and residual may be). */
 int hofa_lm_linear_fwd(const hofa_linear_args* args, void* stream);
 
 /* ------------------------------------------------------------------------ */

@@ -9,13 +9,19 @@
 //
 // At decode batch sizes a projection is a matrix-vector product: every weight
 // is read once and used M times, so the kernel streams W at HBM speed with
-// 16-byte loads and does the few FMAs per element on the CUDA cores.  One CTA
-// per SM (grid-stride over row groups): each CTA first issues its first row
-// group's weight loads, then stages the transformed input rows in shared
+// 16-byte loads and does the few FMAs per element on the CUDA cores.  Two CTAs
+// of 8 warps per SM (grid-stride over row groups).  The kernel is launched
+// with programmatic dependent launch: each warp issues its first row group's
+// weight loads BEFORE waiting for the previous kernel of the stream (the
+// weights are parameters: no kernel of a decode loop writes them, so they may
+// be read while the kernel that produces x is still running), then waits,
+// releases the next kernel, and stages the transformed input rows in shared
 // memory (the norm's reduction and the SwiGLU product happen here, once per
-// CTA), so the staging latency hides behind the first weight round trip.
-// Each warp owns a group of rows; all of a group's loads are in flight before
-// the first FMA.  The warp reduction leaves one sum per (row, m) in lane m.
+// CTA).  So the weight fetch of every projection overlaps the end of the
+// kernel before it.  Contract: the weight, norm_w and any memory other than
+// x and residual must not be written by the kernel immediately preceding
+// this launch on the stream.  All of a row group's loads are in flight before
+// its first FMA; the warp reduction leaves one sum per (row, m) in lane m.
 #include <cstdio>
 
 #include "common.cuh"
@@ -33,7 +39,7 @@ struct LinearParams {
 
 namespace {
 
-constexpr int kLinWarps = 16;
+constexpr int kLinWarps = 8;
 constexpr int kLinThreads = kLinWarps * 32;
 constexpr int kMaxM = 8;
 
@@ -56,7 +62,7 @@ __device__ __forceinline__ uint4 pack8(const float f[8]) {
 // KCH: 16-byte weight chunks per lane per row (K / 256 for 2-byte types);
 // RG: rows per warp group (all RG*KCH loads in flight together).
 template <typename T, int MODE, bool RES, int KCH, int RG>
-__global__ void __launch_bounds__(kLinThreads, 1) lm_linear_kernel(const LinearParams p) {
+__global__ void __launch_bounds__(kLinThreads, 2) lm_linear_kernel(const LinearParams p) {
   static_assert(sizeof(T) == 2, "2-byte activations");
   extern __shared__ __align__(16) unsigned char smem_raw[];
   T* sxin = reinterpret_cast<T*>(smem_raw);          // [M][K]
@@ -83,6 +89,10 @@ __global__ void __launch_bounds__(kLinThreads, 1) lm_linear_kernel(const LinearP
     }
   };
   if (g < groups) issue(g);
+  // x / residual come from the kernels before: wait for them, then let the
+  // next kernel of the stream start its own weight fetch
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 
   // stage the transformed input rows
   const T* X = reinterpret_cast<const T*>(p.x);
@@ -204,8 +214,19 @@ cudaError_t launch_k(const LinearParams& p, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     const int groups = (p.N + rg - 1) / rg;
     int grid = (groups + kLinWarps - 1) / kLinWarps;
-    if (grid > sms) grid = sms;
-    kern<<<grid, kLinThreads, smem, st>>>(p);
+    if (grid > 2 * sms) grid = 2 * sms;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(kLinThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kern, p);
+    if (e != cudaSuccess) return e;
     return cudaGetLastError();
   };
   if (p.K <= 1024) return go(lm_linear_kernel<T, MODE, RES, 4, 2>, 2);
