@@ -401,6 +401,7 @@ def run_ours(args):
         out["triton_reference"] = measure_triton_reference(dev)
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         out["cpu_baseline"] = cpu_baseline(B, args.cpu_seconds)
+        out["cpu_baseline"]["reference_layer"] = cpu_reference_layer(B, args.cpu_seconds / 2)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
@@ -1080,6 +1081,53 @@ def cpu_baseline(B: int, seconds: float):
     return {"value": round(value, 2), "unit": "tokens/s", "cores": torch.get_num_threads(), "kind": "port",
             "sample": f"{n} decode steps of config 1 (B={B}, L={L}) in float32, {el:.1f} s",
             "ms_per_step": round(1e3 * el / n, 3)}
+
+
+def cpu_reference_layer(B: int, seconds: float):
+    """The reference's own CPU PyTorch path for one decode step of the layer:
+    ``HybridOutlierFactorizedAttentionTrain.forward_step``
+    (src/HybridOutlierFactorizedAttentionTrain.py:298-438), imported
+    unmodified from baseline/_ref, at config 1 (d_model 1024, H=16, r=16,
+    B sequences with 4095 cached rows, so every step attends 4096), float32
+    and bfloat16, all host threads; projections, gates, RoPE, the cache
+    concatenation, the attention core and out_proj per step -- the work of
+    this library's ``layer_step`` figure."""
+    if not os.path.isdir(os.path.join(REF_DIR, "src")):
+        return {"unavailable": "baseline/_ref is not installed"}
+    sys.path.insert(0, REF_DIR)
+    try:
+        from src.config import ModelConfig as RefConfig
+        from src.HybridOutlierFactorizedAttentionTrain import HybridOutlierFactorizedAttention as RefTrain
+    except Exception as e:  # noqa: BLE001
+        return {"unavailable": f"import of the reference failed: {e!r}"}
+    finally:
+        if REF_DIR in sys.path:
+            sys.path.remove(REF_DIR)
+    torch.set_num_threads(max(1, len(os.sched_getaffinity(0))))
+    out = {"path": "HybridOutlierFactorizedAttentionTrain.forward_step, unmodified (baseline/_ref), CPU",
+           "cores": torch.get_num_threads(), "workload": f"config1-layer-forward_step-B{B}-L{L}"}
+    for dt in (torch.float32, torch.bfloat16):
+        torch.manual_seed(0)
+        layer = RefTrain(RefConfig(d_model=1024, num_heads=H, num_layers=1, r=R, chunk_size=64)).eval().to(dt)
+        g = torch.Generator().manual_seed(6)
+        x = torch.randn(B, 1, 1024, generator=g).to(dt)
+        cache = ((torch.randn(B, H, L - 1, R, generator=g) * KEY_STD).to(dt),
+                 (torch.randn(B, H, L - 1, D, generator=g) * VAL_STD).to(dt))
+        state = torch.randn(B, H, D, D, generator=g) * 0.1
+        state[:, :, J:] = 0
+        with torch.no_grad():
+            for _ in range(2):
+                layer.forward_step(x, cache, state)
+            n, t0 = 0, time.perf_counter()
+            while True:
+                layer.forward_step(x, cache, state)
+                n += 1
+                el = time.perf_counter() - t0
+                if el >= seconds and n >= 3:
+                    break
+        out[str(dt).replace("torch.", "")] = {"ms_per_step": round(1e3 * el / n, 3), "tokens_per_s": round(B * n / el, 2),
+                                               "steps": n}
+    return out
 
 
 def run_reference(args):

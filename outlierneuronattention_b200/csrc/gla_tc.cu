@@ -64,7 +64,7 @@ struct Geo {
   // A, Y1 and Y2 side by side (512 columns, one CTA per SM)
   static constexpr bool SHARE = D == 64;
   static constexpr uint32_t OUT_COLS = SHARE ? 128 : 512;
-  static constexpr size_t STATE_SMEM = 2 * OP + 1024 + 256;
+  static constexpr size_t STATE_SMEM = 3 * OP + 1024 + 256;   // K (then Kd hi), V, Kd lo
   // D = 64: 80 KB keeps <= 2 CTAs (2 x 256 TMEM columns) per SM; D = 128: one CTA
   static constexpr size_t OUT_SMEM = 4 * OP + 1024 + 4096;
 };
@@ -111,7 +111,8 @@ gla_tc_state_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   unsigned char* sK = base;
   unsigned char* sV = base + Gm::OP;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(base + 2 * Gm::OP);
+  unsigned char* sL = base + 2 * Gm::OP;   // Kd lo
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + 3 * Gm::OP);
   float* sm_warp = reinterpret_cast<float*>(bars + 4);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm_warp + 4);
   int* err = reinterpret_cast<int*>(tmem_slot + 1);
@@ -156,20 +157,20 @@ gla_tc_state_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
   // the fp32 state keeps about 16 significant bits of every key instead of
   // the 8 of a single bf16 operand.  The reference rounds Kd once
   // (src/chunk_gla_inlier.py:122-125); that alone puts about 2e-2 of absolute
-  // error into a state of magnitude 10 over 8192 tokens.  The two products
-  // accumulate into the same TMEM columns; hi goes first, lo waits in
-  // registers until the first MMA has read the shared-memory tile.
-  uint4 lo_regs[Gm::NB][8];
+  // error into a state of magnitude 10 over 8192 tokens.  hi replaces the K
+  // tile, lo has a tile of its own, and both products accumulate into the same
+  // TMEM columns under one commit.
   {
     const float w = sm100::ex2_approx((gc - G) * kLog2e);
 #pragma unroll
     for (int nb = 0; nb < Gm::NB; ++nb) {
       uint4* row = reinterpret_cast<uint4*>(sK + nb * kTile + tid * 128);
+      uint4* lrow = reinterpret_cast<uint4*>(sL + nb * kTile + tid * 128);
 #pragma unroll
       for (int q = 0; q < 8; ++q) {
-        uint4 u = row[q];
+        uint4 u = row[q], l;
         uint32_t* pu = reinterpret_cast<uint32_t*>(&u);
-        uint32_t* pl = reinterpret_cast<uint32_t*>(&lo_regs[nb][q]);
+        uint32_t* pl = reinterpret_cast<uint32_t*>(&l);
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
           float a, bb;
@@ -183,35 +184,28 @@ gla_tc_state_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
           pl[e] = pack2(xa - ha, xb - hb, BF16);
         }
         row[q] = u;
+        lrow[q] = l;
       }
     }
   }
-  const uint64_t adesc = sm100::smem_desc(sK, Gm::LBO, 1024, sm100::kSwizzle128);
-  const uint64_t bdesc = sm100::smem_desc(sV, Gm::LBO, 1024, sm100::kSwizzle128);
-#pragma unroll 1
-  for (int term = 0; term < 2; ++term) {
-    if (term == 1) {  // the hi product has completed: its operand tile may be overwritten with lo
-#pragma unroll
-      for (int nb = 0; nb < Gm::NB; ++nb) {
-        uint4* row = reinterpret_cast<uint4*>(sK + nb * kTile + tid * 128);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) row[q] = lo_regs[nb][q];
-      }
-    }
-    fence_async_smem();
-    sm100::tc_fence_before();
-    __syncthreads();
-    if (tid == 0 && !*verr) {
-      sm100::tc_fence_after();
-#pragma unroll
-      for (int ks = 0; ks < kC / 16; ++ks)
-        sm100::mma_ss(tmem, adesc + (uint64_t)(ks * 2048 >> 4), bdesc + (uint64_t)(ks * 2048 >> 4), IDESC,
-                      term > 0 || ks > 0);
-      sm100::mma_commit(&bars[1]);
-    }
-    if (!*verr && !sm100::mbar_wait(&bars[1], term)) atomicOr(err, 1);
+  fence_async_smem();
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (tid == 0 && !*verr) {
     sm100::tc_fence_after();
+    const uint64_t adesc = sm100::smem_desc(sK, Gm::LBO, 1024, sm100::kSwizzle128);
+    const uint64_t ldesc = sm100::smem_desc(sL, Gm::LBO, 1024, sm100::kSwizzle128);
+    const uint64_t bdesc = sm100::smem_desc(sV, Gm::LBO, 1024, sm100::kSwizzle128);
+#pragma unroll
+    for (int ks = 0; ks < kC / 16; ++ks)
+      sm100::mma_ss(tmem, adesc + (uint64_t)(ks * 2048 >> 4), bdesc + (uint64_t)(ks * 2048 >> 4), IDESC, ks > 0);
+#pragma unroll
+    for (int ks = 0; ks < kC / 16; ++ks)
+      sm100::mma_ss(tmem, ldesc + (uint64_t)(ks * 2048 >> 4), bdesc + (uint64_t)(ks * 2048 >> 4), IDESC, true);
+    sm100::mma_commit(&bars[1]);
   }
+  if (!*verr && !sm100::mbar_wait(&bars[1], 0)) atomicOr(err, 1);
+  sm100::tc_fence_after();
   // D (M = 64): row j lives in lane 32*(j/16) + j%16; (M = 128): row j in lane j
   const int j = Gm::STATE_M == 64 ? 16 * warp + lane : tid;
   const bool row_ok = (Gm::STATE_M == 64 ? lane < 16 : true) && j < p.J && !*verr;
@@ -510,491 +504,6 @@ gla_tc_out_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
   if (warp == 0) sm100::tmem_dealloc(tmem, Gm::OUT_COLS);
 }
 
-// ---------------------------------------------------------------------------
-// Segment-parallel path (head dim 64).  A head's chunks are cut into NSEG
-// segments of CPS consecutive chunks; one CTA per segment in both passes:
-//
-//   S1 gla_seg_state_kernel  the segment's state from a zero start,
-//        dS_seg = sum_t exp(G_end - G_t) k_t v_t^T  (G cumulative over the
-//        segment, every factor <= 1), accumulated in TMEM over the segment's
-//        chunks (keys as hi + lo terms) and written once with G_end;
-//   S2 gla_seg_scan_kernel   start state of every segment (fp32), final state;
-//   S3 gla_seg_out_kernel    walks the segment's chunks in order with the
-//        running state S in TMEM (fp32): per chunk A = Q K^T, Y2 = Q S (S as
-//        a bf16 operand, as in the reference), P = A * decay mask, Y1 = P V,
-//        S <- exp(G_C) S + Kd^T V, and the fused epilogue.
-//
-// Against the chunk-wise kernels above this reads K and V twice instead of
-// K/V twice plus a per-chunk fp32 state round trip through the workspace
-// (write, scan read and write, output read).
-// ---------------------------------------------------------------------------
-constexpr int kSegStages = 2;
-
-constexpr int kMaxSegChunksHost = 128;   // chunks per segment (kernel shared arrays)
-
-struct SegGeo {
-  int nc, cps, nseg;
-};
-inline SegGeo seg_geometry(int64_t B, int64_t H, int64_t T, int sms) {
-  SegGeo g;
-  g.nc = (int)((T + kC - 1) / kC);
-  int64_t ns = (2 * (int64_t)sms + B * H - 1) / (B * H);   // about two CTAs per SM in one wave
-  if (ns < 1) ns = 1;
-  if (ns > g.nc) ns = g.nc;
-  if (ns < (g.nc + kMaxSegChunksHost - 1) / kMaxSegChunksHost) ns = (g.nc + kMaxSegChunksHost - 1) / kMaxSegChunksHost;
-  g.cps = (int)((g.nc + ns - 1) / ns);
-  g.nseg = (g.nc + g.cps - 1) / g.cps;
-  return g;
-}
-
-// Chunk totals of the log decay over this segment's chunks -> sm_gc[c], and
-// suffix sums sm_suf[c] = sum_{c' > c} sm_gc[c'].  Every thread takes part.
-__device__ __forceinline__ void seg_chunk_totals(const GlaParams& p, int b, int h, int c0, int nch, float* sm_gc,
-                                                 float* sm_suf, float (*sm_part)[4], int tid) {
-  const int lane = tid & 31, warp = tid >> 5;
-  for (int c = 0; c < nch; ++c) {
-    const int t = (c0 + c) * kC + tid;
-    const float g = t < p.T ? ld_any(p.log_gamma, p.dt_lg, b * p.slg[0] + h * p.slg[1] + (int64_t)t * p.slg[2]) : 0.f;
-    const float sw = warp_sum(g);
-    if (lane == 0) sm_part[c][warp] = sw;
-  }
-  __syncthreads();
-  if (tid < nch) sm_gc[tid] = sm_part[tid][0] + sm_part[tid][1] + sm_part[tid][2] + sm_part[tid][3];
-  __syncthreads();
-  if (tid == 0) {
-    float acc = 0.f;
-    for (int c = nch - 1; c >= 0; --c) { sm_suf[c] = acc; acc += sm_gc[c]; }
-  }
-  __syncthreads();
-}
-
-constexpr int kMaxSegChunks = kMaxSegChunksHost;
-
-template <typename T>
-__global__ void __launch_bounds__(kThreads)
-gla_seg_state_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
-                     const GlaParams p, const int cps, const int nseg) {
-  constexpr int D = 64;
-  constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
-  constexpr uint32_t IDESC = sm100::idesc_f16(BF16, true, true, 64, D);
-  extern __shared__ unsigned char smem_raw[];
-  unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  unsigned char* sK = base;                              // [stage] K tiles (become Kd hi)
-  unsigned char* sV = base + kSegStages * kTile;         // [stage] V tiles
-  unsigned char* sL = base + 2 * kSegStages * kTile;     // [stage] Kd lo
-  __shared__ __align__(8) uint64_t full[kSegStages], done[kSegStages];
-  __shared__ float sm_gc[kMaxSegChunks], sm_suf[kMaxSegChunks], sm_part[kMaxSegChunks][4], sm_warp[4];
-  __shared__ uint32_t tmem_slot;
-  __shared__ int err;
-
-  const int sg = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int bh = b * p.H + h;
-  const int c0 = sg * cps;
-  const int nch = min(cps, p.nseg - c0);   // p.nseg holds the chunk count of a head here
-  if (tid == 0) {
-    for (int i = 0; i < kSegStages; ++i) { sm100::mbar_init(&full[i], 1); sm100::mbar_init(&done[i], 1); }
-    err = 0;
-    sm100::fence_mbar_init();
-  }
-  if (warp == 0) { sm100::tmem_alloc(&tmem_slot, 64); sm100::tmem_relinquish(); }
-  sm100::tc_fence_before();
-  __syncthreads();
-  sm100::tc_fence_after();
-  const uint32_t tmem = tmem_slot;
-  auto load = [&](int c) {
-    const int st = c % kSegStages;
-    sm100::mbar_arrive_expect_tx(&full[st], 2 * kTile);
-    sm100::tma_load_4d(sK + st * kTile, &tk, p.R, (c0 + c) * kC, h, b, &full[st]);
-    sm100::tma_load_4d(sV + st * kTile, &tv, 0, (c0 + c) * kC, h, b, &full[st]);
-  };
-  if (tid == 0)
-    for (int c = 0; c < min(kSegStages, nch); ++c) load(c);
-  seg_chunk_totals(p, b, h, c0, nch, sm_gc, sm_suf, sm_part, tid);
-  volatile int* verr = &err;
-  const uint64_t vdesc0 = sm100::smem_desc(sV, 16, 1024, sm100::kSwizzle128);
-  for (int c = 0; c < nch; ++c) {
-    const int st = c % kSegStages;
-    const int t = (c0 + c) * kC + tid;
-    const float g = t < p.T ? ld_any(p.log_gamma, p.dt_lg, b * p.slg[0] + h * p.slg[1] + (int64_t)t * p.slg[2]) : 0.f;
-    const float G = block_scan128(g, sm_warp, tid);          // inclusive, within the chunk
-    // weight of this token's key in the segment's end state: exp(G_end - G_t) <= 1
-    const float w = sm100::ex2_approx((sm_suf[c] + sm_gc[c] - G) * kLog2e);
-    if (!*verr && !sm100::mbar_wait(&full[st], (c / kSegStages) & 1)) atomicOr(&err, 1);
-    uint4* row = reinterpret_cast<uint4*>(sK + st * kTile + tid * 128);
-    uint4* lrow = reinterpret_cast<uint4*>(sL + st * kTile + tid * 128);
-#pragma unroll
-    for (int q = 0; q < 8; ++q) {
-      uint4 u = row[q], l;
-      uint32_t* pu = reinterpret_cast<uint32_t*>(&u);
-      uint32_t* pl = reinterpret_cast<uint32_t*>(&l);
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float a, bb, ha, hb;
-        if (BF16) bf16x2_to_f(pu[e], a, bb); else f16x2_to_f(pu[e], a, bb);
-        const float xa = a * w, xb = bb * w;
-        pu[e] = pack2(xa, xb, BF16);
-        if (BF16) bf16x2_to_f(pu[e], ha, hb); else f16x2_to_f(pu[e], ha, hb);
-        pl[e] = pack2(xa - ha, xb - hb, BF16);
-      }
-      row[q] = u;
-      lrow[q] = l;
-    }
-    fence_async_smem();
-    sm100::tc_fence_before();
-    __syncthreads();
-    if (tid == 0 && !*verr) {
-      sm100::tc_fence_after();
-      // the previous chunk's stage is refilled once its MMAs have read it
-      if (c >= 1 && c - 1 + kSegStages < nch) {
-        if (!sm100::mbar_wait(&done[(c - 1) % kSegStages], ((c - 1) / kSegStages) & 1)) atomicOr(&err, 1);
-        else load(c - 1 + kSegStages);
-      }
-      const uint64_t hdesc = sm100::smem_desc(sK + st * kTile, 16, 1024, sm100::kSwizzle128);
-      const uint64_t ldesc = sm100::smem_desc(sL + st * kTile, 16, 1024, sm100::kSwizzle128);
-      const uint64_t vdesc = vdesc0 + (uint64_t)((st * kTile) >> 4);
-#pragma unroll
-      for (int ks = 0; ks < kC / 16; ++ks)
-        sm100::mma_ss(tmem, hdesc + (uint64_t)(ks * 2048 >> 4), vdesc + (uint64_t)(ks * 2048 >> 4), IDESC, c > 0 || ks > 0);
-#pragma unroll
-      for (int ks = 0; ks < kC / 16; ++ks)
-        sm100::mma_ss(tmem, ldesc + (uint64_t)(ks * 2048 >> 4), vdesc + (uint64_t)(ks * 2048 >> 4), IDESC, true);
-      sm100::mma_commit(&done[st]);
-    }
-  }
-  // the last chunk's MMAs (and so all before them) have completed
-  if (nch > 0 && !*verr) {
-    const int cl = nch - 1;
-    if (!sm100::mbar_wait(&done[cl % kSegStages], (cl / kSegStages) & 1)) atomicOr(&err, 1);
-  }
-  __syncthreads();
-  sm100::tc_fence_after();
-  // M = 64 accumulator: row j lives in lane 32*(j/16) + j%16
-  const int j = 16 * warp + lane;
-  const bool row_ok = lane < 16 && j < p.J && !*verr;
-  const uint32_t taddr = tmem + ((uint32_t)(warp * 32) << 16);
-  float* dst = p.ws_state + (((int64_t)bh * nseg + sg) * p.J + j) * D;
-#pragma unroll
-  for (int half = 0; half < D / 32; ++half) {
-    uint32_t r[32];
-    sm100::tmem_ld32(taddr + half * 32, r);
-    sm100::tc_wait_ld();
-    if (row_ok) {
-#pragma unroll
-      for (int i = 0; i < 32; i += 4)
-        *reinterpret_cast<float4*>(dst + half * 32 + i) =
-            make_float4(__uint_as_float(r[i]), __uint_as_float(r[i + 1]), __uint_as_float(r[i + 2]), __uint_as_float(r[i + 3]));
-    }
-  }
-  if (tid == 0) {
-    float tot = 0.f;
-    for (int c = 0; c < nch; ++c) tot += sm_gc[c];
-    p.ws_decay[(int64_t)bh * nseg + sg] = tot;
-  }
-  sm100::tc_fence_before();
-  __syncthreads();
-  if (err && tid == 0) atomicOr(&g_gla_tc_status, 1);
-  if (warp == 0) sm100::tmem_dealloc(tmem, 64);
-}
-
-// start state of every segment (in place over its end state) and the final state
-__global__ void __launch_bounds__(256) gla_seg_scan_kernel(const GlaParams p, const int nseg) {
-  const int e = blockIdx.x * 256 + threadIdx.x;
-  const int h = blockIdx.y, b = blockIdx.z;
-  if (e >= p.J * p.D) return;
-  const int j = e / p.D, d = e % p.D;
-  const int64_t bh = (int64_t)b * p.H + h;
-  float S = p.state_init ? p.state_init[b * p.ssi[0] + h * p.ssi[1] + j * p.ssi[2] + d] : 0.f;
-  float* ws = p.ws_state + bh * nseg * p.J * p.D + e;
-  const float* gs = p.ws_decay + bh * nseg;
-  const int64_t cs = (int64_t)p.J * p.D;
-  for (int s = 0; s < nseg; ++s) {
-    const float dS = ws[s * cs];
-    ws[s * cs] = S;
-    S = fmaf(__expf(gs[s]), S, dS);
-  }
-  if (p.state_out) p.state_out[b * p.sso[0] + h * p.sso[1] + j * p.sso[2] + d * p.sso[3]] = S;
-}
-
-template <typename T>
-__global__ void __launch_bounds__(kThreads, 2)
-gla_seg_out_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                   const __grid_constant__ CUtensorMap tv, const GlaParams p, const int cps, const int nseg) {
-  constexpr int D = 64;
-  constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
-  constexpr uint32_t IDESC_A = sm100::idesc_f16(BF16, false, false, 128, 128);
-  constexpr uint32_t IDESC_Y = sm100::idesc_f16(BF16, false, true, 128, D);
-  constexpr uint32_t IDESC_S = sm100::idesc_f16(BF16, true, true, 64, D);
-  extern __shared__ unsigned char smem_raw[];
-  unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  unsigned char* sQ = base;                                // one Q tile
-  unsigned char* sK = base + kTile;                        // [stage] K tiles (become Kd hi after A)
-  unsigned char* sV = base + (1 + kSegStages) * kTile;     // [stage] V tiles
-  unsigned char* sL = base + (1 + 2 * kSegStages) * kTile; // Kd lo
-  unsigned char* sS = sL + kTile;                          // running state as a bf16 operand: 64 rows x 128 B
-  __shared__ __align__(8) uint64_t full_q, full_kv[kSegStages], bar_a, bar_b, bar_c;
-  __shared__ float sG[kC], sGS[D], sm_warp[4];
-  __shared__ uint32_t tmem_slot;
-  __shared__ int err;
-
-  const int sg = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int bh = b * p.H + h;
-  const int c0 = sg * cps;
-  const int nch = min(cps, p.nseg - c0);
-  const int J = p.J, KS = (J + 15) / 16;
-  if (tid == 0) {
-    sm100::mbar_init(&full_q, 1);
-    for (int i = 0; i < kSegStages; ++i) sm100::mbar_init(&full_kv[i], 1);
-    sm100::mbar_init(&bar_a, 1); sm100::mbar_init(&bar_b, 1); sm100::mbar_init(&bar_c, 1);
-    err = 0;
-    sm100::fence_mbar_init();
-  }
-  if (warp == 0) { sm100::tmem_alloc(&tmem_slot, 256); sm100::tmem_relinquish(); }
-  sm100::tc_fence_before();
-  __syncthreads();
-  sm100::tc_fence_after();
-  const uint32_t tmem = tmem_slot;
-  const uint32_t tA = tmem, tY = tmem + 64, tS = tmem + 128;   // Y2 then Y1 reuse A's upper half
-  const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-  auto load_q = [&](int c) {
-    sm100::mbar_arrive_expect_tx(&full_q, kTile);
-    sm100::tma_load_4d(sQ, &tq, p.R, (c0 + c) * kC, h, b, &full_q);
-  };
-  auto load_kv = [&](int c) {
-    const int st = c % kSegStages;
-    sm100::mbar_arrive_expect_tx(&full_kv[st], 2 * kTile);
-    sm100::tma_load_4d(sK + st * kTile, &tk, p.R, (c0 + c) * kC, h, b, &full_kv[st]);
-    sm100::tma_load_4d(sV + st * kTile, &tv, 0, (c0 + c) * kC, h, b, &full_kv[st]);
-  };
-  if (tid == 0 && nch > 0) {
-    load_q(0);
-    for (int c = 0; c < min(kSegStages, nch); ++c) load_kv(c);
-  }
-  if (tid < D) sGS[tid] = p.fuse ? ld_any(p.gla_scale, p.dt_gs, h * p.sgs[0] + tid * p.sgs[1]) : 1.f;
-  // the segment's start state -> TMEM (fp32, M = 64 layout) and sS (bf16 operand)
-  const int jrow = 16 * warp + lane;          // the state row this thread's lane holds (lanes < 16)
-  auto state_to_operand = [&](const uint32_t (&r)[32], int half) {
-    // row jrow, channels [32 half, 32 half + 32) -> sS (128-byte swizzled rows)
-    if (lane < 16) {
-      uint4* srow = reinterpret_cast<uint4*>(sS + jrow * 128);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        uint4 u;
-        u.x = pack2(__uint_as_float(r[8 * q]), __uint_as_float(r[8 * q + 1]), BF16);
-        u.y = pack2(__uint_as_float(r[8 * q + 2]), __uint_as_float(r[8 * q + 3]), BF16);
-        u.z = pack2(__uint_as_float(r[8 * q + 4]), __uint_as_float(r[8 * q + 5]), BF16);
-        u.w = pack2(__uint_as_float(r[8 * q + 6]), __uint_as_float(r[8 * q + 7]), BF16);
-        const int chunk16 = half * 4 + q;
-        srow[chunk16 ^ (jrow & 7)] = u;
-      }
-    }
-  };
-  {
-    const float* src = p.ws_state + (((int64_t)bh * nseg + sg) * J + jrow) * D;
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      uint32_t r[32];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) r[i] = __float_as_uint((lane < 16 && jrow < J) ? src[half * 32 + i] : 0.f);
-      sm100::tmem_st32(tS + lane_off + half * 32, r);
-      state_to_operand(r, half);
-    }
-    sm100::tc_wait_st();
-  }
-  volatile int* verr = &err;
-  const uint64_t qdesc = sm100::smem_desc(sQ, 16, 1024, sm100::kSwizzle128);
-  const uint64_t sdesc = sm100::smem_desc(sS, 16, 1024, sm100::kSwizzle128);
-  const uint64_t ldesc = sm100::smem_desc(sL, 16, 1024, sm100::kSwizzle128);
-  auto kstep = [](int ks) { return (uint64_t)(((ks >> 2) * kTile + (ks & 3) * 32) >> 4); };
-  for (int c = 0; c < nch; ++c) {
-    const int st = c % kSegStages;
-    const uint32_t ph = c & 1;
-    const uint64_t kdesc = sm100::smem_desc(sK + st * kTile, 16, 1024, sm100::kSwizzle128);
-    const uint64_t vdesc = sm100::smem_desc(sV + st * kTile, 16, 1024, sm100::kSwizzle128);
-    const int t = (c0 + c) * kC + tid;
-    const float g = t < p.T ? ld_any(p.log_gamma, p.dt_lg, b * p.slg[0] + h * p.slg[1] + (int64_t)t * p.slg[2]) : 0.f;
-    float mix = 0.f;
-    if (p.fuse && t < p.T) mix = ld_any(p.mix_g, p.dt_mg, b * p.smg[0] + h * p.smg[1] + (int64_t)t * p.smg[2]);
-    // 1. A = Q_I K_I^T (the operand sS already holds this chunk's start state)
-    fence_async_smem();
-    if (!*verr && !sm100::mbar_wait(&full_q, ph)) atomicOr(&err, 1);
-    if (!*verr && !sm100::mbar_wait(&full_kv[st], (c / kSegStages) & 1)) atomicOr(&err, 1);
-    sm100::tc_fence_before();
-    __syncthreads();
-    if (tid == 0 && !*verr) {
-      sm100::tc_fence_after();
-      for (int ks = 0; ks < KS; ++ks) sm100::mma_ss(tA, qdesc + kstep(ks), kdesc + kstep(ks), IDESC_A, ks > 0);
-      sm100::mma_commit(&bar_a);
-    }
-    // decay scan (log2 units) while A runs
-    const float Gl = block_scan128(g, sm_warp, tid) * kLog2e;
-    sG[tid] = Gl;
-    __shared__ float sm_gc_last;
-    if (tid == kThreads - 1) sm_gc_last = Gl;
-    if (!*verr && !sm100::mbar_wait(&bar_a, ph)) atomicOr(&err, 1);
-    sm100::tc_fence_after();
-    __syncthreads();
-    const float GC = sm_gc_last;                 // the chunk's total log2 decay
-    // 2. P = A * 2^(G_i - G_j) for j <= i, bf16 pairs over columns [0, 64)
-    const int i = tid;
-#pragma unroll
-    for (int cc = 0; cc < kC; cc += 64) {
-      uint32_t r0[32], r1[32], pk[32];
-      sm100::tmem_ld32(tA + lane_off + cc, r0);
-      sm100::tmem_ld32(tA + lane_off + cc + 32, r1);
-      sm100::tc_wait_ld();
-#pragma unroll
-      for (int u = 0; u < 16; ++u) {
-        const int j0 = cc + 2 * u, j1 = cc + 32 + 2 * u;
-        const float a0 = j0 <= i ? __uint_as_float(r0[2 * u]) * sm100::ex2_approx(Gl - sG[j0]) : 0.f;
-        const float a1 = j0 + 1 <= i ? __uint_as_float(r0[2 * u + 1]) * sm100::ex2_approx(Gl - sG[j0 + 1]) : 0.f;
-        const float a2 = j1 <= i ? __uint_as_float(r1[2 * u]) * sm100::ex2_approx(Gl - sG[j1]) : 0.f;
-        const float a3 = j1 + 1 <= i ? __uint_as_float(r1[2 * u + 1]) * sm100::ex2_approx(Gl - sG[j1 + 1]) : 0.f;
-        pk[u] = pack2(a0, a1, BF16);
-        pk[16 + u] = pack2(a2, a3, BF16);
-      }
-      sm100::tmem_st32(tA + lane_off + cc / 2, pk);
-    }
-    sm100::tc_wait_st();
-    sm100::tc_fence_before();
-    __syncthreads();
-    // 3. Y2 = Q_I S_start into A's upper half
-    if (tid == 0 && !*verr) {
-      sm100::tc_fence_after();
-      for (int ks = 0; ks < KS; ++ks) sm100::mma_ss(tY, qdesc + kstep(ks), sdesc + (uint64_t)(ks * 2048 >> 4), IDESC_Y, ks > 0);
-      sm100::mma_commit(&bar_b);
-    }
-    // 4. while Y2 runs: Kd = K * 2^(GC - G_t) as hi (in place: A has read K) + lo,
-    //    and S <- 2^GC * S in TMEM (Y2 reads the bf16 copy, not TMEM)
-    {
-      const float w = sm100::ex2_approx(GC - Gl);
-      uint4* row = reinterpret_cast<uint4*>(sK + st * kTile + tid * 128);
-      uint4* lrow = reinterpret_cast<uint4*>(sL + tid * 128);
-#pragma unroll
-      for (int q = 0; q < 8; ++q) {
-        uint4 u = row[q], l;
-        uint32_t* pu = reinterpret_cast<uint32_t*>(&u);
-        uint32_t* pl = reinterpret_cast<uint32_t*>(&l);
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          float a, bb, ha, hb;
-          if (BF16) bf16x2_to_f(pu[e], a, bb); else f16x2_to_f(pu[e], a, bb);
-          const float xa = a * w, xb = bb * w;
-          pu[e] = pack2(xa, xb, BF16);
-          if (BF16) bf16x2_to_f(pu[e], ha, hb); else f16x2_to_f(pu[e], ha, hb);
-          pl[e] = pack2(xa - ha, xb - hb, BF16);
-        }
-        row[q] = u;
-        lrow[q] = l;
-      }
-      const float dc = sm100::ex2_approx(GC);
-#pragma unroll
-      for (int half = 0; half < 2; ++half) {
-        uint32_t r[32];
-        sm100::tmem_ld32(tS + lane_off + half * 32, r);
-        sm100::tc_wait_ld();
-#pragma unroll
-        for (int u = 0; u < 32; ++u) r[u] = __float_as_uint(__uint_as_float(r[u]) * dc);
-        sm100::tmem_st32(tS + lane_off + half * 32, r);
-      }
-      sm100::tc_wait_st();
-    }
-    fence_async_smem();
-    if (!*verr && !sm100::mbar_wait(&bar_b, ph)) atomicOr(&err, 1);
-    sm100::tc_fence_after();
-    float y2r[D];
-#pragma unroll
-    for (int cc = 0; cc < D; cc += 32) {
-      uint32_t a[32];
-      sm100::tmem_ld32(tY + lane_off + cc, a);
-      sm100::tc_wait_ld();
-#pragma unroll
-      for (int u = 0; u < 32; ++u) y2r[cc + u] = __uint_as_float(a[u]);
-    }
-    sm100::tc_fence_before();
-    __syncthreads();
-    // 5. Y1 = P V into A's upper half; S += Kd_hi^T V + Kd_lo^T V.  Q is free:
-    //    the next chunk's Q tile starts loading.
-    if (tid == 0 && !*verr) {
-      sm100::tc_fence_after();
-      if (c + 1 < nch) load_q(c + 1);
-#pragma unroll
-      for (int kk = 0; kk < kC / 16; ++kk)
-        sm100::mma_ts(tY, tA + kk * 8, vdesc + (uint64_t)(kk * 2048 >> 4), IDESC_Y, kk > 0);
-#pragma unroll
-      for (int ks = 0; ks < kC / 16; ++ks)
-        sm100::mma_ss(tS, kdesc + (uint64_t)(ks * 2048 >> 4), vdesc + (uint64_t)(ks * 2048 >> 4), IDESC_S, true);
-#pragma unroll
-      for (int ks = 0; ks < kC / 16; ++ks)
-        sm100::mma_ss(tS, ldesc + (uint64_t)(ks * 2048 >> 4), vdesc + (uint64_t)(ks * 2048 >> 4), IDESC_S, true);
-      sm100::mma_commit(&bar_c);
-    }
-    if (!*verr && !sm100::mbar_wait(&bar_c, ph)) atomicOr(&err, 1);
-    sm100::tc_fence_after();
-    // the K/V stage is free: the chunk two ahead starts loading
-    if (tid == 0 && !*verr && c + kSegStages < nch) load_kv(c + kSegStages);
-    // 6. the next chunk's start state as the bf16 operand
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      uint32_t r[32];
-      sm100::tmem_ld32(tS + lane_off + half * 32, r);
-      sm100::tc_wait_ld();
-      state_to_operand(r, half);
-    }
-    // 7. epilogue: y = Y1 + 2^G_i Y2, (1 - mix) * gla_scale * RMSNorm(y)
-    const float eg = sm100::ex2_approx(Gl);
-    float scale = 1.f;
-    if (p.fuse) {
-      float ss = 0.f;
-#pragma unroll
-      for (int cc = 0; cc < D; cc += 32) {
-        uint32_t a[32];
-        sm100::tmem_ld32(tY + lane_off + cc, a);
-        sm100::tc_wait_ld();
-#pragma unroll
-        for (int u = 0; u < 32; ++u) {
-          const float y = fmaf(eg, y2r[cc + u], __uint_as_float(a[u]));
-          ss = fmaf(y, y, ss);
-        }
-      }
-      scale = rsqrtf(ss / (float)D + p.eps) * (1.f - mix);
-    }
-    const bool store = t < p.T && !*verr;
-    T* yp = reinterpret_cast<T*>(p.y) + b * p.sy[0] + h * p.sy[1] + (int64_t)(store ? t : 0) * p.sy[2];
-    const bool vec = p.sy[3] == 1 && (reinterpret_cast<uintptr_t>(yp) & 15u) == 0;
-#pragma unroll
-    for (int cc = 0; cc < D; cc += 32) {
-      uint32_t a[32];
-      sm100::tmem_ld32(tY + lane_off + cc, a);
-      sm100::tc_wait_ld();
-      if (store) {
-        float y[32];
-#pragma unroll
-        for (int u = 0; u < 32; ++u) y[u] = fmaf(eg, y2r[cc + u], __uint_as_float(a[u])) * scale * sGS[cc + u];
-        if (vec) {
-#pragma unroll
-          for (int d = 0; d < 32; d += 8) {
-            uint4 wq;
-            wq.x = pack2(y[d], y[d + 1], BF16);
-            wq.y = pack2(y[d + 2], y[d + 3], BF16);
-            wq.z = pack2(y[d + 4], y[d + 5], BF16);
-            wq.w = pack2(y[d + 6], y[d + 7], BF16);
-            *reinterpret_cast<uint4*>(yp + cc + d) = wq;
-          }
-        } else {
-#pragma unroll
-          for (int d = 0; d < 32; ++d) yp[(int64_t)(cc + d) * p.sy[3]] = from_f<T>(y[d]);
-        }
-      }
-    }
-    sm100::tc_fence_before();
-    __syncthreads();
-  }
-  if (err && tid == 0) atomicOr(&g_gla_tc_status, 1);
-  if (warp == 0) sm100::tmem_dealloc(tmem, 256);
-}
-
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static bool tried = false;
@@ -1025,48 +534,6 @@ bool make_map(CUtensorMap* m, const void* ptr, bool bf16, int64_t D, int64_t T, 
             CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-// HOFA_GLA_CHUNKWISE (read once at library load): head dim 64 runs the
-// chunk-wise kernels instead of the segment-parallel ones (for comparisons).
-const bool kGlaChunkwise = [] {
-  const char* v = getenv("HOFA_GLA_CHUNKWISE");
-  return v != nullptr && v[0] != '\0' && v[0] != '0';
-}();
-
-int sm_count_gla() {
-  static int cached[64] = {};
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 148;
-  if (cached[dev] == 0) {
-    int n = 0;
-    if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
-    cached[dev] = n;
-  }
-  return cached[dev];
-}
-
-template <typename T>
-cudaError_t launch_seg(const GlaParams& p, const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv,
-                       cudaStream_t st) {
-  const SegGeo g = seg_geometry(p.B, p.H, p.T, sm_count_gla());
-  const size_t smem1 = 1024 + 3 * kSegStages * (size_t)kTile;
-  const size_t smem3 = 1024 + (2 + 2 * kSegStages) * (size_t)kTile + 64 * 128;
-  auto k1 = gla_seg_state_kernel<T>;
-  auto k3 = gla_seg_out_kernel<T>;
-  cudaError_t e = cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1);
-  if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(k3, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem3);
-  if (e != cudaSuccess) return e;
-  GlaParams q = p;
-  q.nseg = g.nc;   // chunk count of a head, read by the kernels
-  const dim3 grid(g.nseg, p.H, p.B);
-  k1<<<grid, kThreads, smem1, st>>>(mk, mv, q, g.cps, g.nseg);
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  gla_seg_scan_kernel<<<dim3((p.J * 64 + 255) / 256, p.H, p.B), 256, 0, st>>>(q, g.nseg);
-  if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  k3<<<grid, kThreads, smem3, st>>>(mq, mk, mv, q, g.cps, g.nseg);
-  return cudaGetLastError();
-}
-
 template <typename T, int D>
 cudaError_t launch_t(const GlaParams& p, cudaStream_t st, bool* taken) {
   using Gm = Geo<D>;
@@ -1075,12 +542,6 @@ cudaError_t launch_t(const GlaParams& p, cudaStream_t st, bool* taken) {
   if (!make_map(&mq, p.q, bf16, D, p.T, p.H, p.B, p.sq) || !make_map(&mk, p.k, bf16, D, p.T, p.H, p.B, p.sk) ||
       !make_map(&mv, p.v, bf16, D, p.T, p.H, p.B, p.sv))
     return cudaSuccess;
-  if constexpr (D == 64) {
-    if (!kGlaChunkwise) {
-      *taken = true;
-      return launch_seg<T>(p, mq, mk, mv, st);
-    }
-  }
   auto kA = gla_tc_state_kernel<T, D>;
   auto kC_ = gla_tc_out_kernel<T, D>;
   cudaError_t e = cudaFuncSetAttribute(kA, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Gm::STATE_SMEM);

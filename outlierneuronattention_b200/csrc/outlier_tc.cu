@@ -66,10 +66,6 @@ const int kEmuSetting = [] {
   const char* v = getenv("HOFA_OUTLIER_EMU");
   return v != nullptr && v[0] != '\0' ? atoi(v) : kEmuDefault;
 }();
-const int kF16ExpSetting = [] {
-  const char* v = getenv("HOFA_OUTLIER_F16EXP");
-  return v != nullptr && v[0] != '\0' ? atoi(v) : 0;
-}();
 
 // TMEM columns: the S/P buffer in [0, kKeys), O in [kKeys, kKeys + D), rounded up to a power of two
 template <int D>
@@ -133,27 +129,11 @@ __device__ __forceinline__ void exp2_pair_poly(uint64_t x2, float& e0, float& e1
   e1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
 }
 
-// 2^x for two lanes with one MUFU operation: the arguments rounded to f16,
-// ex2.approx.f16x2, the results widened to fp32.  The result keeps the 11
-// significant bits of f16 and the argument's f16 rounding adds a relative
-// error of at most 2^-11 * |x| * ln 2 (0.5 % at |x| = 15); P enters the P V
-// product as a 16-bit value anyway.  Exponents above 15.99 overflow to inf,
-// below -24 flush to zero: callers keep x below kRaise = 14.
-__device__ __forceinline__ void exp2_pair_f16(uint64_t x2, float& e0, float& e1) {
-  float x0, x1;
-  sm100::f2_unpack(x2, x0, x1);
-  __half2 h = __floats2half2_rn(x0, x1);
-  uint32_t xh = *reinterpret_cast<uint32_t*>(&h), eh;
-  asm("ex2.approx.f16x2 %0, %1;" : "=r"(eh) : "r"(xh));
-  f16x2_to_f(eh, e0, e1);
-}
-
 // Row of 32 scores -> 32 probabilities packed as 16-bit pairs in pk[16]
 // (pair i = columns 2i, 2i+1); returns the row sum in fp32.  E of the 16
-// pairs, spread evenly (pair i when i*E mod 16 < E), use the polynomial;
-// of the others, pair i uses the two-lane f16 MUFU operation when
-// i*H mod 16 < H, the rest one fp32 MUFU operation per lane.
-template <bool BF16, int E, int H = 0>
+// pairs, spread evenly (pair i when i*E mod 16 < E), use the polynomial, the
+// rest the MUFU unit.
+template <bool BF16, int E>
 __device__ __forceinline__ float row_exp(const uint32_t (&r)[32], float scale, float m, uint32_t (&pk)[16]) {
   const uint64_t sc2 = sm100::f2_pack(scale, scale);
   const uint64_t nm2 = sm100::f2_pack(-m, -m);
@@ -167,8 +147,6 @@ __device__ __forceinline__ float row_exp(const uint32_t (&r)[32], float scale, f
     float e0, e1;
     if ((i * E) % 16 < E) {
       exp2_pair_poly(x, e0, e1);
-    } else if ((i * H) % 16 < H) {
-      exp2_pair_f16(x, e0, e1);
     } else {
       float x0, x1;
       sm100::f2_unpack(x, x0, x1);
@@ -184,7 +162,7 @@ __device__ __forceinline__ float row_exp(const uint32_t (&r)[32], float scale, f
   return a + b;
 }
 
-template <typename T, int D, int R, int EMU, int H16 = 0>
+template <typename T, int D, int R, int EMU>
 __global__ void __launch_bounds__(kThreads, D == 64 ? 4 : 2)
 outlier_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                   const __grid_constant__ CUtensorMap tv, const OutlierParams p) {
@@ -199,8 +177,7 @@ outlier_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
   // P and the fp32 row sums and O share fp32's exponent range, so 2^64 (and
   // a row sum below 2^64 times the key count) is far from overflow; f16 P
   // (largest value 65504) keeps a margin at 2^8
-  // (14 when some exponentials run in f16, whose largest value is 65504)
-  constexpr float kRaise = H16 > 0 ? 14.f : (BF16 ? 64.f : 8.f);
+  constexpr float kRaise = BF16 ? 64.f : 8.f;
 
   extern __shared__ unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -348,7 +325,7 @@ outlier_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
           // exponentials against the running max straight away; a row whose max
           // grew by more than 2^kRaise shows in its sum (>= 2^kRaise, inf or
           // NaN), and only then does the warp redo the half with the row max
-          ls = row_exp<BF16, (EMU > 16 ? 0 : EMU), H16>(r, scale, m_used, pk);
+          ls = row_exp<BF16, (EMU > 16 ? 0 : EMU)>(r, scale, m_used, pk);
           slow = __any_sync(0xffffffffu, !(ls < 1.8446744e19f));  // 2^64
         }
         if (slow) {
@@ -399,7 +376,7 @@ outlier_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
             }
           }
           ls = masked ? row_exp<BF16, 0>(r, scale, m_used, pk)   // exact zeros where masked
-                      : row_exp<BF16, (EMU > 16 ? 0 : EMU), H16>(r, scale, m_used, pk);
+                      : row_exp<BF16, (EMU > 16 ? 0 : EMU)>(r, scale, m_used, pk);
         }
         l_sum = l_sum * factor + ls;
         // P of this half as 16-bit pairs over columns [16 hf, 16 hf + 16), which
@@ -521,10 +498,10 @@ size_t residency_smem(size_t need, uint32_t tmem_cols_per_cta) {
   return cap > (long)need ? (size_t)((cap + 127) & ~127L) : need;
 }
 
-template <typename T, int D, int R, int EMU, int H16 = 0>
+template <typename T, int D, int R, int EMU>
 cudaError_t launch_kernel(const CUtensorMap& mq, const CUtensorMap& mk, const CUtensorMap& mv, const OutlierParams& p,
                           dim3 grid, cudaStream_t st, bool* taken) {
-  auto k = outlier_tc_kernel<T, D, R, EMU, H16>;
+  auto k = outlier_tc_kernel<T, D, R, EMU>;
   const size_t smem = residency_smem(Smem<D, R>::BYTES, tmem_cols<D>());
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
@@ -552,16 +529,6 @@ cudaError_t launch_dr(const OutlierParams& p, cudaStream_t st, bool* taken) {
   // the 16 exp2 pairs of a full half-tile run as the FMA-pipe polynomial
   // (bf16, head dim 64, r = 16)
   if constexpr (std::is_same<T, __nv_bfloat16>::value && D == 64 && R == 16) {
-    // HOFA_OUTLIER_F16EXP (read once at library load): of the 16 exp2 pairs,
-    // this many (4, 8, 12 or 16; less the polynomial ones) run as two-lane f16
-    // MUFU operations
-    switch (kF16ExpSetting) {
-      case 4: return launch_kernel<T, D, R, kEmuDefault, 4>(mq, mk, mv, p, grid, st, taken);
-      case 8: return launch_kernel<T, D, R, kEmuDefault, 8>(mq, mk, mv, p, grid, st, taken);
-      case 12: return launch_kernel<T, D, R, kEmuDefault, 12>(mq, mk, mv, p, grid, st, taken);
-      case 16: return launch_kernel<T, D, R, kEmuDefault, 16>(mq, mk, mv, p, grid, st, taken);
-      default: break;
-    }
     const int e = kEmuSetting;
     if (e == 0) return launch_kernel<T, D, R, 0>(mq, mk, mv, p, grid, st, taken);
     if (e == 1) return launch_kernel<T, D, R, 1>(mq, mk, mv, p, grid, st, taken);
