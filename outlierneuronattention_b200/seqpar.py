@@ -13,10 +13,11 @@ attention work.  One exchange step per layer, one process per GPU over
   needs is sent to it point-to-point (NCCL ``isend``/``irecv`` in one batch)
   straight into the receiver's buffer at the block's sequence position: block
   r goes to every other rank, block 2N-1-r to the ranks below r.  The
-  transfers run on NCCL's stream while the GLA passes run; the attention of
-  each local block then reads the key prefix ending at its last token
+  transfers run on NCCL's stream while the first GLA pass runs; then the
+  attention of each local block reads the key prefix ending at its last token
   (``q_offset`` = the block's first absolute position), the two blocks on two
-  streams so that their CTAs share the GPU;
+  side streams, while the block-state exchange and the second GLA pass run on
+  the caller's stream underneath them;
 * GLA: both local blocks run from a zero state in one call (the blocks are a
   batch of two), giving their end states S_b and total log decays G_b.  These
   are all-gathered, and every rank forms the start state of each of its blocks
@@ -28,7 +29,8 @@ attention work.  One exchange step per layer, one process per GPU over
   start states with the fused ``(1-mix) * gla_scale * RMSNorm`` epilogue
   (RMSNorm is not linear, so the normalised output has to wait for the start
   state);
-* the attention output is then added into the GLA output (as in the layer).
+* the attention output (mix * attention, in a buffer of its own) is then
+  added into the GLA output (as in the layer, two roundings).
 
 ``relayout_seq_to_head`` turns the sequence-sharded result into the caches of
 a head-sharded decode: rank g ends up with the outlier key and value caches
@@ -114,15 +116,18 @@ class PhaseTimer:
         return out
 
 
-_SIDE_STREAMS: Dict[int, torch.cuda.Stream] = {}
+_SIDE_STREAMS: Dict[int, Tuple[torch.cuda.Stream, torch.cuda.Stream]] = {}
 
 
-def _side_stream(dev: torch.device) -> torch.cuda.Stream:
-    """One extra stream per device for the concurrent attention launch."""
+def _side_streams(dev: torch.device):
+    """Two extra streams per device for the attention launches of the two
+    local blocks (concurrent with each other and with the GLA on the current
+    stream)."""
     idx = dev.index if dev.index is not None else torch.cuda.current_device()
     st = _SIDE_STREAMS.get(idx)
     if st is None:
-        st = _SIDE_STREAMS[idx] = torch.cuda.Stream(torch.device("cuda", idx))
+        d = torch.device("cuda", idx)
+        st = _SIDE_STREAMS[idx] = (torch.cuda.Stream(d), torch.cuda.Stream(d))
     return st
 
 
@@ -224,26 +229,52 @@ def sharded_attention_core(Q, K, V, log_gamma, mix, r: int, sm_scale: float, gla
     G_loc = log_gamma.float().unflatten(2, (2, bl)).sum(-1).movedim(2, 0).reshape(2 * B, H)   # [2B, H]
     if log_alpha is not None:
         G_loc = G_loc[..., None] * torch.exp(log_alpha.float().reshape(1, H, J))             # [2B, H, J]
-    mark("gla_pass1")
-
-    # 3. block states of every rank, start states of the local blocks (and the end state)
+    # 3. start the block-state exchange (NCCL orders it after the key/value transfers)
     if world > 1:
         S_all = torch.empty(world * S_loc.shape[0], *S_loc.shape[1:], dtype=S_loc.dtype, device=dev)
         G_all = torch.empty(world * G_loc.shape[0], *G_loc.shape[1:], dtype=G_loc.dtype, device=dev)
-        dist.all_gather_into_tensor(S_all, S_loc.contiguous(), group=group)
-        dist.all_gather_into_tensor(G_all, G_loc.contiguous(), group=group)
-        S_all, G_all = S_all.view(world, *S_loc.shape), G_all.view(world, *G_loc.shape)
+        state_works = [dist.all_gather_into_tensor(S_all, S_loc.contiguous(), group=group, async_op=True),
+                       dist.all_gather_into_tensor(G_all, G_loc.contiguous(), group=group, async_op=True)]
     else:
-        S_all, G_all = S_loc[None], G_loc[None]
+        S_all, G_all, state_works = S_loc, G_loc, []
+    mark("gla_pass1")
+
+    # 4. outlier attention of each local block against its key prefix, as soon
+    #    as the key blocks have landed: on side streams, into a buffer of its
+    #    own (out = mix * attention), so that the state exchange, the block
+    #    prefix and the second GLA pass run on this stream underneath it
+    for w in works:
+        w.wait()
+    mark("exchange_wait")
+    Kv = KB.permute(1, 2, 0, 3)                     # [B, H, T, r] view
+    Vv = VB.permute(1, 2, 0, 3)
+    Ya = torch.empty(B, H, Tl, D, dtype=dt, device=dev)
+    calls = [(Q[:, :, sl], e, a, sl) for (a, e), sl in zip(blocks, local)]
+    sides = _side_streams(dev) if Q.is_cuda else None
+    if sides is not None:
+        cur = torch.cuda.current_stream(dev)
+        for st, (q_, e, a, sl) in zip(sides, calls):
+            st.wait_stream(cur)
+            with torch.cuda.stream(st):
+                attn(q_, Kv[:, :, :e], Vv[:, :, :e], r, sm_scale, mix[:, :, sl], out=Ya[:, :, sl], q_offset=a,
+                     accumulate=False)
+    else:
+        for q_, e, a, sl in calls:
+            attn(q_, Kv[:, :, :e], Vv[:, :, :e], r, sm_scale, mix[:, :, sl], out=Ya[:, :, sl], q_offset=a,
+                 accumulate=False)
+
+    # 5. start states of the local blocks (and the end state) from every rank's block states
+    for w in state_works:
+        w.wait()
+    S_all, G_all = S_all.view(world, *S_loc.shape), G_all.view(world, *G_loc.shape)
     order = [block_owner(i, world) for i in range(nb)]
     S_blocks = torch.stack([S_all[o][li * B:(li + 1) * B] for o, li in order])    # [nb, B, H, J, D]
     G_blocks = torch.stack([G_all[o][li * B:(li + 1) * B] for o, li in order])    # [nb, B, H(, J)]
     with torch.autocast(dev.type, enabled=False):                                # float32 state arithmetic
         starts = _block_prefix_states(S_blocks, G_blocks, [blocks[0][0] // bl, blocks[1][0] // bl, nb])
     S_end = starts[2]
-    mark("state_exchange")
 
-    # 4. GLA again from each local block's start state, fused epilogue
+    # 6. GLA again from each local block's start state, fused epilogue
     Y = torch.empty(B, H, Tl, D, dtype=dt, device=dev)
     Yb = _as_block_batch(Y, bl)
     if batched and Yb is not None:
@@ -254,28 +285,15 @@ def sharded_attention_core(Q, K, V, log_gamma, mix, r: int, sm_scale: float, gla
             gla(Q[:, :, sl], K[:, :, sl], V[:, :, sl], log_gamma[:, :, sl], r, log_alpha=log_alpha,
                 mix_g=mix[:, :, sl], gla_scale=gla_scale, y=Y[:, :, sl], initial_state=starts[i].contiguous(),
                 eps=eps)
-    mark("gla_pass2")
+    mark("state_exchange_gla_pass2")
 
-    # 5. outlier attention of each local block against its key prefix
-    for w in works:
-        w.wait()
-    mark("exchange_wait")
-    Kv = KB.permute(1, 2, 0, 3)                     # [B, H, T, r] view
-    Vv = VB.permute(1, 2, 0, 3)
-    calls = [(Q[:, :, sl], e, a, sl) for (a, e), sl in zip(blocks, local)]
-    side = _side_stream(dev) if Q.is_cuda else None
-    if side is not None:
-        side.wait_stream(torch.cuda.current_stream(dev))
-        with torch.cuda.stream(side):
-            q0, e0, a0, sl0 = calls[0]
-            attn(q0, Kv[:, :, :e0], Vv[:, :, :e0], r, sm_scale, mix[:, :, sl0], out=Y[:, :, sl0], q_offset=a0)
-        q1, e1, a1, sl1 = calls[1]
-        attn(q1, Kv[:, :, :e1], Vv[:, :, :e1], r, sm_scale, mix[:, :, sl1], out=Y[:, :, sl1], q_offset=a1)
-        torch.cuda.current_stream(dev).wait_stream(side)
-    else:
-        for q_, e, a, sl in calls:
-            attn(q_, Kv[:, :, :e], Vv[:, :, :e], r, sm_scale, mix[:, :, sl], out=Y[:, :, sl], q_offset=a)
-    mark("attention")
+    # 7. the attention output joins the GLA output (as in the layer)
+    if sides is not None:
+        for st in sides:
+            torch.cuda.current_stream(dev).wait_stream(st)
+    mark("attention_end")
+    Y.add_(Ya)
+    mark("add")
     if return_kv:
         return Y, S_end, (KB, VB)
     return Y, S_end

@@ -38,8 +38,8 @@ def oracle_gla(Q, K, V, log_gamma, r, *, log_alpha=None, mix_g=None, gla_scale=N
     return y
 
 
-def oracle_attn(q, k, v, r, sm_scale, mix_g, out=None, q_offset=0):
-    res = outlier_attention_core(q, k, v, r, sm_scale, mix_g, out=out, q_offset=q_offset)
+def oracle_attn(q, k, v, r, sm_scale, mix_g, out=None, q_offset=0, accumulate=True):
+    res = outlier_attention_core(q, k, v, r, sm_scale, mix_g, out=out if accumulate else None, q_offset=q_offset)
     out.copy_(res)
     return out
 
