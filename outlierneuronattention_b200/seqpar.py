@@ -7,12 +7,13 @@ attention work.  One exchange step per layer, one process per GPU over
 ``torch.distributed`` (NCCL on GPUs):
 
 * outlier attention: query block i needs the rotated outlier keys K_O and the
-  values V of blocks 0..i.  Every rank keeps a full-sequence key buffer and
-  value buffer in token-major layout ``[T, B, H, C]``, where any block is one
+  values V of blocks 0..i.  Every rank keeps one full-sequence key|value
+  buffer in token-major layout ``[T, B, H, r + D]``, where any block is one
   contiguous range.  Its own blocks are copied in; every block another rank
-  needs is sent to it point-to-point (NCCL ``isend``/``irecv`` in one batch)
-  straight into the receiver's buffer at the block's sequence position: block
-  r goes to every other rank, block 2N-1-r to the ranks below r.  The
+  needs lands straight in the receiver's buffer at the block's sequence
+  position: block r goes to every other rank (one in-place all-gather of the
+  first-half blocks), block 2N-1-r to the ranks below r (NCCL ``isend`` /
+  ``irecv`` in one batch).  The
   transfers run on NCCL's stream while the first GLA pass runs; then the
   attention of each local block reads the key prefix ending at its last token
   (``q_offset`` = the block's first absolute position), the two blocks on two
@@ -176,7 +177,7 @@ def sharded_attention_core(Q, K, V, log_gamma, mix, r: int, sm_scale: float, gla
     the GLA state after all T tokens, identical on every rank); with
     ``return_kv`` also the full-sequence key/value buffers (token-major
     [T,B,H,r] and [T,B,H,D]; rows of blocks this rank did not need are
-    unspecified).
+    unspecified; views of one [T,B,H,r+D] buffer).
     """
     world, rank = _group_info(group)
     B, H, Tl, D = Q.shape
@@ -191,30 +192,61 @@ def sharded_attention_core(Q, K, V, log_gamma, mix, r: int, sm_scale: float, gla
     mark = timer.mark if timer is not None else (lambda name: None)
     mark("start")
 
-    # 1. full-sequence key/value buffers (token-major: a block is one contiguous
-    #    range); own blocks copied in, the point-to-point exchange started
-    KB = torch.empty(T, B, H, r, dtype=dt, device=dev)
-    VB = torch.empty(T, B, H, D, dtype=dt, device=dev)
+    # 1. one full-sequence key|value buffer (token-major [T, B, H, r + D]: a
+    #    block is one contiguous range), own blocks copied in, the exchange
+    #    started: the first-half blocks (block s belongs to rank s, and every
+    #    rank needs it) with one in-place all-gather into [0, N*bl), the
+    #    second-half blocks point-to-point (block 2N-1-s goes to the ranks
+    #    below s)
+    C = r + D
+    KVB = torch.empty(T, B, H, C, dtype=dt, device=dev)
     for (a, e), sl in zip(blocks, local):
-        KB[a:e].copy_(K[:, :, sl, :r].permute(2, 0, 1, 3))
-        VB[a:e].copy_(V[:, :, sl].permute(2, 0, 1, 3))
-    ops = []
+        KVB[a:e, ..., :r].copy_(K[:, :, sl, :r].permute(2, 0, 1, 3))
+        KVB[a:e, ..., r:].copy_(V[:, :, sl].permute(2, 0, 1, 3))
+    works = []
     if world > 1:
-        for i in range(nb):
+        first = KVB[:world * bl]
+        works.append(dist.all_gather_into_tensor(first, KVB[rank * bl:(rank + 1) * bl], group=group, async_op=True))
+        ops = []
+        for s_ in range(world):
+            i = nb - 1 - s_                      # rank s_'s second block
             a, e = i * bl, (i + 1) * bl
-            owner, _ = block_owner(i, world)
-            dests = block_receivers(i, world)
-            if owner == rank:
-                for s in dests:
-                    peer = _global_rank(group, s)
-                    ops += [dist.P2POp(dist.isend, KB[a:e], peer, group), dist.P2POp(dist.isend, VB[a:e], peer, group)]
-            elif rank in dests:
-                peer = _global_rank(group, owner)
-                ops += [dist.P2POp(dist.irecv, KB[a:e], peer, group), dist.P2POp(dist.irecv, VB[a:e], peer, group)]
-    works = dist.batch_isend_irecv(ops) if ops else []
+            if s_ == rank:
+                ops += [dist.P2POp(dist.isend, KVB[a:e], _global_rank(group, d), group) for d in range(rank)]
+            elif rank < s_:
+                ops.append(dist.P2POp(dist.irecv, KVB[a:e], _global_rank(group, s_), group))
+        if ops:
+            works += dist.batch_isend_irecv(ops)
     mark("pack_and_post")
 
-    # 2. GLA from a zero state for both local blocks (one call, a batch of two blocks)
+    # 2. outlier attention of each local block against its key prefix, on two
+    #    side streams that wait only for the key/value exchange (and, through
+    #    it, the packing copies): it runs beside the GLA passes and the
+    #    block-state exchange on this stream, into a buffer of its own
+    #    (out = mix * attention)
+    Kv = KVB[..., :r].permute(1, 2, 0, 3)           # [B, H, T, r] view
+    Vv = KVB[..., r:].permute(1, 2, 0, 3)           # [B, H, T, D] view
+    Ya = torch.empty(B, H, Tl, D, dtype=dt, device=dev)
+    calls = [(Q[:, :, sl], e, a, sl) for (a, e), sl in zip(blocks, local)]
+    sides = _side_streams(dev) if Q.is_cuda else None
+    if sides is not None:
+        cur = torch.cuda.current_stream(dev)
+        for st, (q_, e, a, sl) in zip(sides, calls):
+            st.wait_stream(cur)
+            with torch.cuda.stream(st):
+                for w in works:
+                    w.wait()
+                attn(q_, Kv[:, :, :e], Vv[:, :, :e], r, sm_scale, mix[:, :, sl], out=Ya[:, :, sl], q_offset=a,
+                     accumulate=False)
+    else:
+        for w in works:
+            w.wait()
+        for q_, e, a, sl in calls:
+            attn(q_, Kv[:, :, :e], Vv[:, :, :e], r, sm_scale, mix[:, :, sl], out=Ya[:, :, sl], q_offset=a,
+                 accumulate=False)
+    mark("attention_issued")
+
+    # 3. GLA from a zero state for both local blocks (one call, a batch of two blocks)
     Qb, Kb, Vb = (_as_block_batch(x, bl) for x in (Q, K, V))
     lgb, mixb = _as_block_batch(log_gamma, bl), _as_block_batch(mix, bl)
     batched = all(x is not None for x in (Qb, Kb, Vb, lgb, mixb))
@@ -229,7 +261,7 @@ def sharded_attention_core(Q, K, V, log_gamma, mix, r: int, sm_scale: float, gla
     G_loc = log_gamma.float().unflatten(2, (2, bl)).sum(-1).movedim(2, 0).reshape(2 * B, H)   # [2B, H]
     if log_alpha is not None:
         G_loc = G_loc[..., None] * torch.exp(log_alpha.float().reshape(1, H, J))             # [2B, H, J]
-    # 3. start the block-state exchange (NCCL orders it after the key/value transfers)
+    #    and the block-state exchange
     if world > 1:
         S_all = torch.empty(world * S_loc.shape[0], *S_loc.shape[1:], dtype=S_loc.dtype, device=dev)
         G_all = torch.empty(world * G_loc.shape[0], *G_loc.shape[1:], dtype=G_loc.dtype, device=dev)
@@ -239,31 +271,7 @@ def sharded_attention_core(Q, K, V, log_gamma, mix, r: int, sm_scale: float, gla
         S_all, G_all, state_works = S_loc, G_loc, []
     mark("gla_pass1")
 
-    # 4. outlier attention of each local block against its key prefix, as soon
-    #    as the key blocks have landed: on side streams, into a buffer of its
-    #    own (out = mix * attention), so that the state exchange, the block
-    #    prefix and the second GLA pass run on this stream underneath it
-    for w in works:
-        w.wait()
-    mark("exchange_wait")
-    Kv = KB.permute(1, 2, 0, 3)                     # [B, H, T, r] view
-    Vv = VB.permute(1, 2, 0, 3)
-    Ya = torch.empty(B, H, Tl, D, dtype=dt, device=dev)
-    calls = [(Q[:, :, sl], e, a, sl) for (a, e), sl in zip(blocks, local)]
-    sides = _side_streams(dev) if Q.is_cuda else None
-    if sides is not None:
-        cur = torch.cuda.current_stream(dev)
-        for st, (q_, e, a, sl) in zip(sides, calls):
-            st.wait_stream(cur)
-            with torch.cuda.stream(st):
-                attn(q_, Kv[:, :, :e], Vv[:, :, :e], r, sm_scale, mix[:, :, sl], out=Ya[:, :, sl], q_offset=a,
-                     accumulate=False)
-    else:
-        for q_, e, a, sl in calls:
-            attn(q_, Kv[:, :, :e], Vv[:, :, :e], r, sm_scale, mix[:, :, sl], out=Ya[:, :, sl], q_offset=a,
-                 accumulate=False)
-
-    # 5. start states of the local blocks (and the end state) from every rank's block states
+    # 4. start states of the local blocks (and the end state) from every rank's block states
     for w in state_works:
         w.wait()
     S_all, G_all = S_all.view(world, *S_loc.shape), G_all.view(world, *G_loc.shape)
@@ -274,7 +282,7 @@ def sharded_attention_core(Q, K, V, log_gamma, mix, r: int, sm_scale: float, gla
         starts = _block_prefix_states(S_blocks, G_blocks, [blocks[0][0] // bl, blocks[1][0] // bl, nb])
     S_end = starts[2]
 
-    # 6. GLA again from each local block's start state, fused epilogue
+    # 5. GLA again from each local block's start state, fused epilogue
     Y = torch.empty(B, H, Tl, D, dtype=dt, device=dev)
     Yb = _as_block_batch(Y, bl)
     if batched and Yb is not None:
@@ -287,7 +295,7 @@ def sharded_attention_core(Q, K, V, log_gamma, mix, r: int, sm_scale: float, gla
                 eps=eps)
     mark("state_exchange_gla_pass2")
 
-    # 7. the attention output joins the GLA output (as in the layer)
+    # 6. the attention output joins the GLA output (as in the layer)
     if sides is not None:
         for st in sides:
             torch.cuda.current_stream(dev).wait_stream(st)
@@ -295,7 +303,7 @@ def sharded_attention_core(Q, K, V, log_gamma, mix, r: int, sm_scale: float, gla
     Y.add_(Ya)
     mark("add")
     if return_kv:
-        return Y, S_end, (KB, VB)
+        return Y, S_end, (KVB[..., :r], KVB[..., r:])
     return Y, S_end
 
 
