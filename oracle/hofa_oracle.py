@@ -248,9 +248,13 @@ class OracleLayer:
     """
 
     def __init__(self, shape: LayerShape, state_dict: dict, dtype=torch.float64,
-                 act_dtype=None, gla_mode: str = "chunk"):
+                 act_dtype=None, gla_mode: str = "chunk", prefill_eps: float = FP32_EPS):
         self.s = shape
         self.dtype = dtype
+        # RMSNorm epsilon of the hybrid prefill: float32 epsilon in the training
+        # layer (Train.py:71); the inference layer's Triton prefill uses 1e-5
+        # (src/chunk_gla_inlier.py:234)
+        self.prefill_eps = prefill_eps
         self.act_dtype = act_dtype
         self.gla_mode = gla_mode
         self.p = {k: v.detach().to(dtype) for k, v in state_dict.items()
@@ -329,7 +333,7 @@ class OracleLayer:
         Y_I, S = chunk_gla_core(Q, K, V, log_gamma, s.r, s.chunk_size,
                                 log_alpha=self._log_alpha(), dtype=self.dtype, mode=self.gla_mode)
         var = (Y_I * Y_I).mean(-1, keepdim=True)
-        Y_I = Y_I * torch.rsqrt(var + FP32_EPS) * self.p['gla_scale'].reshape(1, s.num_heads, 1, s.d_head)
+        Y_I = Y_I * torch.rsqrt(var + self.prefill_eps) * self.p['gla_scale'].reshape(1, s.num_heads, 1, s.d_head)
         m = mix[..., None]
         Y = Y_I + m * (Y_O - Y_I)          # torch.lerp(Y_I, Y_O, mix_g), Train.py:294
         out = self._out(Y)

@@ -17,10 +17,15 @@ kernel in the reference either (``r == d_head``: plain SDPA; width split:
 SDPA heads + GLA heads) follow the reference's PyTorch code, with the GLA
 heads of the width split on the native GLA kernel.
 
-RMSNorm epsilon: float32 machine epsilon for both prefill and decode (the
-reference decode kernel and the reference training layer use it; the
-reference prefill kernel hard-codes 1e-5, a difference below 1e-6 relative
-for non-degenerate inputs).
+RMSNorm epsilon: float32 machine epsilon for prefill and decode by default,
+as in the reference's decode kernel and its training layer
+(src/HybridOutlierFactorizedAttentionTrain.py:71, nn.RMSNorm with eps=None).
+The reference's inference layer hard-codes 1e-5 in its hybrid prefill
+(src/HybridOutlierFactorizedAttention.py:203-206 -> src/chunk_gla_inlier.py:234)
+while its decode uses float32 epsilon; where the GLA outputs are small (early
+tokens, small projections) the two epsilons give visibly different normalised
+outputs.  ``layer.hybrid_prefill_eps = 1e-5`` reproduces the inference
+layer's prefill.
 """
 from __future__ import annotations
 
@@ -77,6 +82,8 @@ class HybridOutlierFactorizedAttention(nn.Module):
 
         self.inlier_norm = nn.RMSNorm(self.d_head, elementwise_affine=False)
         self.gla_scale = nn.Parameter(torch.ones(1, self.num_heads, 1, self.d_head))
+        # RMSNorm epsilon of the hybrid prefill (see the module docstring); not a parameter or buffer
+        self.hybrid_prefill_eps = FP32_EPS
 
     # ------------------------------------------------------------------ helpers
     def _qkv_weight(self):
@@ -165,7 +172,7 @@ class HybridOutlierFactorizedAttention(nn.Module):
                  if return_state else None)
         Y = gla_forward(Q, K, V, log_gamma, self.r,
                         log_alpha=self.log_alpha if self.learnable_alpha else None,
-                        mix_g=mix, gla_scale=self.gla_scale, state_out=state, eps=FP32_EPS)
+                        mix_g=mix, gla_scale=self.gla_scale, state_out=state, eps=self.hybrid_prefill_eps)
         sm_scale = (self.d_head / self.r) ** 0.5
         exact_attention_triton(Q, K, V, self.r, sm_scale, mix, out=Y)
         Y_out = self._out(Y, B, N, dtype_in)

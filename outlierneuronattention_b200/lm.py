@@ -5,8 +5,11 @@ embedding, ``num_layers`` pre-norm blocks of (RMSNorm, the drop-in
 ``HybridOutlierFactorizedAttention``, RMSNorm, SwiGLU MLP), a final RMSNorm
 and a language-model head tied to the embedding.  At the 350M shape (24
 layers, d_model 1024, 16 heads of 64, r = 16, MLP 4096, vocabulary 32000) it
-holds 435.6M parameters.  The projections and the MLP are cuBLAS GEMMs; the
-attention of every layer runs on this library's kernels.
+holds 435.6M parameters.  The attention of every layer runs on this
+library's kernels; in decode steps of up to 8 sequences the projections and
+the MLP run on its small-batch linear kernel (``hofa_lm_linear_fwd``, with the
+RMSNorm, the SwiGLU product and the residual add folded in), otherwise (and in
+the prefill) as cuBLAS GEMMs.
 
 ``DecodeEngine`` replaces the per-token host loop of the reference's
 generation (src/inference.py:174-239, one ``.item()`` per token and the

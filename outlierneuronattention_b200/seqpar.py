@@ -377,7 +377,8 @@ def sharded_layer_forward(layer, x_local: torch.Tensor, T: int, group=None, retu
         mix[:, :, sl] = mix_b
     sm_scale = (layer.d_head / layer.r) ** 0.5
     Y, S_end = sharded_attention_core(Q, K, V, lg, mix, layer.r, sm_scale, layer.gla_scale, T, group=group,
-                                      log_alpha=layer.log_alpha if layer.learnable_alpha else None)
+                                      log_alpha=layer.log_alpha if layer.learnable_alpha else None,
+                                      eps=layer.hybrid_prefill_eps)
     out = layer._out(Y, B, Tl, dtype_in)
     if return_state:
         return out, S_end, (K[..., :layer.r], V)

@@ -130,6 +130,32 @@ def test_bf16_autocast_prefill_matches_reference(name, T0):
     assert err(state[0], g["states"][T0]) <= 2e-2
 
 
+def test_hybrid_prefill_eps_reproduces_the_inference_layer_choice():
+    """The reference's inference layer normalises the hybrid prefill's GLA
+    output with eps 1e-5 (src/chunk_gla_inlier.py:234), its training layer
+    with float32 epsilon.  Small projections make the difference visible; the
+    layer follows the oracle with either choice (float32)."""
+    from outlierneuronattention_b200 import HybridOutlierFactorizedAttention, ModelConfig
+    torch.manual_seed(0)
+    m = HybridOutlierFactorizedAttention(ModelConfig(d_model=256, num_heads=4, num_layers=1, r=16, chunk_size=64))
+    with torch.no_grad():
+        m.gate_proj.weight.normal_(0, 0.02)
+        m.mix_proj.weight.normal_(0, 0.02)
+    sd = {k: v.clone() for k, v in m.state_dict().items()}
+    x = torch.randn(2, 200, 256, generator=torch.Generator().manual_seed(4)) * 0.5
+    m = m.cuda().eval()
+    outs = {}
+    for eps in (None, 1e-5):
+        if eps is not None:
+            m.hybrid_prefill_eps = eps
+        ref = OracleLayer(LayerShape(256, 4, 16, 64), sd, **({} if eps is None else {"prefill_eps": eps}))
+        with torch.no_grad():
+            y = m(x.cuda())
+        outs[eps] = y
+        assert err(y, ref.forward(x.double())) <= 1e-4, eps
+    assert err(outs[None], outs[1e-5]) > 1e-3   # the choice matters at this scale
+
+
 def test_config0_fp32_against_oracle():
     """BASELINE config 0 shape (B=2, T=512, d_model=512, H=8, d_h=64, r=16,
     chunk 64) in float32, random gates and the outlier x8 weights."""
