@@ -18,6 +18,7 @@
 namespace hofa {
 int gla_internal_chunk(int D);
 size_t gla_tc_workspace_bytes(int64_t B, int64_t H, int64_t T, int64_t J, int64_t D);
+void gla_tc_bind_workspace(GlaParams& p, void* ws);
 bool gla_tc_eligible(const GlaParams& p, int dtype);
 cudaError_t launch_gla_tc(const GlaParams& p, int dtype, cudaStream_t st, bool* taken);
 int gla_tc_chunk();
@@ -593,8 +594,7 @@ int hofa_prefill_gla_fwd(const hofa_gla_args* a, void* stream) {
       tp.dt_lg = a->log_gamma.dtype;
       tp.dt_mg = p.fuse ? a->mix_g.dtype : 0;
       tp.dt_gs = p.fuse ? a->gla_scale.dtype : 0;
-      tp.ws_state = reinterpret_cast<float*>(a->workspace);
-      tp.ws_decay = tp.ws_state + (size_t)B * H * tp.nseg * J * D;
+      hofa::gla_tc_bind_workspace(tp, a->workspace);
       bool taken = false;
       cudaError_t e = hofa::launch_gla_tc(tp, dt, reinterpret_cast<cudaStream_t>(stream), &taken);
       if (e != cudaSuccess) return cuda_fail(e, "hofa_prefill_gla_fwd launch (tensor cores)");

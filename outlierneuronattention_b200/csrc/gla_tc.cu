@@ -162,12 +162,14 @@ gla_tc_state_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
   // TMEM columns under one commit.
   {
     const float w = sm100::ex2_approx((gc - G) * kLog2e);
+    const int rot = tid & 7;  // chunk order q ^ (lane & 7): the warp's lanes spread over all banks
 #pragma unroll
     for (int nb = 0; nb < Gm::NB; ++nb) {
       uint4* row = reinterpret_cast<uint4*>(sK + nb * kTile + tid * 128);
       uint4* lrow = reinterpret_cast<uint4*>(sL + nb * kTile + tid * 128);
 #pragma unroll
-      for (int q = 0; q < 8; ++q) {
+      for (int q0 = 0; q0 < 8; ++q0) {
+        const int q = q0 ^ rot;
         uint4 u = row[q], l;
         uint32_t* pu = reinterpret_cast<uint32_t*>(&u);
         uint32_t* pl = reinterpret_cast<uint32_t*>(&l);
@@ -504,6 +506,495 @@ gla_tc_out_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
   if (warp == 0) sm100::tmem_dealloc(tmem, Gm::OUT_COLS);
 }
 
+// ---------------------------------------------------------------------------
+// F: single-launch form at head dim 64 (replaces A + B + C there)
+//
+// One CTA per chunk as in C, but the chunk comes from a ticket (atomic counter)
+// handed out chunk-major over all (b,h), and the chunk-to-chunk state carry is
+// done inside the launch by a decoupled look-back (Merrill and Garland, "Single-
+// pass Parallel Prefix Scan with Decoupled Look-back", 2016):
+//   1. dS_c = Kd^T V as in A (hi + lo terms), stored as the chunk's aggregate;
+//      flag_c = AGG (release).  This needs nothing from other chunks.
+//   2. start_c = sum over the chunks k < c back to the nearest one whose
+//      inclusive state is published: exp(G_{k+1} + ... + G_{c-1}) * (dS_k, or
+//      the inclusive state of the last one), or state_init when the walk
+//      reaches the sequence start.  The multipliers are exponentials of sums
+//      of non-positive chunk log decays.
+//   3. inclusive_c = exp(G_C) start_c + dS_c; flag_c = INCL (release).
+//   4. outputs as in C, with start_c as the bf16 operand of Y2.
+// A CTA waits only for chunks with a lower ticket, which are resident and reach
+// step 1 without waiting on anything, so every wait ends; each is bounded by
+// wall time all the same, and a CTA that gives up publishes ERR, which its
+// successors propagate instead of waiting.  DRAM traffic: Q, K, V read once, y
+// written once; the per-chunk states live in L2 between publication and use.
+//
+// TMEM (128 columns, three CTAs per SM): A = Q K^T in [0,128); P in [0,64);
+// dS (M = 64) in [64,128), read out before Y1 = P V takes [64,128); Y2 in
+// [0,64) once Y1 has consumed P.  Shared memory: Q, K (then Kd hi, then dS as
+// fp32), V, X (Kd lo, then start_c as the bf16 operand).
+// ---------------------------------------------------------------------------
+constexpr int kFlagAgg = 1, kFlagIncl = 2, kFlagErr = 3;
+constexpr uint32_t kFusedCols = 128;
+constexpr size_t kFusedSmem = 4 * (size_t)kTile + 1024 + 2048;
+
+// flag word: state in the low 32 bits, the chunk's natural-log decay G_C (f32
+// bits) in the high 32, so one acquire load returns both
+__device__ __forceinline__ unsigned long long ld_acquire_gpu(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.acquire.gpu.global.b64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_gpu(unsigned long long* p, int state, float gc) {
+  const unsigned long long v = ((unsigned long long)__float_as_uint(gc) << 32) | (unsigned)state;
+  asm volatile("st.release.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 3)
+gla_tc_fused_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                    const __grid_constant__ CUtensorMap tv, const GlaParams p) {
+  constexpr int D = 64;
+  constexpr bool BF16 = std::is_same<T, __nv_bfloat16>::value;
+  constexpr uint32_t IDESC_A = sm100::idesc_f16(BF16, false, false, 128, 128);
+  constexpr uint32_t IDESC_Y = sm100::idesc_f16(BF16, false, true, 128, D);
+  constexpr uint32_t IDESC_S = sm100::idesc_f16(BF16, true, true, 64, D);
+  extern __shared__ unsigned char smem_raw[];
+  unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* sQ = base;
+  unsigned char* sK = base + kTile;
+  unsigned char* sV = base + 2 * kTile;
+  unsigned char* sX = base + 3 * kTile;
+  float* sG = reinterpret_cast<float*>(base + 4 * kTile);  // cumulative log2 decay per token
+  float* sGS = sG + kC;                                     // gla_scale[h, 0:64]
+  float* sPm = sGS + D;                                     // look-back plan: multipliers
+  int* sPi = reinterpret_cast<int*>(sPm + 32);              //   and entries (4 * chunk + kind)
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sPi + 32);
+  float* sm_warp = reinterpret_cast<float*>(bars + 3);
+  int* misc = reinterpret_cast<int*>(sm_warp + 4);  // tmem slot, err, ticket, plan size, plan final, G_C
+  float* sGC = reinterpret_cast<float*>(misc + 6);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (warp == 0) {
+    sm100::tmem_alloc(reinterpret_cast<uint32_t*>(&misc[0]), kFusedCols);
+    sm100::tmem_relinquish();
+  }
+  // the ticket is taken once the TMEM columns are held: a CTA that waits in the
+  // allocation (for CTAs of another kernel on the SM) holds no place in the
+  // chain that other chunks wait on
+  if (tid == 0) {
+    sm100::mbar_init(&bars[0], 1);
+    sm100::mbar_init(&bars[1], 1);
+    sm100::mbar_init(&bars[2], 1);
+    misc[1] = 0;
+    misc[2] = (int)atomicAdd(p.ws_ticket, 1u);
+    sm100::fence_mbar_init();
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  sm100::tc_fence_after();
+  const uint32_t tmem = static_cast<uint32_t>(misc[0]);
+  const int BH = p.B * p.H;
+  const int c = misc[2] / BH, bh = misc[2] % BH;
+  const int b = bh / p.H, h = bh % p.H;
+  const int t0 = c * kC;
+  const int J = p.J, KS = (J + 15) / 16;
+  const int64_t ci = (int64_t)bh * p.nseg + c;  // this chunk's slot in the workspace
+  const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+  int* err = &misc[1];
+  volatile int* verr = err;
+  if (tid == 0) {
+    sm100::mbar_arrive_expect_tx(&bars[0], 3 * kTile);
+    sm100::tma_load_4d(sQ, &tq, p.R, t0, h, b, &bars[0]);
+    sm100::tma_load_4d(sK, &tk, p.R, t0, h, b, &bars[0]);
+    sm100::tma_load_4d(sV, &tv, 0, t0, h, b, &bars[0]);
+  }
+  const int t = t0 + tid;
+  const float g = t < p.T ? ld_any(p.log_gamma, p.dt_lg, b * p.slg[0] + h * p.slg[1] + (int64_t)t * p.slg[2]) : 0.f;
+  float mix = 0.f;
+  if (p.fuse && t < p.T) mix = ld_any(p.mix_g, p.dt_mg, b * p.smg[0] + h * p.smg[1] + (int64_t)t * p.smg[2]);
+  const float gsv = tid < D && p.fuse ? ld_any(p.gla_scale, p.dt_gs, h * p.sgs[0] + tid * p.sgs[1]) : 1.f;
+  const float Gn = block_scan128(g, sm_warp, tid);  // natural log, inclusive over the chunk
+  const float G = Gn * kLog2e;
+  sG[tid] = G;
+  if (tid == kThreads - 1) *sGC = Gn;
+  if (tid < D) sGS[tid] = gsv;
+  if (!sm100::mbar_wait(&bars[0], 0)) atomicOr(err, 1);
+  sm100::tc_fence_before();
+  __syncthreads();
+  const float gc = *sGC;
+  auto kstep = [](int ks) { return (uint64_t)((ks & 3) * 32 >> 4); };  // 16 channels in a 128-byte row
+  if (tid == 0 && !*verr) {
+    sm100::tc_fence_after();
+    const uint64_t qdesc = sm100::smem_desc(sQ, 16, 1024, sm100::kSwizzle128);
+    const uint64_t kdesc = sm100::smem_desc(sK, 16, 1024, sm100::kSwizzle128);
+    for (int ks = 0; ks < KS; ++ks) sm100::mma_ss(tmem, qdesc + kstep(ks), kdesc + kstep(ks), IDESC_A, ks > 0);
+    sm100::mma_commit(&bars[1]);
+  }
+  // Kd = K * exp(G_C - G_t) as hi + lo 16-bit terms (see A): lo into X now, hi
+  // kept in registers until the A product has read K.  Lane l visits the
+  // 16-byte chunks of its row in the order q ^ (l & 7), so the 32 lanes of a
+  // warp spread over all banks (the scale is the same for the whole row).
+  uint32_t khi[32];
+  const int rot = tid & 7;
+  {
+    const float w = sm100::ex2_approx((gc - Gn) * kLog2e);
+    const uint4* row = reinterpret_cast<const uint4*>(sK + tid * 128);
+    uint4* lrow = reinterpret_cast<uint4*>(sX + tid * 128);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const uint4 u = row[q ^ rot];
+      const uint32_t pu[4] = {u.x, u.y, u.z, u.w};
+      uint32_t pl[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float a, bb;
+        if (BF16) bf16x2_to_f(pu[e], a, bb);
+        else f16x2_to_f(pu[e], a, bb);
+        const float xa = a * w, xb = bb * w;
+        khi[4 * q + e] = pack2(xa, xb, BF16);
+        float ha, hb;
+        if (BF16) bf16x2_to_f(khi[4 * q + e], ha, hb);
+        else f16x2_to_f(khi[4 * q + e], ha, hb);
+        pl[e] = pack2(xa - ha, xb - hb, BF16);
+      }
+      lrow[q ^ rot] = make_uint4(pl[0], pl[1], pl[2], pl[3]);
+    }
+  }
+  if (!*verr && !sm100::mbar_wait(&bars[1], 0)) atomicOr(err, 1);
+  sm100::tc_fence_after();
+  {
+    uint4* row = reinterpret_cast<uint4*>(sK + tid * 128);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) row[q ^ rot] = make_uint4(khi[4 * q], khi[4 * q + 1], khi[4 * q + 2], khi[4 * q + 3]);
+  }
+  // P = A * exp(G_i - G_j) for j <= i, as 16-bit pairs over columns [0, 64)
+  const int i = tid;
+#pragma unroll
+  for (int cc = 0; cc < kC; cc += 64) {
+    uint32_t r0[32], r1[32], pk[32];
+    sm100::tmem_ld32(tmem + lane_off + cc, r0);
+    sm100::tmem_ld32(tmem + lane_off + cc + 32, r1);
+    sm100::tc_wait_ld();
+#pragma unroll
+    for (int u = 0; u < 16; ++u) {
+      const int j0 = cc + 2 * u, j1 = cc + 32 + 2 * u;
+      const float a0 = j0 <= i ? __uint_as_float(r0[2 * u]) * sm100::ex2_approx(G - sG[j0]) : 0.f;
+      const float a1 = j0 + 1 <= i ? __uint_as_float(r0[2 * u + 1]) * sm100::ex2_approx(G - sG[j0 + 1]) : 0.f;
+      const float a2 = j1 <= i ? __uint_as_float(r1[2 * u]) * sm100::ex2_approx(G - sG[j1]) : 0.f;
+      const float a3 = j1 + 1 <= i ? __uint_as_float(r1[2 * u + 1]) * sm100::ex2_approx(G - sG[j1 + 1]) : 0.f;
+      pk[u] = pack2(a0, a1, BF16);
+      pk[16 + u] = pack2(a2, a3, BF16);
+    }
+    sm100::tmem_st32(tmem + lane_off + cc / 2, pk);
+  }
+  sm100::tc_wait_st();
+  fence_async_smem();
+  sm100::tc_fence_before();
+  __syncthreads();
+  // dS = Kd^T V (M = 64 inlier rows, N = 64, K = 128 tokens) into columns [64, 128)
+  if (tid == 0 && !*verr) {
+    sm100::tc_fence_after();
+    const uint64_t adesc = sm100::smem_desc(sK, 16, 1024, sm100::kSwizzle128);
+    const uint64_t ldesc = sm100::smem_desc(sX, 16, 1024, sm100::kSwizzle128);
+    const uint64_t vdesc = sm100::smem_desc(sV, 16, 1024, sm100::kSwizzle128);
+#pragma unroll
+    for (int ks = 0; ks < kC / 16; ++ks)
+      sm100::mma_ss(tmem + 64, adesc + (uint64_t)(ks * 2048 >> 4), vdesc + (uint64_t)(ks * 2048 >> 4), IDESC_S, ks > 0);
+#pragma unroll
+    for (int ks = 0; ks < kC / 16; ++ks)
+      sm100::mma_ss(tmem + 64, ldesc + (uint64_t)(ks * 2048 >> 4), vdesc + (uint64_t)(ks * 2048 >> 4), IDESC_S, true);
+    sm100::mma_commit(&bars[1]);
+  }
+  if (!*verr && !sm100::mbar_wait(&bars[1], 1)) atomicOr(err, 1);
+  sm100::tc_fence_after();
+  // aggregate: dS rows (M = 64: row j in lane 32*(j/16) + j%16) into shared
+  // memory over the K tile as fp32 [J][64], 16-byte chunk c of row j at
+  // position c ^ (j & 15) (the row-owning lanes then spread over the banks);
+  // from there to the workspace in coalesced slots below
+  float* sA = reinterpret_cast<float*>(sK);
+  auto sa_at = [&](int j, int c) { return sA + j * D + ((c ^ (j & 15)) << 2); };
+  {
+    const int jr = 16 * warp + lane;
+    const bool row_ok = lane < 16 && jr < J;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      uint32_t r[32];
+      sm100::tmem_ld32(tmem + 64 + lane_off + half * 32, r);
+      sm100::tc_wait_ld();
+      if (row_ok) {
+#pragma unroll
+        for (int u = 0; u < 32; u += 4)
+          *reinterpret_cast<float4*>(sa_at(jr, (half * 32 + u) >> 2)) =
+              make_float4(__uint_as_float(r[u]), __uint_as_float(r[u + 1]), __uint_as_float(r[u + 2]),
+                          __uint_as_float(r[u + 3]));
+      }
+    }
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  // Y1 = P V into columns [64, 128) (dS has been read out).  The publication
+  // (a fence that waits for every store above, then the flag) is left to warp
+  // 3, off the paths of the MMA issue and of the look-back (warp 1).
+  if (tid == 0 && !*verr) {
+    sm100::tc_fence_after();
+    const uint64_t vdesc = sm100::smem_desc(sV, 16, 1024, sm100::kSwizzle128);
+#pragma unroll
+    for (int kk = 0; kk < kC / 16; ++kk)
+      sm100::mma_ts(tmem + 64, tmem + kk * 8, vdesc + (uint64_t)(kk * 2048 >> 4), IDESC_Y, kk > 0);
+    sm100::mma_commit(&bars[1]);
+  }
+  {
+    float4* agg = reinterpret_cast<float4*>(p.ws_agg + ci * J * D);
+    for (int f = tid; f < 16 * J; f += kThreads) agg[f] = *reinterpret_cast<const float4*>(sa_at(f >> 4, f & 15));
+  }
+  __syncthreads();
+  if (tid == 96) {
+    __threadfence();
+    st_release_gpu(&p.ws_flags[ci], *verr ? kFlagErr : kFlagAgg, gc);
+  }
+
+  // look-back for start_c.  Thread tid owns the float4 slots f = tid + 128 q of
+  // the [J][64] state (16 per row).  Warp 1 reads the flags of 32 chunks at a
+  // time (lane l: chunk k_hi - l) and writes a plan: every chunk before the
+  // first one with a published inclusive state (or the sequence start) enters
+  // with its aggregate, that one with its inclusive state; all threads then add
+  // their slots of the planned entries.
+  constexpr int NQ = 8;  // J <= 64: at most 1024 float4 slots
+  float4 acc[NQ];
+#pragma unroll
+  for (int q = 0; q < NQ; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
+  const int nslot = 16 * J;
+  const int64_t chunk0 = (int64_t)bh * p.nseg;
+  int k_hi = c - 1;
+  float logm = 0.f;  // natural-log multiplier of the next planned entry (warp 1)
+  const uint64_t t_start = sm100::globaltimer_ns();
+  while (true) {
+    if (warp == 1) {
+      const int kk = k_hi - lane;
+      int fl = 0, s = 32;
+      float gdk = 0.f;
+      while (true) {
+        if (kk >= 0) {
+          const unsigned long long w = ld_acquire_gpu(&p.ws_flags[chunk0 + kk]);
+          fl = (int)(unsigned)(w & 0xffffffffu);
+          gdk = __uint_as_float((unsigned)(w >> 32));
+        } else {
+          fl = kFlagIncl;
+        }
+        const unsigned term = __ballot_sync(0xffffffffu, fl >= kFlagIncl);
+        const unsigned none = __ballot_sync(0xffffffffu, fl == 0);
+        s = term ? __ffs(term) - 1 : 32;
+        const unsigned need = s == 32 ? 0xffffffffu : ((1u << s) - 1u);
+        if ((none & need) == 0) break;
+        int late = 0;
+        if (lane == 0) late = sm100::globaltimer_ns() - t_start > 200000000ull;
+        if (__shfl_sync(0xffffffffu, late, 0)) {
+          s = -1;
+          break;
+        }
+        __nanosleep(64);
+      }
+      if (s < 0 || (s < 32 && __shfl_sync(0xffffffffu, fl, s) == kFlagErr)) {
+        if (lane == 0) {
+          atomicOr(err, 1);
+          misc[3] = 0;
+          misc[4] = 1;
+        }
+      } else {
+        // multipliers: exp(logm + sum of the decays of the aggregate entries before)
+        const float gd = lane < s ? gdk : 0.f;
+        float pre = gd;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const float y = __shfl_up_sync(0xffffffffu, pre, o);
+          if (lane >= o) pre += y;
+        }
+        const float lm = logm + pre - gd;
+        if (lane <= s && lane < 32) {
+          const int kind = lane < s ? 0 : (kk >= 0 ? 1 : 2);  // aggregate, inclusive, state_init
+          sPi[lane] = 4 * (kk >= 0 ? kk : 0) + kind;
+          sPm[lane] = sm100::ex2_approx(lm * kLog2e);
+        }
+        logm += __shfl_sync(0xffffffffu, pre, 31);
+        if (lane == 0) {
+          misc[3] = s < 32 ? s + 1 : 32;
+          misc[4] = s < 32;
+        }
+      }
+    }
+    __syncthreads();
+    const int n = misc[3];
+    const bool fin = misc[4] != 0;
+    // two planned entries per step, their loads in flight together
+    auto src_of = [&](int code) {
+      return reinterpret_cast<const float4*>(((code & 3) == 0 ? p.ws_agg : p.ws_incl) + (chunk0 + (code >> 2)) * J * D);
+    };
+    auto add_init = [&](float m) {
+      if (p.state_init == nullptr) return;
+      const float* s0 = p.state_init + b * p.ssi[0] + h * p.ssi[1];
+#pragma unroll
+      for (int q = 0; q < NQ; ++q) {
+        const int f = tid + 128 * q;
+        if (f < nslot) {
+          const float* r = s0 + (f >> 4) * p.ssi[2] + (f & 15) * 4;
+          acc[q].x = fmaf(m, r[0], acc[q].x);
+          acc[q].y = fmaf(m, r[1], acc[q].y);
+          acc[q].z = fmaf(m, r[2], acc[q].z);
+          acc[q].w = fmaf(m, r[3], acc[q].w);
+        }
+      }
+    };
+    for (int e = 0; e < n; e += 2) {
+      const int c0 = sPi[e];
+      const int c1 = e + 1 < n ? sPi[e + 1] : 2;  // a missing second entry reads as "state_init" with m = 0
+      const float m0 = sPm[e];
+      const float m1 = e + 1 < n ? sPm[e + 1] : 0.f;
+      const bool g0 = (c0 & 3) != 2, g1 = (c1 & 3) != 2;
+      const float4* p0 = src_of(g0 ? c0 : 0);
+      const float4* p1 = src_of(g1 ? c1 : 0);
+      float4 x0[NQ], x1[NQ];
+#pragma unroll
+      for (int q = 0; q < NQ; ++q) {
+        const int f = tid + 128 * q;
+        x0[q] = g0 && f < nslot ? __ldcg(p0 + f) : make_float4(0.f, 0.f, 0.f, 0.f);
+        x1[q] = g1 && f < nslot ? __ldcg(p1 + f) : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int q = 0; q < NQ; ++q) {
+        acc[q].x = fmaf(m1, x1[q].x, fmaf(m0, x0[q].x, acc[q].x));
+        acc[q].y = fmaf(m1, x1[q].y, fmaf(m0, x0[q].y, acc[q].y));
+        acc[q].z = fmaf(m1, x1[q].z, fmaf(m0, x0[q].z, acc[q].z));
+        acc[q].w = fmaf(m1, x1[q].w, fmaf(m0, x0[q].w, acc[q].w));
+      }
+      if (!g0) add_init(m0);
+      if (!g1 && e + 1 < n) add_init(m1);
+    }
+    if (fin) break;
+    k_hi -= 32;
+    __syncthreads();  // warp 1 rewrites the plan next round
+  }
+
+  // start_c -> X as the bf16 operand of Y2 (rows j, 128-byte swizzled, rows
+  // J .. 16*KS zero); inclusive_c = exp(G_C) start_c + dS_c -> workspace (and
+  // the final state for the last chunk)
+  const float egc = sm100::ex2_approx(gc * kLog2e);
+  float* incl = p.ws_incl + ci * J * D;
+  const bool last = c == p.nseg - 1 && p.state_out != nullptr;
+#pragma unroll
+  for (int q = 0; q < NQ; ++q) {
+    const int f = tid + 128 * q;
+    const int j = f >> 4, d0 = (f & 15) * 4;
+    if (j < 16 * KS) {
+      const float4 v = f < nslot ? acc[q] : make_float4(0.f, 0.f, 0.f, 0.f);
+      *reinterpret_cast<uint2*>(sX + j * 128 + (((d0 >> 3) ^ (j & 7)) << 4) + (d0 & 7) * 2) =
+          make_uint2(pack2(v.x, v.y, BF16), pack2(v.z, v.w, BF16));
+    }
+    if (f < nslot) {
+      const float4 a = *reinterpret_cast<const float4*>(sa_at(j, f & 15));
+      const float4 o = make_float4(fmaf(egc, acc[q].x, a.x), fmaf(egc, acc[q].y, a.y), fmaf(egc, acc[q].z, a.z),
+                                   fmaf(egc, acc[q].w, a.w));
+      *reinterpret_cast<float4*>(incl + f * 4) = o;
+      if (last) {
+        float* so = p.state_out + b * p.sso[0] + h * p.sso[1] + j * p.sso[2] + d0 * p.sso[3];
+        so[0] = o.x;
+        so[p.sso[3]] = o.y;
+        so[2 * p.sso[3]] = o.z;
+        so[3 * p.sso[3]] = o.w;
+      }
+    }
+  }
+  fence_async_smem();
+  __syncthreads();
+  if (tid == 96) {
+    __threadfence();
+    st_release_gpu(&p.ws_flags[ci], *verr ? kFlagErr : kFlagIncl, gc);
+  }
+  // Y1 complete -> P's columns are free: Y2 = Q_I start_c into [0, 64)
+  if (!*verr && !sm100::mbar_wait(&bars[1], 0)) atomicOr(err, 1);
+  sm100::tc_fence_after();
+  if (tid == 0 && !*verr) {
+    const uint64_t qdesc = sm100::smem_desc(sQ, 16, 1024, sm100::kSwizzle128);
+    const uint64_t sdesc = sm100::smem_desc(sX, 16, 1024, sm100::kSwizzle128);
+    for (int ks = 0; ks < KS; ++ks)
+      sm100::mma_ss(tmem, qdesc + kstep(ks), sdesc + (uint64_t)(ks * 2048 >> 4), IDESC_Y, ks > 0);
+    sm100::mma_commit(&bars[2]);
+  }
+  // Y2 completes on a barrier of its own: a thread still on its way to the Y1
+  // wait (the publishing warp) must not find bars[1] two phases ahead
+  if (!*verr && !sm100::mbar_wait(&bars[2], 0)) atomicOr(err, 1);
+  sm100::tc_fence_after();
+
+  // epilogue as in C: y = Y1 + exp(G_i) Y2, fused (1 - mix) * gla_scale * RMSNorm(y)
+  const uint32_t tY1 = tmem + 64, tY2 = tmem;
+  const float eg = sm100::ex2_approx(G);
+  float scale = 1.f;
+  if (p.fuse) {
+    float ss = 0.f;
+#pragma unroll
+    for (int cc = 0; cc < D; cc += 32) {
+      uint32_t a[32], bb[32];
+      sm100::tmem_ld32(tY1 + lane_off + cc, a);
+      sm100::tmem_ld32(tY2 + lane_off + cc, bb);
+      sm100::tc_wait_ld();
+#pragma unroll
+      for (int u = 0; u < 32; ++u) {
+        const float y = fmaf(eg, __uint_as_float(bb[u]), __uint_as_float(a[u]));
+        ss = fmaf(y, y, ss);
+      }
+    }
+    scale = rsqrtf(ss / (float)D + p.eps) * (1.f - mix);
+  }
+  const bool store = t < p.T && !*verr;
+  T* yp = reinterpret_cast<T*>(p.y) + b * p.sy[0] + h * p.sy[1] + (int64_t)(store ? t : 0) * p.sy[2];
+  const bool vec = p.sy[3] == 1 && (reinterpret_cast<uintptr_t>(yp) & 15u) == 0;
+#pragma unroll
+  for (int cc = 0; cc < D; cc += 32) {
+    uint32_t a[32], bb[32];
+    sm100::tmem_ld32(tY1 + lane_off + cc, a);
+    sm100::tmem_ld32(tY2 + lane_off + cc, bb);
+    sm100::tc_wait_ld();
+    if (store) {
+      float y[32];
+#pragma unroll
+      for (int u = 0; u < 32; ++u) y[u] = fmaf(eg, __uint_as_float(bb[u]), __uint_as_float(a[u])) * scale * sGS[cc + u];
+      if (vec) {
+#pragma unroll
+        for (int d = 0; d < 32; d += 8) {
+          uint4 w;
+          w.x = pack2(y[d], y[d + 1], BF16);
+          w.y = pack2(y[d + 2], y[d + 3], BF16);
+          w.z = pack2(y[d + 4], y[d + 5], BF16);
+          w.w = pack2(y[d + 6], y[d + 7], BF16);
+          *reinterpret_cast<uint4*>(yp + cc + d) = w;
+        }
+      } else {
+#pragma unroll
+        for (int d = 0; d < 32; ++d) yp[(int64_t)(cc + d) * p.sy[3]] = from_f<T>(y[d]);
+      }
+    }
+  }
+  sm100::tc_fence_before();
+  __syncthreads();
+  if (*err && tid == 0) atomicOr(&g_gla_tc_status, 1);
+  if (warp == 0) sm100::tmem_dealloc(tmem, kFusedCols);
+}
+
+// Workspace of the single-launch form: ticket counter, per-chunk flags and
+// log decays, aggregates and inclusive states (byte offsets from the base).
+struct FusedLayout {
+  size_t flags, decay, agg, incl, total;
+};
+FusedLayout fused_layout(int64_t nch, int64_t J) {
+  auto r256 = [](size_t x) { return (x + 255) / 256 * 256; };
+  FusedLayout L;
+  L.flags = 256;
+  L.decay = L.flags + r256((size_t)nch * 8);
+  L.agg = L.decay + r256((size_t)nch * 4);
+  L.incl = L.agg + r256((size_t)nch * J * 64 * 4);
+  L.total = L.incl + r256((size_t)nch * J * 64 * 4);
+  return L;
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static bool tried = false;
@@ -542,6 +1033,18 @@ cudaError_t launch_t(const GlaParams& p, cudaStream_t st, bool* taken) {
   if (!make_map(&mq, p.q, bf16, D, p.T, p.H, p.B, p.sq) || !make_map(&mk, p.k, bf16, D, p.T, p.H, p.B, p.sk) ||
       !make_map(&mv, p.v, bf16, D, p.T, p.H, p.B, p.sv))
     return cudaSuccess;
+  if constexpr (D == 64) {
+    auto kF = gla_tc_fused_kernel<T>;
+    cudaError_t e = cudaFuncSetAttribute(kF, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFusedSmem);
+    if (e != cudaSuccess) return e;
+    *taken = true;
+    const int64_t nch = (int64_t)p.B * p.H * p.nseg;
+    // ticket and flags start at zero in every call (one memset of the front of the workspace)
+    e = cudaMemsetAsync(p.ws_ticket, 0, fused_layout(nch, p.J).decay, st);
+    if (e != cudaSuccess) return e;
+    kF<<<(unsigned)nch, kThreads, kFusedSmem, st>>>(mq, mk, mv, p);
+    return cudaGetLastError();
+  }
   auto kA = gla_tc_state_kernel<T, D>;
   auto kC_ = gla_tc_out_kernel<T, D>;
   cudaError_t e = cudaFuncSetAttribute(kA, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Gm::STATE_SMEM);
@@ -560,10 +1063,29 @@ cudaError_t launch_t(const GlaParams& p, cudaStream_t st, bool* taken) {
 
 }  // namespace
 
-// Workspace bytes of the tensor-core path (start states + chunk decays).
+// Workspace bytes of the tensor-core path: at head dim 64 the single-launch
+// form's layout, otherwise start states + chunk decays of the three-launch form.
 size_t gla_tc_workspace_bytes(int64_t B, int64_t H, int64_t T, int64_t J, int64_t D) {
   const int64_t nc = (T + kC - 1) / kC;
+  if (D == 64) return fused_layout(B * H * nc, J).total;
   return (size_t)(B * H * nc * (J * D + 1)) * sizeof(float) + 256;
+}
+
+// Points the workspace fields of `p` (B, H, J, D and nseg set) into `ws`.
+void gla_tc_bind_workspace(GlaParams& p, void* ws) {
+  unsigned char* base = reinterpret_cast<unsigned char*>(ws);
+  if (p.D == 64) {
+    const FusedLayout L = fused_layout((int64_t)p.B * p.H * p.nseg, p.J);
+    p.ws_ticket = reinterpret_cast<unsigned*>(base);
+    p.ws_flags = reinterpret_cast<unsigned long long*>(base + L.flags);
+    p.ws_decay = reinterpret_cast<float*>(base + L.decay);
+    p.ws_agg = reinterpret_cast<float*>(base + L.agg);
+    p.ws_incl = reinterpret_cast<float*>(base + L.incl);
+    p.ws_state = nullptr;
+    return;
+  }
+  p.ws_state = reinterpret_cast<float*>(ws);
+  p.ws_decay = p.ws_state + (size_t)p.B * p.H * p.nseg * p.J * p.D;
 }
 
 bool gla_tc_eligible(const GlaParams& p, int dtype) {

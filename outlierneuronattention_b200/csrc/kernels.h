@@ -71,6 +71,12 @@ struct GlaParams {
   int dt_lg, dt_mg, dt_la, dt_gs;
   float* ws_state;            // [B,H,nseg,J,D] local end states
   float* ws_decay;            // [B,H,nseg,J] log of the segment's total decay
+  // single-launch tensor-core form (head dim 64): chunk tickets, per-chunk
+  // publication flags, each chunk's state contribution and the state after it
+  unsigned* ws_ticket;
+  unsigned long long* ws_flags;  // [B*H*nseg]: state in the low word, the chunk's log decay (f32 bits) in the high
+  float* ws_agg;              // [B*H*nseg, J, D]
+  float* ws_incl;             // [B*H*nseg, J, D]
 };
 
 cudaError_t launch_gla(const GlaParams& p, int dtype, cudaStream_t st);
