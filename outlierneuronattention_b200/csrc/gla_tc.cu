@@ -5,7 +5,9 @@
 // Operand tiles are [128 tokens x D channels] in 64-channel column blocks of
 // 128-byte swizzled rows (one TMA box each), so D = 128 uses two blocks.  The
 // reference runs one program per (b,h) that walks every chunk in sequence; here
-// every 128-token chunk of every (b,h) is its own CTA in two of three launches:
+// every 128-token chunk of every (b,h) is its own CTA.  Head dim 64 runs the
+// single launch F below (the chunk-to-chunk state carry done inside the launch
+// by a decoupled look-back); head dim 128 runs three launches:
 //
 //   A  gla_tc_state_kernel   (one CTA per chunk c)
 //        G   = inclusive cumsum of log_gamma over the chunk, G_C = its total
@@ -528,14 +530,16 @@ gla_tc_out_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
 // successors propagate instead of waiting.  DRAM traffic: Q, K, V read once, y
 // written once; the per-chunk states live in L2 between publication and use.
 //
-// TMEM (128 columns, three CTAs per SM): A = Q K^T in [0,128); P in [0,64);
-// dS (M = 64) in [64,128), read out before Y1 = P V takes [64,128); Y2 in
-// [0,64) once Y1 has consumed P.  Shared memory: Q, K (then Kd hi, then dS as
-// fp32), V, X (Kd lo, then start_c as the bf16 operand).
+// Four CTAs per SM: TMEM 128 columns each -- A = Q K^T in [0,128); P in
+// [0,64); dS (M = 64) in [64,128), read out before Y1 = P V takes [64,128); Y2
+// in [0,64) once Y1 has consumed P -- and three 16 KB tiles of shared memory:
+// Q (then Kd lo, then Q again, reloaded by TMA for Y2), K (then Kd hi, then dS
+// as fp32) and V (then start_c as the bf16 operand of Y2); at most 128
+// registers per thread.
 // ---------------------------------------------------------------------------
 constexpr int kFlagAgg = 1, kFlagIncl = 2, kFlagErr = 3;
 constexpr uint32_t kFusedCols = 128;
-constexpr size_t kFusedSmem = 4 * (size_t)kTile + 1024 + 2048;
+constexpr size_t kFusedSmem = 3 * (size_t)kTile + 1024 + 2048;
 
 // flag word: state in the low 32 bits, the chunk's natural-log decay G_C (f32
 // bits) in the high 32, so one acquire load returns both
@@ -549,8 +553,8 @@ __device__ __forceinline__ void st_release_gpu(unsigned long long* p, int state,
   asm volatile("st.release.gpu.global.b64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
 
-template <typename T>
-__global__ void __launch_bounds__(kThreads, 3)
+template <typename T, int NQ>
+__global__ void __launch_bounds__(kThreads, 4)
 gla_tc_fused_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                     const __grid_constant__ CUtensorMap tv, const GlaParams p) {
   constexpr int D = 64;
@@ -560,17 +564,16 @@ gla_tc_fused_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
   constexpr uint32_t IDESC_S = sm100::idesc_f16(BF16, true, true, 64, D);
   extern __shared__ unsigned char smem_raw[];
   unsigned char* base = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  unsigned char* sQ = base;
-  unsigned char* sK = base + kTile;
-  unsigned char* sV = base + 2 * kTile;
-  unsigned char* sX = base + 3 * kTile;
-  float* sG = reinterpret_cast<float*>(base + 4 * kTile);  // cumulative log2 decay per token
+  unsigned char* sQ = base;              // Q, then Kd lo, then Q again (reloaded)
+  unsigned char* sK = base + kTile;      // K, then Kd hi, then dS as fp32
+  unsigned char* sV = base + 2 * kTile;  // V, then start_c as the bf16 operand of Y2
+  float* sG = reinterpret_cast<float*>(base + 3 * kTile);  // cumulative log2 decay per token
   float* sGS = sG + kC;                                     // gla_scale[h, 0:64]
   float* sPm = sGS + D;                                     // look-back plan: multipliers
   int* sPi = reinterpret_cast<int*>(sPm + 32);              //   and entries (4 * chunk + kind)
   uint64_t* bars = reinterpret_cast<uint64_t*>(sPi + 32);
   float* sm_warp = reinterpret_cast<float*>(bars + 3);
-  int* misc = reinterpret_cast<int*>(sm_warp + 4);  // tmem slot, err, ticket, plan size, plan final, G_C
+  int* misc = reinterpret_cast<int*>(sm_warp + 4);  // tmem slot, err, ticket, plan size, plan final, plan valid
   float* sGC = reinterpret_cast<float*>(misc + 6);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -587,6 +590,7 @@ gla_tc_fused_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
     sm100::mbar_init(&bars[2], 1);
     misc[1] = 0;
     misc[2] = (int)atomicAdd(p.ws_ticket, 1u);
+    misc[5] = 0;
     sm100::fence_mbar_init();
   }
   sm100::tc_fence_before();
@@ -599,6 +603,7 @@ gla_tc_fused_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
   const int t0 = c * kC;
   const int J = p.J, KS = (J + 15) / 16;
   const int64_t ci = (int64_t)bh * p.nseg + c;  // this chunk's slot in the workspace
+  const int64_t chunk0 = (int64_t)bh * p.nseg;
   const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
   int* err = &misc[1];
   volatile int* verr = err;
@@ -630,62 +635,66 @@ gla_tc_fused_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
     for (int ks = 0; ks < KS; ++ks) sm100::mma_ss(tmem, qdesc + kstep(ks), kdesc + kstep(ks), IDESC_A, ks > 0);
     sm100::mma_commit(&bars[1]);
   }
-  // Kd = K * exp(G_C - G_t) as hi + lo 16-bit terms (see A): lo into X now, hi
-  // kept in registers until the A product has read K.  Lane l visits the
-  // 16-byte chunks of its row in the order q ^ (l & 7), so the 32 lanes of a
-  // warp spread over all banks (the scale is the same for the whole row).
-  uint32_t khi[32];
+  // Kd = K * exp(G_C - G_t) as hi + lo 16-bit terms (see A).  lo is formed in
+  // registers while the A product runs; once it has read Q and K, hi goes over
+  // K and lo over Q.  Lane l visits the 16-byte chunks of its row in the order
+  // q ^ (l & 7), so the 32 lanes of a warp spread over all banks.
   const int rot = tid & 7;
+  const float kw = sm100::ex2_approx((gc - Gn) * kLog2e);
+  auto kd_hi = [&](uint32_t u, float& xa, float& xb) {
+    float a, bb;
+    if (BF16) bf16x2_to_f(u, a, bb);
+    else f16x2_to_f(u, a, bb);
+    xa = a * kw;
+    xb = bb * kw;
+    return pack2(xa, xb, BF16);
+  };
+  uint32_t klo[32];
   {
-    const float w = sm100::ex2_approx((gc - Gn) * kLog2e);
     const uint4* row = reinterpret_cast<const uint4*>(sK + tid * 128);
-    uint4* lrow = reinterpret_cast<uint4*>(sX + tid * 128);
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       const uint4 u = row[q ^ rot];
       const uint32_t pu[4] = {u.x, u.y, u.z, u.w};
-      uint32_t pl[4];
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
-        float a, bb;
-        if (BF16) bf16x2_to_f(pu[e], a, bb);
-        else f16x2_to_f(pu[e], a, bb);
-        const float xa = a * w, xb = bb * w;
-        khi[4 * q + e] = pack2(xa, xb, BF16);
-        float ha, hb;
-        if (BF16) bf16x2_to_f(khi[4 * q + e], ha, hb);
-        else f16x2_to_f(khi[4 * q + e], ha, hb);
-        pl[e] = pack2(xa - ha, xb - hb, BF16);
+        float xa, xb, ha, hb;
+        const uint32_t hi = kd_hi(pu[e], xa, xb);
+        if (BF16) bf16x2_to_f(hi, ha, hb);
+        else f16x2_to_f(hi, ha, hb);
+        klo[4 * q + e] = pack2(xa - ha, xb - hb, BF16);
       }
-      lrow[q ^ rot] = make_uint4(pl[0], pl[1], pl[2], pl[3]);
     }
   }
   if (!*verr && !sm100::mbar_wait(&bars[1], 0)) atomicOr(err, 1);
   sm100::tc_fence_after();
   {
     uint4* row = reinterpret_cast<uint4*>(sK + tid * 128);
+    uint4* qrow = reinterpret_cast<uint4*>(sQ + tid * 128);
 #pragma unroll
-    for (int q = 0; q < 8; ++q) row[q ^ rot] = make_uint4(khi[4 * q], khi[4 * q + 1], khi[4 * q + 2], khi[4 * q + 3]);
+    for (int q = 0; q < 8; ++q) {
+      const uint4 u = row[q ^ rot];
+      float xa, xb;
+      row[q ^ rot] = make_uint4(kd_hi(u.x, xa, xb), kd_hi(u.y, xa, xb), kd_hi(u.z, xa, xb), kd_hi(u.w, xa, xb));
+      qrow[q ^ rot] = make_uint4(klo[4 * q], klo[4 * q + 1], klo[4 * q + 2], klo[4 * q + 3]);
+    }
   }
-  // P = A * exp(G_i - G_j) for j <= i, as 16-bit pairs over columns [0, 64)
+  // P = A * exp(G_i - G_j) for j <= i, as 16-bit pairs over columns [0, 64),
+  // 32 columns of A at a time
   const int i = tid;
 #pragma unroll
-  for (int cc = 0; cc < kC; cc += 64) {
-    uint32_t r0[32], r1[32], pk[32];
-    sm100::tmem_ld32(tmem + lane_off + cc, r0);
-    sm100::tmem_ld32(tmem + lane_off + cc + 32, r1);
+  for (int cc = 0; cc < kC; cc += 32) {
+    uint32_t r[32], pk[16];
+    sm100::tmem_ld32(tmem + lane_off + cc, r);
     sm100::tc_wait_ld();
 #pragma unroll
     for (int u = 0; u < 16; ++u) {
-      const int j0 = cc + 2 * u, j1 = cc + 32 + 2 * u;
-      const float a0 = j0 <= i ? __uint_as_float(r0[2 * u]) * sm100::ex2_approx(G - sG[j0]) : 0.f;
-      const float a1 = j0 + 1 <= i ? __uint_as_float(r0[2 * u + 1]) * sm100::ex2_approx(G - sG[j0 + 1]) : 0.f;
-      const float a2 = j1 <= i ? __uint_as_float(r1[2 * u]) * sm100::ex2_approx(G - sG[j1]) : 0.f;
-      const float a3 = j1 + 1 <= i ? __uint_as_float(r1[2 * u + 1]) * sm100::ex2_approx(G - sG[j1 + 1]) : 0.f;
+      const int j0 = cc + 2 * u;
+      const float a0 = j0 <= i ? __uint_as_float(r[2 * u]) * sm100::ex2_approx(G - sG[j0]) : 0.f;
+      const float a1 = j0 + 1 <= i ? __uint_as_float(r[2 * u + 1]) * sm100::ex2_approx(G - sG[j0 + 1]) : 0.f;
       pk[u] = pack2(a0, a1, BF16);
-      pk[16 + u] = pack2(a2, a3, BF16);
     }
-    sm100::tmem_st32(tmem + lane_off + cc / 2, pk);
+    sm100::tmem_st16(tmem + lane_off + cc / 2, pk);
   }
   sm100::tc_wait_st();
   fence_async_smem();
@@ -695,7 +704,7 @@ gla_tc_fused_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
   if (tid == 0 && !*verr) {
     sm100::tc_fence_after();
     const uint64_t adesc = sm100::smem_desc(sK, 16, 1024, sm100::kSwizzle128);
-    const uint64_t ldesc = sm100::smem_desc(sX, 16, 1024, sm100::kSwizzle128);
+    const uint64_t ldesc = sm100::smem_desc(sQ, 16, 1024, sm100::kSwizzle128);
     const uint64_t vdesc = sm100::smem_desc(sV, 16, 1024, sm100::kSwizzle128);
 #pragma unroll
     for (int ks = 0; ks < kC / 16; ++ks)
@@ -705,14 +714,85 @@ gla_tc_fused_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
       sm100::mma_ss(tmem + 64, ldesc + (uint64_t)(ks * 2048 >> 4), vdesc + (uint64_t)(ks * 2048 >> 4), IDESC_S, true);
     sm100::mma_commit(&bars[1]);
   }
+  // look-back plan (warp 1): lanes read the flags of chunks k_hi - lane; every
+  // chunk before the first one with a published inclusive state (or the
+  // sequence start) enters with its aggregate, that one with its inclusive
+  // state (or state_init), each with multiplier exp(sum of the log decays of
+  // the aggregate entries before it, and of earlier rounds).  Without
+  // may_wait, a plan that would need an unpublished aggregate is left invalid.
+  const uint64_t t_start = sm100::globaltimer_ns();
+  float logm = 0.f;
+  auto plan_round = [&](int k_hi, bool may_wait) {
+    const int kk = k_hi - lane;
+    int fl = 0, s = 32;
+    float gdk = 0.f;
+    while (true) {
+      if (kk >= 0) {
+        const unsigned long long w = ld_acquire_gpu(&p.ws_flags[chunk0 + kk]);
+        fl = (int)(unsigned)(w & 0xffffffffu);
+        gdk = __uint_as_float((unsigned)(w >> 32));
+      } else {
+        fl = kFlagIncl;
+      }
+      const unsigned term = __ballot_sync(0xffffffffu, fl >= kFlagIncl);
+      const unsigned none = __ballot_sync(0xffffffffu, fl == 0);
+      s = term ? __ffs(term) - 1 : 32;
+      const unsigned need = s == 32 ? 0xffffffffu : ((1u << s) - 1u);
+      if ((none & need) == 0) break;
+      if (!may_wait) return;
+      int late = 0;
+      if (lane == 0) late = sm100::globaltimer_ns() - t_start > 200000000ull;
+      if (__shfl_sync(0xffffffffu, late, 0)) {
+        s = -1;
+        break;
+      }
+      __nanosleep(64);
+    }
+    if (s < 0 || (s < 32 && __shfl_sync(0xffffffffu, fl, s) == kFlagErr)) {
+      if (lane == 0) {
+        atomicOr(err, 1);
+        misc[3] = 0;
+        misc[4] = 1;
+        misc[5] = 1;
+      }
+      return;
+    }
+    const float gd = lane < s ? gdk : 0.f;
+    float pre = gd;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float y = __shfl_up_sync(0xffffffffu, pre, o);
+      if (lane >= o) pre += y;
+    }
+    if (lane <= s) {
+      const int kind = lane < s ? 0 : (kk >= 0 ? 1 : 2);  // aggregate, inclusive, state_init
+      sPi[lane] = 4 * (kk >= 0 ? kk : 0) + kind;
+      sPm[lane] = sm100::ex2_approx((logm + pre - gd) * kLog2e);
+    }
+    logm += __shfl_sync(0xffffffffu, pre, 31);
+    if (lane == 0) {
+      misc[3] = s < 32 ? s + 1 : 32;
+      misc[4] = s < 32;
+      misc[5] = 1;
+    }
+  };
+  // a first plan while the dS product runs, taken only if nothing in it is missing
+  if (warp == 1) plan_round(c - 1, false);
   if (!*verr && !sm100::mbar_wait(&bars[1], 1)) atomicOr(err, 1);
   sm100::tc_fence_after();
+  // Q again for Y2 (its tile held Kd lo, which the dS product has read)
+  bool reloading = false;
+  if (tid == 0 && !*verr) {
+    sm100::mbar_arrive_expect_tx(&bars[0], kTile);
+    sm100::tma_load_4d(sQ, &tq, p.R, t0, h, b, &bars[0]);
+    reloading = true;
+  }
   // aggregate: dS rows (M = 64: row j in lane 32*(j/16) + j%16) into shared
   // memory over the K tile as fp32 [J][64], 16-byte chunk c of row j at
   // position c ^ (j & 15) (the row-owning lanes then spread over the banks);
-  // from there to the workspace in coalesced slots below
+  // from there to the workspace in coalesced slots
   float* sA = reinterpret_cast<float*>(sK);
-  auto sa_at = [&](int j, int c) { return sA + j * D + ((c ^ (j & 15)) << 2); };
+  auto sa_at = [&](int j, int cq) { return sA + j * D + ((cq ^ (j & 15)) << 2); };
   {
     const int jr = 16 * warp + lane;
     const bool row_ok = lane < 16 && jr < J;
@@ -732,9 +812,8 @@ gla_tc_fused_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
   }
   sm100::tc_fence_before();
   __syncthreads();
-  // Y1 = P V into columns [64, 128) (dS has been read out).  The publication
-  // (a fence that waits for every store above, then the flag) is left to warp
-  // 3, off the paths of the MMA issue and of the look-back (warp 1).
+  const bool early_plan = misc[5] != 0;
+  // Y1 = P V into columns [64, 128) (dS has been read out)
   if (tid == 0 && !*verr) {
     sm100::tc_fence_after();
     const uint64_t vdesc = sm100::smem_desc(sV, 16, 1024, sm100::kSwizzle128);
@@ -748,102 +827,45 @@ gla_tc_fused_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
     for (int f = tid; f < 16 * J; f += kThreads) agg[f] = *reinterpret_cast<const float4*>(sa_at(f >> 4, f & 15));
   }
   __syncthreads();
+  // publication: a fence that waits for every store above, then the flag; left
+  // to warp 3, off the paths of the MMA issue and of the look-back
   if (tid == 96) {
     __threadfence();
     st_release_gpu(&p.ws_flags[ci], *verr ? kFlagErr : kFlagAgg, gc);
   }
 
-  // look-back for start_c.  Thread tid owns the float4 slots f = tid + 128 q of
-  // the [J][64] state (16 per row).  Warp 1 reads the flags of 32 chunks at a
-  // time (lane l: chunk k_hi - l) and writes a plan: every chunk before the
-  // first one with a published inclusive state (or the sequence start) enters
-  // with its aggregate, that one with its inclusive state; all threads then add
-  // their slots of the planned entries.
-  constexpr int NQ = 8;  // J <= 64: at most 1024 float4 slots
+  // look-back for start_c: thread tid owns the float4 slots f = tid + 128 q of
+  // the [J][64] state (16 per row); two planned entries per step, their loads
+  // in flight together
   float4 acc[NQ];
 #pragma unroll
   for (int q = 0; q < NQ; ++q) acc[q] = make_float4(0.f, 0.f, 0.f, 0.f);
   const int nslot = 16 * J;
-  const int64_t chunk0 = (int64_t)bh * p.nseg;
-  int k_hi = c - 1;
-  float logm = 0.f;  // natural-log multiplier of the next planned entry (warp 1)
-  const uint64_t t_start = sm100::globaltimer_ns();
-  while (true) {
-    if (warp == 1) {
-      const int kk = k_hi - lane;
-      int fl = 0, s = 32;
-      float gdk = 0.f;
-      while (true) {
-        if (kk >= 0) {
-          const unsigned long long w = ld_acquire_gpu(&p.ws_flags[chunk0 + kk]);
-          fl = (int)(unsigned)(w & 0xffffffffu);
-          gdk = __uint_as_float((unsigned)(w >> 32));
-        } else {
-          fl = kFlagIncl;
-        }
-        const unsigned term = __ballot_sync(0xffffffffu, fl >= kFlagIncl);
-        const unsigned none = __ballot_sync(0xffffffffu, fl == 0);
-        s = term ? __ffs(term) - 1 : 32;
-        const unsigned need = s == 32 ? 0xffffffffu : ((1u << s) - 1u);
-        if ((none & need) == 0) break;
-        int late = 0;
-        if (lane == 0) late = sm100::globaltimer_ns() - t_start > 200000000ull;
-        if (__shfl_sync(0xffffffffu, late, 0)) {
-          s = -1;
-          break;
-        }
-        __nanosleep(64);
-      }
-      if (s < 0 || (s < 32 && __shfl_sync(0xffffffffu, fl, s) == kFlagErr)) {
-        if (lane == 0) {
-          atomicOr(err, 1);
-          misc[3] = 0;
-          misc[4] = 1;
-        }
-      } else {
-        // multipliers: exp(logm + sum of the decays of the aggregate entries before)
-        const float gd = lane < s ? gdk : 0.f;
-        float pre = gd;
+  auto src_of = [&](int code) {
+    return reinterpret_cast<const float4*>(((code & 3) == 0 ? p.ws_agg : p.ws_incl) + (chunk0 + (code >> 2)) * J * D);
+  };
+  auto add_init = [&](float m) {
+    if (p.state_init == nullptr) return;
+    const float* s0 = p.state_init + b * p.ssi[0] + h * p.ssi[1];
 #pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-          const float y = __shfl_up_sync(0xffffffffu, pre, o);
-          if (lane >= o) pre += y;
-        }
-        const float lm = logm + pre - gd;
-        if (lane <= s && lane < 32) {
-          const int kind = lane < s ? 0 : (kk >= 0 ? 1 : 2);  // aggregate, inclusive, state_init
-          sPi[lane] = 4 * (kk >= 0 ? kk : 0) + kind;
-          sPm[lane] = sm100::ex2_approx(lm * kLog2e);
-        }
-        logm += __shfl_sync(0xffffffffu, pre, 31);
-        if (lane == 0) {
-          misc[3] = s < 32 ? s + 1 : 32;
-          misc[4] = s < 32;
-        }
+    for (int q = 0; q < NQ; ++q) {
+      const int f = tid + 128 * q;
+      if (f < nslot) {
+        const float* r = s0 + (f >> 4) * p.ssi[2] + (f & 15) * 4;
+        acc[q].x = fmaf(m, r[0], acc[q].x);
+        acc[q].y = fmaf(m, r[1], acc[q].y);
+        acc[q].z = fmaf(m, r[2], acc[q].z);
+        acc[q].w = fmaf(m, r[3], acc[q].w);
       }
     }
+  };
+  int k_hi = c - 1;
+  bool first = true;
+  while (true) {
+    if (!(first && early_plan) && warp == 1) plan_round(k_hi, true);
     __syncthreads();
     const int n = misc[3];
     const bool fin = misc[4] != 0;
-    // two planned entries per step, their loads in flight together
-    auto src_of = [&](int code) {
-      return reinterpret_cast<const float4*>(((code & 3) == 0 ? p.ws_agg : p.ws_incl) + (chunk0 + (code >> 2)) * J * D);
-    };
-    auto add_init = [&](float m) {
-      if (p.state_init == nullptr) return;
-      const float* s0 = p.state_init + b * p.ssi[0] + h * p.ssi[1];
-#pragma unroll
-      for (int q = 0; q < NQ; ++q) {
-        const int f = tid + 128 * q;
-        if (f < nslot) {
-          const float* r = s0 + (f >> 4) * p.ssi[2] + (f & 15) * 4;
-          acc[q].x = fmaf(m, r[0], acc[q].x);
-          acc[q].y = fmaf(m, r[1], acc[q].y);
-          acc[q].z = fmaf(m, r[2], acc[q].z);
-          acc[q].w = fmaf(m, r[3], acc[q].w);
-        }
-      }
-    };
     for (int e = 0; e < n; e += 2) {
       const int c0 = sPi[e];
       const int c1 = e + 1 < n ? sPi[e + 1] : 2;  // a missing second entry reads as "state_init" with m = 0
@@ -871,12 +893,16 @@ gla_tc_fused_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
     }
     if (fin) break;
     k_hi -= 32;
+    first = false;
     __syncthreads();  // warp 1 rewrites the plan next round
   }
 
-  // start_c -> X as the bf16 operand of Y2 (rows j, 128-byte swizzled, rows
-  // J .. 16*KS zero); inclusive_c = exp(G_C) start_c + dS_c -> workspace (and
-  // the final state for the last chunk)
+  // Y1 complete: V's tile and P's columns are free.  inclusive_c = exp(G_C)
+  // start_c + dS_c -> workspace (and the final state for the last chunk);
+  // start_c -> V's tile as the bf16 operand of Y2 (rows j, 128-byte swizzled,
+  // rows J .. 16*KS zero)
+  if (!*verr && !sm100::mbar_wait(&bars[1], 0)) atomicOr(err, 1);
+  sm100::tc_fence_after();
   const float egc = sm100::ex2_approx(gc * kLog2e);
   float* incl = p.ws_incl + ci * J * D;
   const bool last = c == p.nseg - 1 && p.state_out != nullptr;
@@ -886,7 +912,7 @@ gla_tc_fused_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
     const int j = f >> 4, d0 = (f & 15) * 4;
     if (j < 16 * KS) {
       const float4 v = f < nslot ? acc[q] : make_float4(0.f, 0.f, 0.f, 0.f);
-      *reinterpret_cast<uint2*>(sX + j * 128 + (((d0 >> 3) ^ (j & 7)) << 4) + (d0 & 7) * 2) =
+      *reinterpret_cast<uint2*>(sV + j * 128 + (((d0 >> 3) ^ (j & 7)) << 4) + (d0 & 7) * 2) =
           make_uint2(pack2(v.x, v.y, BF16), pack2(v.z, v.w, BF16));
     }
     if (f < nslot) {
@@ -904,40 +930,47 @@ gla_tc_fused_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
     }
   }
   fence_async_smem();
+  sm100::tc_fence_before();
   __syncthreads();
   if (tid == 96) {
     __threadfence();
     st_release_gpu(&p.ws_flags[ci], *verr ? kFlagErr : kFlagIncl, gc);
   }
-  // Y1 complete -> P's columns are free: Y2 = Q_I start_c into [0, 64)
-  if (!*verr && !sm100::mbar_wait(&bars[1], 0)) atomicOr(err, 1);
-  sm100::tc_fence_after();
-  if (tid == 0 && !*verr) {
-    const uint64_t qdesc = sm100::smem_desc(sQ, 16, 1024, sm100::kSwizzle128);
-    const uint64_t sdesc = sm100::smem_desc(sX, 16, 1024, sm100::kSwizzle128);
-    for (int ks = 0; ks < KS; ++ks)
-      sm100::mma_ss(tmem, qdesc + kstep(ks), sdesc + (uint64_t)(ks * 2048 >> 4), IDESC_Y, ks > 0);
-    sm100::mma_commit(&bars[2]);
+  // Y2 = Q_I start_c into [0, 64), once the reloaded Q has landed; on a
+  // barrier of its own (a thread still on its way to an earlier wait must not
+  // find bars[1] two phases ahead)
+  // (a reload in flight is always waited for, so the CTA never leaves with a
+  // copy into its shared memory outstanding)
+  if (tid == 0 && reloading) {
+    if (!sm100::mbar_wait(&bars[0], 1)) {
+      atomicOr(err, 1);
+    } else if (!*verr) {
+      sm100::tc_fence_after();
+      const uint64_t qdesc = sm100::smem_desc(sQ, 16, 1024, sm100::kSwizzle128);
+      const uint64_t sdesc = sm100::smem_desc(sV, 16, 1024, sm100::kSwizzle128);
+      for (int ks = 0; ks < KS; ++ks)
+        sm100::mma_ss(tmem, qdesc + kstep(ks), sdesc + (uint64_t)(ks * 2048 >> 4), IDESC_Y, ks > 0);
+      sm100::mma_commit(&bars[2]);
+    }
   }
-  // Y2 completes on a barrier of its own: a thread still on its way to the Y1
-  // wait (the publishing warp) must not find bars[1] two phases ahead
   if (!*verr && !sm100::mbar_wait(&bars[2], 0)) atomicOr(err, 1);
   sm100::tc_fence_after();
 
-  // epilogue as in C: y = Y1 + exp(G_i) Y2, fused (1 - mix) * gla_scale * RMSNorm(y)
+  // epilogue as in C: y = Y1 + exp(G_i) Y2, fused (1 - mix) * gla_scale * RMSNorm(y),
+  // 16 columns of TMEM at a time
   const uint32_t tY1 = tmem + 64, tY2 = tmem;
   const float eg = sm100::ex2_approx(G);
   float scale = 1.f;
   if (p.fuse) {
     float ss = 0.f;
 #pragma unroll
-    for (int cc = 0; cc < D; cc += 32) {
-      uint32_t a[32], bb[32];
-      sm100::tmem_ld32(tY1 + lane_off + cc, a);
-      sm100::tmem_ld32(tY2 + lane_off + cc, bb);
+    for (int cc = 0; cc < D; cc += 16) {
+      uint32_t a[16], bb[16];
+      sm100::tmem_ld16(tY1 + lane_off + cc, a);
+      sm100::tmem_ld16(tY2 + lane_off + cc, bb);
       sm100::tc_wait_ld();
 #pragma unroll
-      for (int u = 0; u < 32; ++u) {
+      for (int u = 0; u < 16; ++u) {
         const float y = fmaf(eg, __uint_as_float(bb[u]), __uint_as_float(a[u]));
         ss = fmaf(y, y, ss);
       }
@@ -948,18 +981,18 @@ gla_tc_fused_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
   T* yp = reinterpret_cast<T*>(p.y) + b * p.sy[0] + h * p.sy[1] + (int64_t)(store ? t : 0) * p.sy[2];
   const bool vec = p.sy[3] == 1 && (reinterpret_cast<uintptr_t>(yp) & 15u) == 0;
 #pragma unroll
-  for (int cc = 0; cc < D; cc += 32) {
-    uint32_t a[32], bb[32];
-    sm100::tmem_ld32(tY1 + lane_off + cc, a);
-    sm100::tmem_ld32(tY2 + lane_off + cc, bb);
+  for (int cc = 0; cc < D; cc += 16) {
+    uint32_t a[16], bb[16];
+    sm100::tmem_ld16(tY1 + lane_off + cc, a);  // warp-collective: every lane executes it
+    sm100::tmem_ld16(tY2 + lane_off + cc, bb);
     sm100::tc_wait_ld();
     if (store) {
-      float y[32];
+      float y[16];
 #pragma unroll
-      for (int u = 0; u < 32; ++u) y[u] = fmaf(eg, __uint_as_float(bb[u]), __uint_as_float(a[u])) * scale * sGS[cc + u];
+      for (int u = 0; u < 16; ++u) y[u] = fmaf(eg, __uint_as_float(bb[u]), __uint_as_float(a[u])) * scale * sGS[cc + u];
       if (vec) {
 #pragma unroll
-        for (int d = 0; d < 32; d += 8) {
+        for (int d = 0; d < 16; d += 8) {
           uint4 w;
           w.x = pack2(y[d], y[d + 1], BF16);
           w.y = pack2(y[d + 2], y[d + 3], BF16);
@@ -969,7 +1002,7 @@ gla_tc_fused_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constan
         }
       } else {
 #pragma unroll
-        for (int d = 0; d < 32; ++d) yp[(int64_t)(cc + d) * p.sy[3]] = from_f<T>(y[d]);
+        for (int d = 0; d < 16; ++d) yp[(int64_t)(cc + d) * p.sy[3]] = from_f<T>(y[d]);
       }
     }
   }
@@ -1034,7 +1067,7 @@ cudaError_t launch_t(const GlaParams& p, cudaStream_t st, bool* taken) {
       !make_map(&mv, p.v, bf16, D, p.T, p.H, p.B, p.sv))
     return cudaSuccess;
   if constexpr (D == 64) {
-    auto kF = gla_tc_fused_kernel<T>;
+    auto kF = p.J <= 48 ? gla_tc_fused_kernel<T, 6> : gla_tc_fused_kernel<T, 8>;
     cudaError_t e = cudaFuncSetAttribute(kF, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFusedSmem);
     if (e != cudaSuccess) return e;
     *taken = true;
