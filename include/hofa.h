@@ -147,11 +147,15 @@ typedef struct hofa_gla_args {
 } hofa_gla_args;
 
 /* Replaces chunk_gla_inlier_fwd (src/chunk_gla_inlier.py:153-237) and
- * chunk_gla_fwd_kernel (:5-150).  bf16/f16 inputs with D = 64, R % 8 == 0 and
- * no log_alpha run three chunk-parallel tcgen05 kernels (per-chunk state
- * contributions, a scan over chunks, per-chunk outputs) when the workspace
- * holds hofa_gla_workspace_size() bytes; other cases run a segment-parallel
- * CUDA-core kernel. */
+ * chunk_gla_fwd_kernel (:5-150).  bf16/f16 inputs with R % 8 == 0 run
+ * chunk-parallel tcgen05 kernels when the workspace holds
+ * hofa_gla_workspace_size() bytes: at D = 64 with a scalar decay one launch
+ * (the state carried between chunks by a look-back inside the launch; the
+ * call also clears the front of the workspace, so it needs no
+ * initialisation), otherwise three (per-chunk state contributions, a scan
+ * over chunks, per-chunk outputs), a per-channel decay (log_alpha) included.
+ * Other cases run a segment-parallel CUDA-core kernel.  Calls that share a
+ * workspace must not run concurrently. */
 int hofa_prefill_gla_fwd(const hofa_gla_args* args, void* stream);
 size_t hofa_gla_workspace_size(int32_t B, int32_t H, int32_t T, int32_t D, int32_t R,
                                int32_t chunk_size, int32_t num_segments);

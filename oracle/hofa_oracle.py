@@ -188,6 +188,59 @@ def chunk_gla_core(Q, K, V, log_gamma, r: int, chunk_size: int = 64,
     return Y, S
 
 
+def chunk_gla_reference_rounding(Q, K, V, log_gamma, r: int, chunk_size: int = 64, log_alpha=None,
+                                 mix_g=None, gla_scale=None, eps: float = 1e-5, state_init=None):
+    """``chunk_gla_fwd_kernel`` (src/chunk_gla_inlier.py:5-150) with its rounding
+    points: the same chunk loop as ``chunk_gla_core`` in float64, but every
+    operand the reference casts to the input dtype before a ``tl.dot`` is
+    rounded to it here -- with a per-channel decay (``HAS_ALPHA``, :90-107) the
+    factored queries and keys, the masked score matrix, the decayed queries of
+    the inter-chunk term and the carried state; with a scalar decay (:108-126)
+    the masked score matrix, the carried state and the decayed keys.  The
+    output is rounded to the input dtype at the end (:143-144).  Used by the
+    tests as the reference's own error against the float64 ``chunk_gla_core``
+    on the same inputs.  Returns (Y [B,H,T,D] float64, S_T [B,H,J,D]).
+    """
+    B, H, T, D = Q.shape
+    J = D - r
+    lowp = Q.dtype
+    f = lambda t: t.to(torch.float64)
+    rnd = lambda t: t.to(lowp).to(torch.float64)
+    q, kk, vv = f(Q[..., r:]), f(K[..., r:]), f(V)
+    lg = f(log_gamma).reshape(B, H, T)
+    alpha = torch.exp(f(log_alpha).reshape(-1, H, J))[:, :, None, :] if log_alpha is not None else None
+    S = torch.zeros(B, H, J, D, dtype=torch.float64) if state_init is None else f(state_init).clone()
+    Y = torch.empty(B, H, T, D, dtype=torch.float64)
+    for s0 in range(0, T, chunk_size):
+        s1 = min(T, s0 + chunk_size)
+        C = s1 - s0
+        qc, kc, vc = q[:, :, s0:s1], kk[:, :, s0:s1], vv[:, :, s0:s1]
+        G = torch.cumsum(lg[:, :, s0:s1], dim=2)                               # [B,H,C]
+        GL = G[:, :, -1:]
+        causal = torch.tril(torch.ones(C, C, dtype=torch.bool))
+        if alpha is not None:
+            qf = rnd(qc * torch.exp((G - GL)[..., None] * alpha))
+            kf = rnd(kc * torch.exp((GL - G)[..., None] * alpha))
+            attn = rnd(torch.where(causal, qf @ kf.transpose(-1, -2), torch.zeros((), dtype=torch.float64)))
+            y_intra = attn @ vc
+            y_inter = rnd(qc * torch.exp(G[..., None] * alpha)) @ rnd(S)
+            S = S * torch.exp(GL[..., None] * alpha).transpose(-1, -2) + kf.transpose(-1, -2) @ vc
+        else:
+            mask = torch.where(causal, torch.exp((G[..., :, None] - G[..., None, :]).clamp(max=0.0)),
+                               torch.zeros((), dtype=torch.float64))
+            attn = rnd((qc @ kc.transpose(-1, -2)) * mask)
+            y_intra = attn @ vc
+            y_inter = (qc @ rnd(S)) * torch.exp(G)[..., None]
+            kd = rnd(kc * torch.exp(GL - G)[..., None])
+            S = S * torch.exp(GL)[..., None] + kd.transpose(-1, -2) @ vc
+        Y[:, :, s0:s1] = y_intra + y_inter
+    if mix_g is not None and gla_scale is not None:
+        var = (Y * Y).mean(-1, keepdim=True)
+        Y = Y * torch.rsqrt(var + eps) * f(gla_scale).reshape(1, H, 1, D)
+        Y = Y * (1.0 - f(mix_g).reshape(B, H, T, 1))
+    return rnd(Y), S
+
+
 def outlier_attention_core(Q, K, V, r: int, sm_scale: float, mix_g, out=None,
                            q_offset: int = 0, dtype=torch.float64, block: int = 256):
     """Causal softmax attention over the first ``r`` channels of Q/K with

@@ -565,7 +565,7 @@ int hofa_prefill_gla_fwd(const hofa_gla_args* a, void* stream) {
     if (a->state_out.dtype != HOFA_DTYPE_F32) return fail(HOFA_ERR_INVALID_ARGUMENT, "state_out must be float32");
   }
   if (T == 0) return HOFA_OK;
-  // tensor-core path: chunk-parallel tcgen05 kernels (bf16/f16, head dim 64, scalar decay)
+  // tensor-core path: chunk-parallel tcgen05 kernels (bf16/f16, head dim 64 or 128, scalar or per-channel decay)
   {
     hofa::GlaParams tp;
     memset(&tp, 0, sizeof(tp));
@@ -576,6 +576,8 @@ int hofa_prefill_gla_fwd(const hofa_gla_args* a, void* stream) {
       tp = p;  // side-tensor strides filled above
       tp.q = a->q.data; tp.k = a->k.data; tp.v = a->v.data;
       tp.log_gamma = a->log_gamma.data;
+      tp.log_alpha = alpha ? a->log_alpha.data : nullptr;
+      tp.dt_la = alpha ? a->log_alpha.dtype : 0;
       tp.mix_g = p.fuse ? a->mix_g.data : nullptr;
       tp.gla_scale = p.fuse ? a->gla_scale.data : nullptr;
       tp.state_init = present(a->state_init) ? (const float*)a->state_init.data : nullptr;

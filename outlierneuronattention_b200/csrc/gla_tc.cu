@@ -1,7 +1,8 @@
 // Prefill GLA on the tensor cores (tcgen05 + TMEM + TMA), chunk-parallel.
 //
 // Replaces chunk_gla_fwd_kernel (src/chunk_gla_inlier.py:5-150) for bf16/f16
-// inputs with head dim 64 or 128 and a per-head scalar decay (no log_alpha).
+// inputs with head dim 64 or 128, with a per-head scalar decay or a per-channel
+// one (log_alpha: the ALPHA variants of A, B and C, described at C).
 // Operand tiles are [128 tokens x D channels] in 64-channel column blocks of
 // 128-byte swizzled rows (one TMA box each), so D = 128 uses two blocks.  The
 // reference runs one program per (b,h) that walks every chunk in sequence; here
@@ -27,9 +28,13 @@
 //        P   = A * exp(G_i - G_j) [j <= i]  -> bf16, written back into TMEM
 //        Y1  = P V                  tcgen05.mma, A = P from TMEM, V MN-major
 //        y   = Y1 + exp(G_i) Y2, then (1 - mix) * gla_scale * RMSNorm(y)
+//      with a per-channel decay (ALPHA) A is the reference's factored form over
+//      key sub-blocks of 64 / 32 / 16 tokens (decayed Q and K as hi + lo terms),
+//      P = A masked, Y2's operand Q exp(G_i a) and y = Y1 + Y2 (see the kernel);
+//      A and B decay key channel c / state row j by exp(... a_c) / exp(G_C a_j)
 //
-// All decay factors are exponentials of non-positive differences of cumulative
-// log decays (no overflow).  Rounding points: the masked score matrix and the
+// All decay factors of the scalar form are exponentials of non-positive
+// differences of cumulative log decays (no overflow).  Rounding points: the masked score matrix and the
 // carried state enter the output kernel's tensor-core products in the input
 // dtype, as in the reference kernel; the decayed keys of the state update
 // enter as a hi + lo pair of 16-bit terms (the reference rounds them once),
@@ -66,9 +71,11 @@ struct Geo {
   // A, Y1 and Y2 side by side (512 columns, one CTA per SM)
   static constexpr bool SHARE = D == 64;
   static constexpr uint32_t OUT_COLS = SHARE ? 128 : 512;
-  static constexpr size_t STATE_SMEM = 3 * OP + 1024 + 256;   // K (then Kd hi), V, Kd lo
+  static constexpr size_t STATE_SMEM = 3 * OP + 1024 + 256 + 4 * D;   // K (then Kd hi), V, Kd lo; alpha
   // D = 64: 80 KB keeps <= 2 CTAs (2 x 256 TMEM columns) per SM; D = 128: one CTA
-  static constexpr size_t OUT_SMEM = 4 * OP + 1024 + 4096;
+  static constexpr size_t OUT_SMEM = 4 * OP + 1024 + 4096 + 4 * D;
+  // per-channel decay: two more tiles for the lo terms of the decayed Q and K
+  static constexpr size_t OUT_SMEM_ALPHA = 6 * OP + 1024 + 4096 + 4 * D;
 };
 
 __device__ __forceinline__ uint32_t pack2(float a, float b, bool bf16) {
@@ -102,7 +109,7 @@ __device__ __forceinline__ void fence_async_smem() {
 // ---------------------------------------------------------------------------
 // A: per-chunk state contribution dS = (K * exp(G_C - G_t))^T V
 // ---------------------------------------------------------------------------
-template <typename T, int D>
+template <typename T, int D, bool ALPHA>
 __global__ void __launch_bounds__(kThreads)
 gla_tc_state_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constant__ CUtensorMap tv,
                     const GlaParams p) {
@@ -118,6 +125,7 @@ gla_tc_state_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
   float* sm_warp = reinterpret_cast<float*>(bars + 4);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm_warp + 4);
   int* err = reinterpret_cast<int*>(tmem_slot + 1);
+  float* sAl = reinterpret_cast<float*>(base + 3 * Gm::OP + 256);  // alpha_c = exp(log_alpha_c) per inlier channel
 
   const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -128,6 +136,10 @@ gla_tc_state_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
     sm100::mbar_init(&bars[1], 1);
     *err = 0;
     sm100::fence_mbar_init();
+  }
+  if constexpr (ALPHA) {
+    for (int cc = tid; cc < D; cc += kThreads)
+      sAl[cc] = cc < p.J ? __expf(ld_any(p.log_alpha, p.dt_la, b * p.sla[0] + h * p.sla[1] + cc * p.sla[2])) : 0.f;
   }
   if (warp == 0) {
     sm100::tmem_alloc(tmem_slot, D);
@@ -162,8 +174,14 @@ gla_tc_state_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
   // error into a state of magnitude 10 over 8192 tokens.  hi replaces the K
   // tile, lo has a tile of its own, and both products accumulate into the same
   // TMEM columns under one commit.
+  // With a per-channel decay (ALPHA) the factor is exp((G_C - G_t) alpha_c)
+  // (src/chunk_gla_inlier.py:90-107), still <= 1.  With the rotated chunk order
+  // the loop index q0 is the logical 16-byte chunk of the row (the 128-byte
+  // swizzle stores logical chunk L of row r at L ^ (r & 7)), so its channels
+  // are 64 nb + 8 q0 + [0, 8).
   {
-    const float w = sm100::ex2_approx((gc - G) * kLog2e);
+    const float dG = (gc - G) * kLog2e;
+    const float w = sm100::ex2_approx(dG);
     const int rot = tid & 7;  // chunk order q ^ (lane & 7): the warp's lanes spread over all banks
 #pragma unroll
     for (int nb = 0; nb < Gm::NB; ++nb) {
@@ -180,7 +198,13 @@ gla_tc_state_kernel(const __grid_constant__ CUtensorMap tk, const __grid_constan
           float a, bb;
           if (BF16) bf16x2_to_f(pu[e], a, bb);
           else f16x2_to_f(pu[e], a, bb);
-          const float xa = a * w, xb = bb * w;
+          float wa = w, wb = w;
+          if constexpr (ALPHA) {
+            const int ch = 64 * nb + 8 * q0 + 2 * e;
+            wa = sm100::ex2_approx(dG * sAl[ch]);
+            wb = sm100::ex2_approx(dG * sAl[ch + 1]);
+          }
+          const float xa = a * wa, xb = bb * wb;
           pu[e] = pack2(xa, xb, BF16);
           float ha, hb;
           if (BF16) bf16x2_to_f(pu[e], ha, hb);
@@ -244,6 +268,8 @@ __global__ void __launch_bounds__(256) gla_tc_scan_kernel(const GlaParams p) {
   const int j = e / p.D, d = e % p.D;
   const int64_t bh = (int64_t)b * p.H + h;
   float S = p.state_init ? p.state_init[b * p.ssi[0] + h * p.ssi[1] + j * p.ssi[2] + d] : 0.f;
+  // row j of the state decays by exp(G_C alpha_j) per chunk (alpha = 1 without log_alpha)
+  const float a2 = kLog2e * (p.log_alpha ? __expf(ld_any(p.log_alpha, p.dt_la, b * p.sla[0] + h * p.sla[1] + j * p.sla[2])) : 1.f);
   float* ws = p.ws_state + bh * p.nseg * p.J * p.D + e;
   const float* gc = p.ws_decay + bh * p.nseg;
   const int64_t cs = (int64_t)p.J * p.D;
@@ -269,13 +295,13 @@ __global__ void __launch_bounds__(256) gla_tc_scan_kernel(const GlaParams p) {
 #pragma unroll
     for (int u = 0; u < kU; ++u) {
       ws[(c + u) * cs] = S;
-      S = fmaf(sm100::ex2_approx(g[u] * kLog2e), S, dS[u]);
+      S = fmaf(sm100::ex2_approx(g[u] * a2), S, dS[u]);
     }
   }
   for (; c < p.nseg; ++c) {
     const float dS = ws[c * cs];
     ws[c * cs] = S;
-    S = fmaf(sm100::ex2_approx(gc[c] * kLog2e), S, dS);
+    S = fmaf(sm100::ex2_approx(gc[c] * a2), S, dS);
   }
   if (p.state_out) p.state_out[b * p.sso[0] + h * p.sso[1] + j * p.sso[2] + d * p.sso[3]] = S;
 }
@@ -283,7 +309,7 @@ __global__ void __launch_bounds__(256) gla_tc_scan_kernel(const GlaParams p) {
 // ---------------------------------------------------------------------------
 // C: per-chunk output
 // ---------------------------------------------------------------------------
-template <typename T, int D>
+template <typename T, int D, bool ALPHA>
 __global__ void __launch_bounds__(kThreads, D == 64 ? 3 : 1)
 gla_tc_out_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                   const __grid_constant__ CUtensorMap tv, const GlaParams p) {
@@ -297,12 +323,15 @@ gla_tc_out_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
   unsigned char* sK = base + Gm::OP;
   unsigned char* sV = base + 2 * Gm::OP;
   unsigned char* sS = base + 3 * Gm::OP;              // start state, [128 rows j][D] bf16 MN-major blocks
-  float* sG = reinterpret_cast<float*>(sS + Gm::OP);  // cumulative log2 decay per token
+  unsigned char* sQl = base + 4 * Gm::OP;             // ALPHA: lo terms of the decayed Q
+  unsigned char* sKl = base + 5 * Gm::OP;             //        and of the decayed K
+  float* sG = reinterpret_cast<float*>(base + (ALPHA ? 6 : 4) * Gm::OP);  // cumulative log2 decay per token
   float* sGS = sG + kC;                                // gla_scale[h, 0:D]
   uint64_t* bars = reinterpret_cast<uint64_t*>(sGS + D);
   float* sm_warp = reinterpret_cast<float*>(bars + 4);
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(sm_warp + 4);
   int* err = reinterpret_cast<int*>(tmem_slot + 1);
+  float* sAl = reinterpret_cast<float*>(err + 1);  // alpha_c = exp(log_alpha_c) (ALPHA)
 
   const int c = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int tid = threadIdx.x, warp = tid >> 5;
@@ -312,8 +341,13 @@ gla_tc_out_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
   if (tid == 0) {
     sm100::mbar_init(&bars[0], 1);
     sm100::mbar_init(&bars[1], 1);
+    sm100::mbar_init(&bars[2], 1);
     *err = 0;
     sm100::fence_mbar_init();
+  }
+  if constexpr (ALPHA) {
+    for (int cc = tid; cc < D; cc += kThreads)
+      sAl[cc] = cc < J ? __expf(ld_any(p.log_alpha, p.dt_la, b * p.sla[0] + h * p.sla[1] + cc * p.sla[2])) : 0.f;
   }
   if (warp == 0) {
     sm100::tmem_alloc(tmem_slot, Gm::OUT_COLS);
@@ -370,29 +404,206 @@ gla_tc_out_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
   const float G = block_scan128(g, sm_warp, tid) * kLog2e;   // log2 units from here on
   sG[tid] = G;
   if (tid < D) sGS[tid] = gsv;
+  if constexpr (ALPHA) {
+    if (warp == 0) {  // largest alpha (sAl is complete: the scan above holds a barrier)
+      float m = 0.f;
+      for (int cc = tid; cc < D; cc += 32) m = fmaxf(m, sAl[cc]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+      if (tid == 0) sAl[D] = m;
+    }
+  }
   fence_async_smem();
   volatile int* verr = err;
   if (!sm100::mbar_wait(&bars[0], 0)) atomicOr(err, 1);
   sm100::tc_fence_before();
   __syncthreads();
-  if (tid == 0 && !*verr) {
+  // K-major steps of 16 channels: 4 per 128-byte block (32 B each), blocks kTile apart
+  auto kstep = [](int ks) { return (uint64_t)(((ks >> 2) * kTile + (ks & 3) * 32) >> 4); };
+  uint32_t ph1 = 0;  // completions of bars[1] waited for so far (its next parity)
+  if constexpr (ALPHA) {
+    // Per-channel decay: the reference's factored form (src/chunk_gla_inlier.py:
+    // 90-107) over key sub-blocks of S tokens: for the keys of sub-block b (last
+    // token e_b)
+    //   A[:, b] = (Q exp((G_i - G_e_b) a)) (K exp((G_e_b - G_j) a))^T,  rows i before b zero.
+    // Key factors are <= 1; query factors exceed 1 only within the key's own
+    // sub-block, so S bounds the exponents: each CTA takes the largest S of 64
+    // (the reference's chunk), 32 and 16 whose sub-blocks keep
+    // (G_first - G_last) max(a) within the type's bound (log2 units), and runs kC / S
+    // products of N = S.  Y2's operand is Q exp(G_i a) (<= 1).  Thread i keeps
+    // its Q row in registers and rewrites Q's tile for each product; K is
+    // decayed in place.  With the rotated chunk order index q0 is the logical
+    // 16-byte chunk of the row (channels 64 nb + 8 q0 + [0, 8)).
+    // A chunk whose 16-token sub-blocks still exceed that range (a decay of
+    // more than about 2^-6 per token over 16 tokens) forms A exactly on the CUDA
+    // cores instead (every A_ij = sum_c Q_ic K_jc exp((G_i - G_j) a_c), j <= i),
+    // so the output stays finite where every factored form overflows.
+    // The range bound is 2^100 for bf16 (range 2^+-126) and 2^10 for f16
+    // (largest value 65504, smallest normal 2^-14).
+    constexpr float kRange = BF16 ? 100.f : 10.f;
+    const int i = tid, rot = tid & 7;
+    const float Gi = sG[i], amax = sAl[D];
+    int S = 0;
+    for (int cand = 64; cand >= 16; cand >>= 1) {
+      bool ok = true;
+      for (int sb = 0; sb < kC / cand; ++sb) ok = ok && (sG[sb * cand] - sG[sb * cand + cand - 1]) * amax <= kRange;
+      if (ok) {
+        S = cand;
+        break;
+      }
+    }
+    uint4 qr[8 * Gm::NB];
+#pragma unroll
+    for (int nb = 0; nb < Gm::NB; ++nb)
+#pragma unroll
+      for (int q0 = 0; q0 < 8; ++q0) qr[nb * 8 + q0] = reinterpret_cast<const uint4*>(sQ + nb * kTile + i * 128)[q0 ^ rot];
+    // x * exp2(dg a_c) as hi + lo 16-bit terms (hi = the rounded value, lo =
+    // the rounded remainder), so that the products of the decayed operands
+    // keep about 16 significant bits (three MMAs: hi*hi + hi*lo + lo*hi)
+    // instead of the 8 of the reference's single rounding
+    auto scaled = [&](uint4 u, int ch0, float dg, uint4& lo) {
+      uint32_t pu[4] = {u.x, u.y, u.z, u.w}, pl[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        float a, bb, ha, hb;
+        if (BF16) bf16x2_to_f(pu[e], a, bb);
+        else f16x2_to_f(pu[e], a, bb);
+        a *= sm100::ex2_approx(dg * sAl[ch0 + 2 * e]);
+        bb *= sm100::ex2_approx(dg * sAl[ch0 + 2 * e + 1]);
+        pu[e] = pack2(a, bb, BF16);
+        if (BF16) bf16x2_to_f(pu[e], ha, hb);
+        else f16x2_to_f(pu[e], ha, hb);
+        pl[e] = pack2(a - ha, bb - hb, BF16);
+      }
+      lo = make_uint4(pl[0], pl[1], pl[2], pl[3]);
+      return make_uint4(pu[0], pu[1], pu[2], pu[3]);
+    };
+    auto write_q = [&](float dg, bool zero) {
+#pragma unroll
+      for (int nb = 0; nb < Gm::NB; ++nb)
+#pragma unroll
+        for (int q0 = 0; q0 < 8; ++q0) {
+          uint4 hi = make_uint4(0u, 0u, 0u, 0u), lo = hi;
+          if (!zero) hi = scaled(qr[nb * 8 + q0], 64 * nb + 8 * q0, dg, lo);
+          reinterpret_cast<uint4*>(sQ + nb * kTile + i * 128)[q0 ^ rot] = hi;
+          reinterpret_cast<uint4*>(sQl + nb * kTile + i * 128)[q0 ^ rot] = lo;
+        }
+    };
+    if (S == 0) {
+      // exact A on the CUDA cores from the unscaled Q row (registers) and K rows
+      // (shared memory, logical chunk L of row j at L ^ (j & 7)), 32 columns at a time
+#pragma unroll 1
+      for (int cc = 0; cc < kC; cc += 32) {
+        uint32_t out[32];
+#pragma unroll 1
+        for (int u = 0; u < 32; ++u) {
+          const int j = cc + u;
+          float acc = 0.f;
+          if (j <= i) {
+            const float dg = Gi - sG[j];
+#pragma unroll
+            for (int nb = 0; nb < Gm::NB; ++nb)
+#pragma unroll
+              for (int q0 = 0; q0 < 8; ++q0) {
+                if (64 * nb + 8 * q0 >= J) continue;
+                const uint4 kv = reinterpret_cast<const uint4*>(sK + nb * kTile + j * 128)[q0 ^ (j & 7)];
+                const uint4 qv = qr[nb * 8 + q0];
+                const uint32_t kk4[4] = {kv.x, kv.y, kv.z, kv.w}, qq4[4] = {qv.x, qv.y, qv.z, qv.w};
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  float qa, qb, ka, kb;
+                  if (BF16) {
+                    bf16x2_to_f(qq4[e], qa, qb);
+                    bf16x2_to_f(kk4[e], ka, kb);
+                  } else {
+                    f16x2_to_f(qq4[e], qa, qb);
+                    f16x2_to_f(kk4[e], ka, kb);
+                  }
+                  const int ch = 64 * nb + 8 * q0 + 2 * e;
+                  acc = fmaf(qa * ka, sm100::ex2_approx(dg * sAl[ch]), acc);
+                  acc = fmaf(qb * kb, sm100::ex2_approx(dg * sAl[ch + 1]), acc);
+                }
+              }
+          }
+          out[u] = __float_as_uint(acc);
+        }
+        sm100::tmem_st32(tA + lane_off + cc, out);
+      }
+      sm100::tc_wait_st();
+    } else {
+      const float dk = sG[(i / S) * S + S - 1] - Gi;
+#pragma unroll
+      for (int nb = 0; nb < Gm::NB; ++nb)
+#pragma unroll
+        for (int q0 = 0; q0 < 8; ++q0) {
+          uint4* kr = reinterpret_cast<uint4*>(sK + nb * kTile + i * 128);
+          uint4 lo;
+          kr[q0 ^ rot] = scaled(kr[q0 ^ rot], 64 * nb + 8 * q0, dk, lo);
+          reinterpret_cast<uint4*>(sKl + nb * kTile + i * 128)[q0 ^ rot] = lo;
+        }
+    }
+    const uint32_t idesc_s = sm100::idesc_f16(BF16, false, false, 128, S > 0 ? S : 16);
+    for (int sb = 0; S > 0 && sb < kC / S; ++sb) {
+      write_q(Gi - sG[sb * S + S - 1], i < sb * S);
+      fence_async_smem();
+      sm100::tc_fence_before();
+      __syncthreads();
+      if (tid == 0 && !*verr) {
+        sm100::tc_fence_after();
+        const uint64_t qdesc = sm100::smem_desc(sQ, 16, 1024, sm100::kSwizzle128);
+        const uint64_t qldesc = sm100::smem_desc(sQl, 16, 1024, sm100::kSwizzle128);
+        const uint64_t kdesc = sm100::smem_desc(sK + sb * S * 128, 16, 1024, sm100::kSwizzle128);
+        const uint64_t kldesc = sm100::smem_desc(sKl + sb * S * 128, 16, 1024, sm100::kSwizzle128);
+        for (int ks = 0; ks < KS; ++ks)
+          sm100::mma_ss(tA + sb * S, qdesc + kstep(ks), kdesc + kstep(ks), idesc_s, ks > 0);
+        for (int ks = 0; ks < KS; ++ks) sm100::mma_ss(tA + sb * S, qdesc + kstep(ks), kldesc + kstep(ks), idesc_s, true);
+        for (int ks = 0; ks < KS; ++ks) sm100::mma_ss(tA + sb * S, qldesc + kstep(ks), kdesc + kstep(ks), idesc_s, true);
+        sm100::mma_commit(&bars[2]);
+      }
+      if (!*verr && !sm100::mbar_wait(&bars[2], sb & 1)) atomicOr(err, 1);
+      sm100::tc_fence_after();
+    }
+    write_q(Gi, false);
+    fence_async_smem();
+    if (!Gm::SHARE) {
+      sm100::tc_fence_before();
+      __syncthreads();
+      if (tid == 0 && !*verr) {
+        sm100::tc_fence_after();
+        const uint64_t qdesc = sm100::smem_desc(sQ, 16, 1024, sm100::kSwizzle128);
+        const uint64_t qldesc = sm100::smem_desc(sQl, 16, 1024, sm100::kSwizzle128);
+        const uint64_t sdesc = sm100::smem_desc(sS, Gm::LBO, 1024, sm100::kSwizzle128);
+        for (int ks = 0; ks < KS; ++ks)
+          sm100::mma_ss(tY2, qdesc + kstep(ks), sdesc + (uint64_t)(ks * 2048 >> 4), IDESC_Y, ks > 0);
+        for (int ks = 0; ks < KS; ++ks)
+          sm100::mma_ss(tY2, qldesc + kstep(ks), sdesc + (uint64_t)(ks * 2048 >> 4), IDESC_Y, true);
+        sm100::mma_commit(&bars[1]);
+      }
+      if (!*verr && !sm100::mbar_wait(&bars[1], ph1 & 1)) atomicOr(err, 1);
+      ++ph1;
+      sm100::tc_fence_after();
+    }
+  } else {
+    if (tid == 0 && !*verr) {
+      sm100::tc_fence_after();
+      const uint64_t qdesc = sm100::smem_desc(sQ, 16, 1024, sm100::kSwizzle128);
+      const uint64_t kdesc = sm100::smem_desc(sK, 16, 1024, sm100::kSwizzle128);
+      const uint64_t sdesc = sm100::smem_desc(sS, Gm::LBO, 1024, sm100::kSwizzle128);
+      for (int ks = 0; ks < KS; ++ks) sm100::mma_ss(tA, qdesc + kstep(ks), kdesc + kstep(ks), IDESC_A, ks > 0);
+      if (!Gm::SHARE)
+        for (int ks = 0; ks < KS; ++ks)
+          sm100::mma_ss(tY2, qdesc + kstep(ks), sdesc + (uint64_t)(ks * 2048 >> 4), IDESC_Y, ks > 0);
+      sm100::mma_commit(&bars[1]);
+    }
+    if (!*verr && !sm100::mbar_wait(&bars[1], ph1 & 1)) atomicOr(err, 1);
+    ++ph1;
     sm100::tc_fence_after();
-    const uint64_t qdesc = sm100::smem_desc(sQ, 16, 1024, sm100::kSwizzle128);
-    const uint64_t kdesc = sm100::smem_desc(sK, 16, 1024, sm100::kSwizzle128);
-    const uint64_t sdesc = sm100::smem_desc(sS, Gm::LBO, 1024, sm100::kSwizzle128);
-    // K-major steps of 16 channels: 4 per 128-byte block (32 B each), blocks kTile apart
-    auto kstep = [](int ks) { return (uint64_t)(((ks >> 2) * kTile + (ks & 3) * 32) >> 4); };
-    for (int ks = 0; ks < KS; ++ks) sm100::mma_ss(tA, qdesc + kstep(ks), kdesc + kstep(ks), IDESC_A, ks > 0);
-    if (!Gm::SHARE)
-      for (int ks = 0; ks < KS; ++ks)
-        sm100::mma_ss(tY2, qdesc + kstep(ks), sdesc + (uint64_t)(ks * 2048 >> 4), IDESC_Y, ks > 0);
-    sm100::mma_commit(&bars[1]);
   }
-  if (!*verr && !sm100::mbar_wait(&bars[1], 0)) atomicOr(err, 1);
-  sm100::tc_fence_after();
 
   // P = A * exp(G_i - G_j) for j <= i, as 16-bit pairs over columns [0, 64)
+  // (with ALPHA the decay is already inside A: P = A for j <= i)
   const int i = tid;
+  auto dec = [&](int j) { return ALPHA ? 1.f : sm100::ex2_approx(G - sG[j]); };
 #pragma unroll
   for (int cc = 0; cc < kC; cc += 64) {
     uint32_t r0[32], r1[32], pk[32];
@@ -402,10 +613,10 @@ gla_tc_out_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
 #pragma unroll
     for (int u = 0; u < 16; ++u) {
       const int j0 = cc + 2 * u, j1 = cc + 32 + 2 * u;
-      const float a0 = j0 <= i ? __uint_as_float(r0[2 * u]) * sm100::ex2_approx(G - sG[j0]) : 0.f;
-      const float a1 = j0 + 1 <= i ? __uint_as_float(r0[2 * u + 1]) * sm100::ex2_approx(G - sG[j0 + 1]) : 0.f;
-      const float a2 = j1 <= i ? __uint_as_float(r1[2 * u]) * sm100::ex2_approx(G - sG[j1]) : 0.f;
-      const float a3 = j1 + 1 <= i ? __uint_as_float(r1[2 * u + 1]) * sm100::ex2_approx(G - sG[j1 + 1]) : 0.f;
+      const float a0 = j0 <= i ? __uint_as_float(r0[2 * u]) * dec(j0) : 0.f;
+      const float a1 = j0 + 1 <= i ? __uint_as_float(r0[2 * u + 1]) * dec(j0 + 1) : 0.f;
+      const float a2 = j1 <= i ? __uint_as_float(r1[2 * u]) * dec(j1) : 0.f;
+      const float a3 = j1 + 1 <= i ? __uint_as_float(r1[2 * u + 1]) * dec(j1 + 1) : 0.f;
       pk[u] = pack2(a0, a1, BF16);
       pk[16 + u] = pack2(a2, a3, BF16);
     }
@@ -422,12 +633,17 @@ gla_tc_out_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
       sm100::tc_fence_after();
       const uint64_t qdesc = sm100::smem_desc(sQ, 16, 1024, sm100::kSwizzle128);
       const uint64_t sdesc = sm100::smem_desc(sS, Gm::LBO, 1024, sm100::kSwizzle128);
-      auto kstep = [](int ks) { return (uint64_t)(((ks >> 2) * kTile + (ks & 3) * 32) >> 4); };
       for (int ks = 0; ks < KS; ++ks)
         sm100::mma_ss(tY2, qdesc + kstep(ks), sdesc + (uint64_t)(ks * 2048 >> 4), IDESC_Y, ks > 0);
+      if constexpr (ALPHA) {  // lo term of Q exp(G_i a)
+        const uint64_t qldesc = sm100::smem_desc(sQl, 16, 1024, sm100::kSwizzle128);
+        for (int ks = 0; ks < KS; ++ks)
+          sm100::mma_ss(tY2, qldesc + kstep(ks), sdesc + (uint64_t)(ks * 2048 >> 4), IDESC_Y, true);
+      }
       sm100::mma_commit(&bars[1]);
     }
-    if (!*verr && !sm100::mbar_wait(&bars[1], 1)) atomicOr(err, 1);
+    if (!*verr && !sm100::mbar_wait(&bars[1], ph1 & 1)) atomicOr(err, 1);
+    ++ph1;
     sm100::tc_fence_after();
 #pragma unroll
     for (int cc = 0; cc < D; cc += 32) {
@@ -448,12 +664,12 @@ gla_tc_out_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant_
       sm100::mma_ts(tY1, tA + kk * 8, vdesc + (uint64_t)(kk * 2048 >> 4), IDESC_Y, kk > 0);
     sm100::mma_commit(&bars[1]);
   }
-  if (!*verr && !sm100::mbar_wait(&bars[1], Gm::SHARE ? 0 : 1)) atomicOr(err, 1);
+  if (!*verr && !sm100::mbar_wait(&bars[1], ph1 & 1)) atomicOr(err, 1);
   sm100::tc_fence_after();
 
   // epilogue: y = Y1 + exp(G_i) Y2, fused (1 - mix) * gla_scale * RMSNorm(y); two passes over
   // 32-column chunks of TMEM (sum of squares, then the scaled store)
-  const float eg = sm100::ex2_approx(G);
+  const float eg = ALPHA ? 1.f : sm100::ex2_approx(G);  // ALPHA: the decay is inside Y2's operand
   float scale = 1.f;
   if (p.fuse) {
     float ss = 0.f;
@@ -1028,6 +1244,10 @@ FusedLayout fused_layout(int64_t nch, int64_t J) {
   return L;
 }
 
+// True when launch_gla_tc runs the single-launch form for `p` (the per-channel
+// decay runs the three launches at every head dim).
+bool gla_tc_single_launch(const GlaParams& p) { return p.D == 64 && p.log_alpha == nullptr; }
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static bool tried = false;
@@ -1066,7 +1286,7 @@ cudaError_t launch_t(const GlaParams& p, cudaStream_t st, bool* taken) {
   if (!make_map(&mq, p.q, bf16, D, p.T, p.H, p.B, p.sq) || !make_map(&mk, p.k, bf16, D, p.T, p.H, p.B, p.sk) ||
       !make_map(&mv, p.v, bf16, D, p.T, p.H, p.B, p.sv))
     return cudaSuccess;
-  if constexpr (D == 64) {
+  if (gla_tc_single_launch(p)) {
     auto kF = p.J <= 48 ? gla_tc_fused_kernel<T, 6> : gla_tc_fused_kernel<T, 8>;
     cudaError_t e = cudaFuncSetAttribute(kF, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kFusedSmem);
     if (e != cudaSuccess) return e;
@@ -1078,11 +1298,13 @@ cudaError_t launch_t(const GlaParams& p, cudaStream_t st, bool* taken) {
     kF<<<(unsigned)nch, kThreads, kFusedSmem, st>>>(mq, mk, mv, p);
     return cudaGetLastError();
   }
-  auto kA = gla_tc_state_kernel<T, D>;
-  auto kC_ = gla_tc_out_kernel<T, D>;
+  const bool alpha = p.log_alpha != nullptr;
+  auto kA = alpha ? gla_tc_state_kernel<T, D, true> : gla_tc_state_kernel<T, D, false>;
+  auto kC_ = alpha ? gla_tc_out_kernel<T, D, true> : gla_tc_out_kernel<T, D, false>;
   cudaError_t e = cudaFuncSetAttribute(kA, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Gm::STATE_SMEM);
   if (e != cudaSuccess) return e;
-  e = cudaFuncSetAttribute(kC_, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)Gm::OUT_SMEM);
+  const size_t out_smem = alpha ? Gm::OUT_SMEM_ALPHA : Gm::OUT_SMEM;
+  e = cudaFuncSetAttribute(kC_, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)out_smem);
   if (e != cudaSuccess) return e;
   *taken = true;
   const dim3 grid(p.nseg, p.H, p.B);
@@ -1090,7 +1312,7 @@ cudaError_t launch_t(const GlaParams& p, cudaStream_t st, bool* taken) {
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   gla_tc_scan_kernel<<<dim3((p.J * D + 255) / 256, p.H, p.B), 256, 0, st>>>(p);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
-  kC_<<<grid, kThreads, Gm::OUT_SMEM, st>>>(mq, mk, mv, p);
+  kC_<<<grid, kThreads, out_smem, st>>>(mq, mk, mv, p);
   return cudaGetLastError();
 }
 
@@ -1104,10 +1326,12 @@ size_t gla_tc_workspace_bytes(int64_t B, int64_t H, int64_t T, int64_t J, int64_
   return (size_t)(B * H * nc * (J * D + 1)) * sizeof(float) + 256;
 }
 
-// Points the workspace fields of `p` (B, H, J, D and nseg set) into `ws`.
+// Points the workspace fields of `p` (B, H, J, D, nseg and log_alpha set) into
+// `ws`: the single-launch layout or the three-launch one, as the launch will
+// use.  (gla_tc_workspace_bytes covers both at head dim 64.)
 void gla_tc_bind_workspace(GlaParams& p, void* ws) {
   unsigned char* base = reinterpret_cast<unsigned char*>(ws);
-  if (p.D == 64) {
+  if (gla_tc_single_launch(p)) {
     const FusedLayout L = fused_layout((int64_t)p.B * p.H * p.nseg, p.J);
     p.ws_ticket = reinterpret_cast<unsigned*>(base);
     p.ws_flags = reinterpret_cast<unsigned long long*>(base + L.flags);
@@ -1125,7 +1349,7 @@ bool gla_tc_eligible(const GlaParams& p, int dtype) {
   const char* off = getenv("HOFA_GLA_NO_TC");
   if (off != nullptr && off[0] != '\0' && off[0] != '0') return false;
   return (dtype == HOFA_DTYPE_BF16 || dtype == HOFA_DTYPE_F16) && (p.D == 64 || p.D == 128) && p.R % 8 == 0 &&
-         p.R < p.D && p.log_alpha == nullptr;
+         p.R < p.D;
 }
 
 // p.nseg must hold the chunk count ceil(T / 128), p.ws_state / p.ws_decay the

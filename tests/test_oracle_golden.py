@@ -11,7 +11,7 @@ import pytest
 import torch
 
 from conftest import GOLDEN_CASES, load_golden
-from oracle.hofa_oracle import (LayerShape, OracleLayer, chunk_gla_core,
+from oracle.hofa_oracle import (LayerShape, OracleLayer, chunk_gla_core, chunk_gla_reference_rounding,
                                 outlier_attention_core, decode_core)
 
 TOL = 2e-6  # fixtures are stored in fp32
@@ -87,6 +87,28 @@ def test_chunk_forms_agree_with_alpha_and_ragged_chunks():
         for u, w in ((a, b), (a, c)):
             torch.testing.assert_close(u[0], w[0], atol=1e-10, rtol=1e-9)
             torch.testing.assert_close(u[1], w[1], atol=1e-10, rtol=1e-9)
+
+
+def test_reference_rounding_form_is_the_chunk_form_in_float64():
+    """The restatement of the reference kernel's rounding points reduces to the
+    float64 chunk form when the inputs are float64 (every rounding is then the
+    identity), with and without a per-channel decay, and on bf16 inputs stays
+    within bf16 rounding of it."""
+    gen = torch.Generator().manual_seed(4)
+    B, H, T, D, r = 1, 2, 200, 64, 16
+    Q, K, V = (torch.randn(B, H, T, D, generator=gen, dtype=torch.float64) * 0.3 for _ in range(3))
+    lg = torch.nn.functional.logsigmoid(torch.randn(B, H, T, generator=gen, dtype=torch.float64) + 3.0)
+    la = torch.randn(1, H, 1, D - r, generator=gen, dtype=torch.float64) * 0.5
+    mix = torch.rand(B, H, T, generator=gen, dtype=torch.float64)
+    gs = torch.randn(1, H, 1, D, generator=gen, dtype=torch.float64)
+    for alpha in (None, la):
+        a = chunk_gla_core(Q, K, V, lg, r, 64, alpha, mix, gs)
+        b = chunk_gla_reference_rounding(Q, K, V, lg, r, 64, alpha, mix, gs)
+        torch.testing.assert_close(a[0], b[0], atol=1e-12, rtol=1e-10)
+        torch.testing.assert_close(a[1], b[1], atol=1e-12, rtol=1e-10)
+        c = chunk_gla_reference_rounding(Q.bfloat16(), K.bfloat16(), V.bfloat16(), lg, r, 64, alpha, mix, gs)
+        d = chunk_gla_core(Q.bfloat16(), K.bfloat16(), V.bfloat16(), lg, r, 64, alpha, mix, gs)
+        assert 0 < (c[0] - d[0]).abs().max().item() < 5e-2
 
 
 def test_outlier_attention_q_offset_equals_suffix_of_full():

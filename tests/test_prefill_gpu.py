@@ -278,6 +278,46 @@ def test_gla_tensor_core_path(monkeypatch, dtype, B, H, T, r, fuse, init, D):
 
 
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("B,H,T,r,D,decay,fuse", [(1, 2, 300, 16, 64, "weak", True), (2, 2, 257, 32, 64, "mixed", True),
+                                                  (1, 2, 1000, 16, 64, "strong", True), (1, 1, 200, 8, 64, "mixed", False),
+                                                  (2, 1, 300, 32, 128, "weak", True), (1, 2, 640, 16, 128, "mixed", True),
+                                                  (1, 1, 500, 64, 128, "strong", False)])
+def test_gla_tensor_core_per_channel_decay(monkeypatch, dtype, B, H, T, r, D, decay, fuse):
+    """learnable_alpha on the tensor cores (the reference's factored decay,
+    src/chunk_gla_inlier.py:90-107, over key sub-blocks of 64, 32 or 16 tokens
+    chosen per chunk so that the factors stay in range, exact CUDA-core scores
+    beyond that; the decayed operands as hi + lo 16-bit terms) and the CUDA-core
+    kernel agree with the float64 oracle, output and final state, with a seeded
+    initial state; every output is finite (the reference's own form, with its
+    single rounding at 64-token chunks, overflows to NaN on the mixed and strong
+    inputs: ``chunk_gla_reference_rounding``); no bounded wait ran out."""
+    from outlierneuronattention_b200.chunk_gla_inlier import gla_forward
+    q, k, v, lg, mix, gs = rand_qkv(B, H, T, D, dtype, seed=T + r + D, scale=0.3)
+    g = torch.Generator().manual_seed(T * 7 + D)
+    mu = {"weak": 4.0, "mixed": 1.0, "strong": -1.0}[decay]
+    lg = F.logsigmoid(torch.randn(B, H, T, generator=g) * (1.0 if decay != "mixed" else 2.0) + mu)
+    la = torch.randn(1, H, 1, D - r, generator=g) * 0.5
+    s0 = torch.randn(B, H, D - r, D, generator=g) * 0.3
+    kw = dict(log_alpha=la, mix_g=mix if fuse else None, gla_scale=gs if fuse else None, eps=1e-5, state_init=s0)
+    Yr, Sr = chunk_gla_core(q, k, v, lg, r, 64, **kw)
+    assert fuse or Yr.abs().max().item() < 4.0  # raw outputs: the 16-bit output's own rounding stays below 1e-2
+    assert _prefill_status() == 0
+    for path in ("tc", "cuda_core"):
+        if path == "cuda_core":
+            monkeypatch.setenv("HOFA_GLA_NO_TC", "1")
+        st = torch.empty(B, H, D - r, D, device="cuda")
+        Y = gla_forward(q.cuda(), k.cuda(), v.cuda(), lg.cuda(), r, log_alpha=la.cuda(),
+                        mix_g=mix.cuda() if fuse else None, gla_scale=gs.cuda() if fuse else None,
+                        state_out=st, initial_state=s0.cuda())
+        torch.cuda.synchronize()
+        assert torch.isfinite(Y).all(), path
+        assert maxabs(Y, Yr) <= 2e-2, (path, maxabs(Y, Yr))
+        assert maxabs(st, Sr) <= 2e-2, (path, maxabs(st, Sr))
+    monkeypatch.delenv("HOFA_GLA_NO_TC")
+    assert _prefill_status() == 0
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
 def test_outlier_tensor_core_growing_logits(dtype):
     """Scores that grow along the keys (about 0.7 log2 units per key, 90 over
     128 keys): later tiles raise the running max far past the lazy-rescale
