@@ -442,11 +442,16 @@ def measure_prefill(dev, B=4, T=8192, steps=5, warmup=3, name="config2"):
     y = torch.empty(B, H, T, D, device=dev, dtype=torch.bfloat16)
     st = torch.empty(B, H, J, D, device=dev)
     flush = torch.empty(2 * 126 * 2 ** 20 // 4, device=dev)
+    # the reference model's per-channel decay variant (learnable_alpha), timed
+    # on its own: not part of the prefill total
+    la = torch.randn(1, H, 1, J, device=dev, generator=g) * 0.5
     ops = {
         "prep": lambda: prep(q, k, v, gate_w, gate_b, lg, mix_w=mix_w, mix_b=mix_b, mix_out=mix,
                              cos=rope.cos_cached, sin=rope.sin_cached, R=R, pos0=0, cache_k=ck, cache_v=cv),
         "gla": lambda: gla_forward(q, k, v, lg, R, mix_g=mix, gla_scale=gs, y=y, state_out=st),
         "outlier": lambda: exact_attention_triton(q, k, v, R, 2.0, mix, out=y),
+        "gla_per_channel_decay": lambda: gla_forward(q, k, v, lg, R, log_alpha=la, mix_g=mix, gla_scale=gs,
+                                                     y=y, state_out=st),
     }
     ms = {}
     for name_, fn in ops.items():
@@ -461,21 +466,30 @@ def measure_prefill(dev, B=4, T=8192, steps=5, warmup=3, name="config2"):
         e1.record()
         torch.cuda.synchronize()
         ms[name_] = e0.elapsed_time(e1) / steps
-    total = sum(ms.values())
+    total = ms["prep"] + ms["gla"] + ms["outlier"]
     attn_flops = B * H * (R + D) * T * T            # causal QK^T + PV, 2 flops per MAC
     gla_flops = 6 * B * H * J * D * T
-    bf16_peak = 1647.9
+    bf16_peak, hbm_peak = 1647.9, 6650.0
     pk = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(pk):
-        bf16_peak = float(json.load(open(pk))["bf16_tflops"])
+        peaks = json.load(open(pk))
+        bf16_peak, hbm_peak = float(peaks["bf16_tflops"]), float(peaks["hbm_gbs"])
     ach = attn_flops / (ms["outlier"] / 1e3) / 1e12
+    # GLA algorithmic bytes: Q_I and K_I as read (32-byte sectors of their 48-channel rows: 3/4 of each
+    # 128-byte row), V, log decay and blend (fp32 / bf16), y written
+    gla_bytes = B * H * T * (2 * (D * 2 * 3 // 4) + D * 2 + 4 + 2 + D * 2)
+    gla_ach = gla_bytes / (ms["gla"] / 1e3) / 1e9
     return {"workload": f"{name}-prefill-B{B}-T{T}", "tokens_per_s": round(B * T / (total / 1e3), 1),
             "ms": round(total, 4), "ms_by_kernel": {k_: round(v_, 4) for k_, v_ in ms.items()},
             "timing": f"CUDA events over {steps} back-to-back calls per operator, inputs larger than L2",
             "algorithmic_flops": attn_flops + gla_flops, "exps": B * H * T * T // 2,
             "roofline_outlier_kernel": {"bound": "tensor", "achieved": round(ach, 2), "peak": bf16_peak,
                                         "unit": "TFLOP/s", "frac": round(ach / bf16_peak, 4),
-                                        "peak_source": "measured bf16_tflops (burst)"}}
+                                        "peak_source": "measured bf16_tflops (burst)"},
+            "roofline_gla_kernel": {"bound": "hbm", "achieved": round(gla_ach, 1), "peak": hbm_peak, "unit": "GB/s",
+                                    "frac": round(gla_ach / hbm_peak, 4), "algorithmic_bytes": gla_bytes,
+                                    "peak_source": "measured hbm_gbs"},
+            "gla_per_channel_decay_ms": round(ms["gla_per_channel_decay"], 4)}
 
 
 def measure_decode_batch(dev, B, steps=200, reps=3):
