@@ -669,8 +669,20 @@ template <typename T, int D, bool ALPHA, bool CLUSTER, int NW, bool PREP>
 cudaError_t launch_bulk(const DecodeParams& p, cudaStream_t st) {
   const size_t smem = (size_t)p.stages * kBulkChunk * (p.R + D) * sizeof(T);
   auto k = decode_bulk_kernel<T, D, ALPHA, CLUSTER, NW, PREP>;
-  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  // the function attributes are set once per device (and again only for a
+  // larger shared-memory size): a decode step's host time is on the critical
+  // path of a serving loop that synchronises every token
+  static int smem_set[64] = {};
+  static bool cluster_set[64] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
+  const int slot = dev >= 0 && dev < 64 ? dev : 0;
+  if (smem_set[slot] < (int)smem || dev >= 64) {
+    e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    smem_set[slot] = (int)smem;
+  }
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(p.split_k, p.H, p.B);
   cfg.blockDim = dim3(NW * 32 + 64);
@@ -682,9 +694,10 @@ cudaError_t launch_bulk(const DecodeParams& p, cudaStream_t st) {
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (CLUSTER) {
-    if (p.split_k > 8) {
+    if (p.split_k > 8 && (!cluster_set[slot] || dev >= 64)) {
       e = cudaFuncSetAttribute(k, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
       if (e != cudaSuccess) return e;
+      cluster_set[slot] = true;
     }
     attr[1].id = cudaLaunchAttributeClusterDimension;
     attr[1].val.clusterDim.x = p.split_k;
