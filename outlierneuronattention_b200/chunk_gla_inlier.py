@@ -25,12 +25,16 @@ def _pow2_at_least16(n: int) -> int:
 
 
 def _workspace(device, B, H, T, D, R, nseg) -> torch.Tensor:
+    """The call's workspace, cached per (device, stream): the tensor-core GLA
+    keeps its chunk tickets and publication flags there, so two calls that
+    may run at the same time (on different streams) must not share one."""
     nbytes = int(_capi.lib().hofa_gla_workspace_size(B, H, T, D, R, 64, nseg))
     idx = device.index if device.index is not None else torch.cuda.current_device()
-    ws = _WS.get(idx)
+    key = (idx, torch.cuda.current_stream(idx).cuda_stream)
+    ws = _WS.get(key)
     if ws is None or ws.numel() < nbytes:
         ws = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
-        _WS[idx] = ws
+        _WS[key] = ws
     return ws
 
 
