@@ -139,6 +139,7 @@ def test_choose_split_and_workspace_size():
     L = _capi.lib()
     assert L.hofa_decode_choose_split(4, 16, 4096, 148) == 4     # 256 CTAs, clusters of 4
     assert L.hofa_decode_choose_split(1, 16, 4096, 148) == 8     # clusters capped at 8
+    assert L.hofa_decode_choose_split(2, 16, 4096, 148) == 6     # 8-CTA clusters would need 256 CTAs
     assert L.hofa_decode_choose_split(1, 16, 65536, 148) == 18   # workspace combine above 16
     assert L.hofa_decode_choose_split(64, 16, 16384, 148) == 1
     assert L.hofa_decode_choose_split(1, 1, 10, 148) == 1

@@ -63,13 +63,13 @@ def check(y, s, y_ref, s_ref, dtype):
     torch.testing.assert_close(s.double().cpu(), s_ref, atol=1e-5, rtol=1e-5)
 
 
-@pytest.mark.parametrize("B", [1, 4])
+@pytest.mark.parametrize("B", [1, 2, 4])
 def test_config1_decode_bf16(B):
     """d_model=1024 -> H=16, d_h=64, r=16, L=4096."""
     check(*run_pair(B, 16, 64, 16, 4096, 4096, torch.bfloat16, seed=B), torch.bfloat16)
 
 
-@pytest.mark.parametrize("split_k", [1, 2, 3, 7, 64])
+@pytest.mark.parametrize("split_k", [1, 2, 3, 6, 7, 64])
 def test_split_counts(split_k):
     check(*run_pair(2, 4, 64, 16, 1000, 1000, torch.bfloat16, seed=10 + split_k, split_k=split_k), torch.bfloat16)
 
