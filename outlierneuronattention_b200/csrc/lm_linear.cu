@@ -10,7 +10,9 @@
 // At decode batch sizes a projection is a matrix-vector product: every weight
 // is read once and used M times, so the kernel streams W at HBM speed with
 // 16-byte loads and does the few FMAs per element on the CUDA cores.  Two CTAs
-// of 8 warps per SM (grid-stride over row groups).  The kernel is launched
+// of 8 warps per SM (grid-stride over row groups); a warp covers at most 1024
+// columns of its rows, so larger K is split over 2 or 4 warps of a CTA (one
+// warp per 4096-wide row took twice as long for the same bytes).  The kernel is launched
 // with programmatic dependent launch: each warp issues its first row group's
 // weight loads BEFORE waiting for the previous kernel of the stream (the
 // weights are parameters: no kernel of a decode loop writes them, so they may
@@ -59,23 +61,31 @@ __device__ __forceinline__ uint4 pack8(const float f[8]) {
   return u;
 }
 
-// KCH: 16-byte weight chunks per lane per row (K / 256 for 2-byte types);
-// RG: rows per warp group (all RG*KCH loads in flight together).
-template <typename T, int MODE, bool RES, int KCH, int RG>
+// KCH: 16-byte weight chunks per lane per row segment (256 columns each);
+// RG: rows per group; SEG: warps that share a group, each taking one
+// contiguous K segment of KCH * 256 columns (their partial sums meet in
+// shared memory).  A CTA works on 8 / SEG groups at a time, in lockstep.  All
+// of a warp's RG * KCH loads are in flight together.  MAXM: the largest batch
+// (rows of x) the instance serves (its accumulators are sized for it).
+template <typename T, int MODE, bool RES, int KCH, int RG, int SEG, int MAXM>
 __global__ void __launch_bounds__(kLinThreads, 2) lm_linear_kernel(const LinearParams p) {
   static_assert(sizeof(T) == 2, "2-byte activations");
+  static_assert(kLinWarps % SEG == 0, "segments of a group share one CTA");
+  constexpr int GPC = kLinWarps / SEG;   // groups per CTA step
   extern __shared__ __align__(16) unsigned char smem_raw[];
   T* sxin = reinterpret_cast<T*>(smem_raw);          // [M][K]
   __shared__ float s_part[kLinWarps][kMaxM];
   __shared__ float s_scale[kMaxM];
+  __shared__ float s_red[SEG > 1 ? kLinWarps : 1][RG][MAXM];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int seg = warp % SEG, slot = warp / SEG;
   const int M = p.M, K = p.K;
+  const int kbase = seg * KCH * 256;
   const T* W = reinterpret_cast<const T*>(p.w);
   const int groups = (p.N + RG - 1) / RG;
-  const int stride_g = gridDim.x * kLinWarps;
-  int g = blockIdx.x * kLinWarps + warp;
+  const int step = gridDim.x * GPC;
 
-  // first group's weights: issued before the input is staged
+  // first step's weights: issued before the input is staged
   uint4 wv[RG][KCH];
   auto issue = [&](int grp) {
 #pragma unroll
@@ -83,12 +93,14 @@ __global__ void __launch_bounds__(kLinThreads, 2) lm_linear_kernel(const LinearP
       const int n = grp * RG + r;
 #pragma unroll
       for (int c = 0; c < KCH; ++c) {
-        const int k0 = (c * 32 + lane) * 8;
-        wv[r][c] = (n < p.N && k0 < K) ? ld_stream16(W + (int64_t)n * p.sw + k0) : make_uint4(0, 0, 0, 0);
+        const int k0 = kbase + (c * 32 + lane) * 8;
+        wv[r][c] = (grp < groups && n < p.N && k0 < K) ? ld_stream16(W + (int64_t)n * p.sw + k0)
+                                                       : make_uint4(0, 0, 0, 0);
       }
     }
   };
-  if (g < groups) issue(g);
+  int g0 = blockIdx.x * GPC;
+  issue(g0 + slot);
   // x / residual come from the kernels before: wait for them, then let the
   // next kernel of the stream start its own weight fetch
   asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -98,12 +110,12 @@ __global__ void __launch_bounds__(kLinThreads, 2) lm_linear_kernel(const LinearP
   const T* X = reinterpret_cast<const T*>(p.x);
   const int K8 = K / 8;
   if constexpr (MODE == 1) {
-    float ss[kMaxM];
+    float ss[MAXM];
 #pragma unroll
-    for (int m = 0; m < kMaxM; ++m) ss[m] = 0.f;
+    for (int m = 0; m < MAXM; ++m) ss[m] = 0.f;
     for (int i = tid; i < K8; i += kLinThreads) {
 #pragma unroll
-      for (int m = 0; m < kMaxM; ++m) {
+      for (int m = 0; m < MAXM; ++m) {
         if (m < M) {
           float f[8];
           Vec8<T> v;
@@ -115,7 +127,7 @@ __global__ void __launch_bounds__(kLinThreads, 2) lm_linear_kernel(const LinearP
       }
     }
 #pragma unroll
-    for (int m = 0; m < kMaxM; ++m) {
+    for (int m = 0; m < MAXM; ++m) {
       const float t = warp_sum(ss[m]);
       if (lane == 0) s_part[warp][m] = t;
     }
@@ -149,15 +161,18 @@ __global__ void __launch_bounds__(kLinThreads, 2) lm_linear_kernel(const LinearP
   }
   __syncthreads();
 
-  for (; g < groups; g += stride_g) {
-    float acc[RG][kMaxM];
+  // every warp of a CTA takes the same number of steps (the shared-memory
+  // combine of the segments needs the whole CTA)
+  for (; g0 < groups; g0 += step) {
+    const int g = g0 + slot;
+    float acc[RG][MAXM];
 #pragma unroll
     for (int r = 0; r < RG; ++r)
 #pragma unroll
-      for (int m = 0; m < kMaxM; ++m) acc[r][m] = 0.f;
+      for (int m = 0; m < MAXM; ++m) acc[r][m] = 0.f;
 #pragma unroll
     for (int c = 0; c < KCH; ++c) {
-      const int k0 = (c * 32 + lane) * 8;
+      const int k0 = kbase + (c * 32 + lane) * 8;
       if (k0 < K) {
         float wf[RG][8];
 #pragma unroll
@@ -167,7 +182,7 @@ __global__ void __launch_bounds__(kLinThreads, 2) lm_linear_kernel(const LinearP
           vec8_to_f(wq, wf[r]);
         }
 #pragma unroll
-        for (int m = 0; m < kMaxM; ++m) {
+        for (int m = 0; m < MAXM; ++m) {
           if (m < M) {
             float xf[8];
             Vec8<T> xv;
@@ -181,23 +196,40 @@ __global__ void __launch_bounds__(kLinThreads, 2) lm_linear_kernel(const LinearP
         }
       }
     }
-    const int gcur = g;
-    if (g + stride_g < groups) issue(g + stride_g);   // next group's loads before the reductions
+    if (g0 + step < groups) issue(g0 + step + slot);   // next step's loads before the reductions
 #pragma unroll
-    for (int r = 0; r < RG; ++r) {
-      const int n = gcur * RG + r;
+    for (int r = 0; r < RG; ++r)
 #pragma unroll
-      for (int m = 0; m < kMaxM; ++m) {
-        if (m < M) {
-          const float t = warp_sum(acc[r][m]);
-          if (lane == m && n < p.N) {
-            float out = t;
+      for (int m = 0; m < MAXM; ++m)
+        if (m < M) acc[r][m] = warp_sum(acc[r][m]);
+    if constexpr (SEG > 1) {
+      if (lane == 0) {
+#pragma unroll
+        for (int r = 0; r < RG; ++r)
+#pragma unroll
+          for (int m = 0; m < MAXM; ++m) s_red[warp][r][m] = acc[r][m];
+      }
+      __syncthreads();
+    }
+    if (seg == 0) {
+#pragma unroll
+      for (int r = 0; r < RG; ++r) {
+        const int n = g * RG + r;
+#pragma unroll
+        for (int m = 0; m < MAXM; ++m) {
+          if (m < M && lane == m && g < groups && n < p.N) {
+            float out = acc[r][m];
+            if constexpr (SEG > 1) {
+#pragma unroll
+              for (int sg = 1; sg < SEG; ++sg) out += s_red[warp + sg][r][m];
+            }
             if constexpr (RES) out += to_f(reinterpret_cast<const T*>(p.res)[(int64_t)m * p.sres + n]);
             reinterpret_cast<T*>(p.y)[(int64_t)m * p.sy + n] = from_f<T>(out);
           }
         }
       }
     }
+    if constexpr (SEG > 1) __syncthreads();   // s_red is rewritten next step
   }
 }
 
@@ -209,11 +241,12 @@ cudaError_t launch_k(const LinearParams& p, cudaStream_t st) {
     int dev = 0;
     if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   }
-  auto go = [&](auto kern, int rg) -> cudaError_t {
+  auto go = [&](auto kern, int rg, int seg) -> cudaError_t {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     const int groups = (p.N + rg - 1) / rg;
-    int grid = (groups + kLinWarps - 1) / kLinWarps;
+    const int gpc = kLinWarps / seg;
+    int grid = (groups + gpc - 1) / gpc;
     if (grid > 2 * sms) grid = 2 * sms;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -229,9 +262,21 @@ cudaError_t launch_k(const LinearParams& p, cudaStream_t st) {
     if (e != cudaSuccess) return e;
     return cudaGetLastError();
   };
-  if (p.K <= 1024) return go(lm_linear_kernel<T, MODE, RES, 4, 2>, 2);
-  if (p.K <= 2048) return go(lm_linear_kernel<T, MODE, RES, 8, 1>, 1);
-  return go(lm_linear_kernel<T, MODE, RES, 16, 1>, 1);
+  // each warp takes up to 1024 columns of its rows (K above that is split
+  // over 2 or 4 warps); for one row of x (accumulators for one row), 4 rows a
+  // warp when 2 would leave weights for a second round of loads behind the first
+  const int slots = 2 * sms * kLinWarps;
+  if (p.M == 1) {  // accumulators for one row of x
+    if (p.K <= 1024) {
+      if ((p.N + 1) / 2 > slots) return go(lm_linear_kernel<T, MODE, RES, 4, 4, 1, 1>, 4, 1);
+      return go(lm_linear_kernel<T, MODE, RES, 4, 2, 1, 1>, 2, 1);
+    }
+    if (p.K <= 2048) return go(lm_linear_kernel<T, MODE, RES, 4, 2, 2, 1>, 2, 2);
+    return go(lm_linear_kernel<T, MODE, RES, 4, 2, 4, 1>, 2, 4);
+  }
+  if (p.K <= 1024) return go(lm_linear_kernel<T, MODE, RES, 4, 2, 1, kMaxM>, 2, 1);
+  if (p.K <= 2048) return go(lm_linear_kernel<T, MODE, RES, 4, 2, 2, kMaxM>, 2, 2);
+  return go(lm_linear_kernel<T, MODE, RES, 4, 2, 4, kMaxM>, 2, 4);
 }
 
 template <typename T>

@@ -75,7 +75,8 @@ def test_fused_step_matches_modules(B):
 
 
 @pytest.mark.parametrize("mode", [0, 1, 2])
-@pytest.mark.parametrize("M,N,K", [(1, 3072, 1024), (4, 1000, 4096), (8, 264, 2048), (3, 32000, 1024)])
+@pytest.mark.parametrize("M,N,K", [(1, 3072, 1024), (4, 1000, 4096), (8, 264, 2048), (3, 32000, 1024),
+                                   (1, 9001, 1024), (1, 1024, 4096), (1, 520, 2048)])
 def test_lm_linear_modes(mode, M, N, K):
     g = torch.Generator(device="cuda").manual_seed(M * 7 + mode)
     x = torch.randn(M, 2 * K if mode == 2 else K, device="cuda", generator=g).to(torch.bfloat16)
