@@ -69,7 +69,7 @@ def test_config1_decode_bf16(B):
     check(*run_pair(B, 16, 64, 16, 4096, 4096, torch.bfloat16, seed=B), torch.bfloat16)
 
 
-@pytest.mark.parametrize("split_k", [1, 2, 3, 6, 7, 64])
+@pytest.mark.parametrize("split_k", [1, 2, 3, 6, 7, 12, 64])
 def test_split_counts(split_k):
     check(*run_pair(2, 4, 64, 16, 1000, 1000, torch.bfloat16, seed=10 + split_k, split_k=split_k), torch.bfloat16)
 
