@@ -101,6 +101,18 @@ __global__ void __launch_bounds__(kLinThreads, 2) lm_linear_kernel(const LinearP
   };
   int g0 = blockIdx.x * GPC;
   issue(g0 + slot);
+  // RMSNorm weights of this thread's staging chunks (columns 8 kc .. 8 kc + 8
+  // for kc = tid, tid + 256; K <= 4096): parameters as well, read before the wait
+  float nwr[MODE == 1 ? 2 : 1][8];
+  if constexpr (MODE == 1) {
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int kc = tid + j * kLinThreads;
+#pragma unroll
+      for (int e = 0; e < 8; ++e)
+        nwr[j][e] = kc < K / 8 ? ld_any(p.norm_w, p.dt_nw, (int64_t)(kc * 8 + e) * p.snw) : 0.f;
+    }
+  }
   // x / residual come from the kernels before: wait for them, then let the
   // next kernel of the stream start its own weight fetch
   asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -138,18 +150,33 @@ __global__ void __launch_bounds__(kLinThreads, 2) lm_linear_kernel(const LinearP
       s_scale[tid] = rsqrtf(t / (float)K + p.eps);
     }
     __syncthreads();
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      const int kc = tid + j * kLinThreads;
+      if (kc < K8) {
+#pragma unroll
+        for (int m = 0; m < MAXM; ++m) {
+          if (m < M) {
+            float f[8];
+            Vec8<T> v;
+            v.w[0] = *reinterpret_cast<const uint4*>(X + (int64_t)m * p.sx + kc * 8);
+            vec8_to_f(v, f);
+            const float sc = s_scale[m];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) f[e] = f[e] * sc * nwr[j][e];
+            *reinterpret_cast<uint4*>(sxin + (int64_t)m * K + kc * 8) = pack8<T>(f);
+          }
+        }
+      }
+    }
   }
-  for (int i = tid; i < M * K8; i += kLinThreads) {
+  for (int i = tid; MODE != 1 && i < M * K8; i += kLinThreads) {
     const int m = i / K8, k0 = (i - m * K8) * 8;
     float f[8];
     Vec8<T> v;
     v.w[0] = *reinterpret_cast<const uint4*>(X + (int64_t)m * p.sx + k0);
     vec8_to_f(v, f);
-    if constexpr (MODE == 1) {
-      const float sc = s_scale[m];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) f[e] = f[e] * sc * ld_any(p.norm_w, p.dt_nw, (int64_t)(k0 + e) * p.snw);
-    } else if constexpr (MODE == 2) {
+    if constexpr (MODE == 2) {
       float u[8];
       Vec8<T> vu;
       vu.w[0] = *reinterpret_cast<const uint4*>(X + (int64_t)m * p.sx + K + k0);
