@@ -69,6 +69,15 @@ def test_config1_decode_bf16(B):
     check(*run_pair(B, 16, 64, 16, 4096, 4096, torch.bfloat16, seed=B), torch.bfloat16)
 
 
+@pytest.mark.parametrize("R", [88, 96])
+def test_fp32_large_r_without_room_for_the_ring(R):
+    """float32 at head dim 128 with most channels in the outlier path: even a
+    4-stage ring of 64-token chunks would need more shared memory than a CTA
+    gets (4 x 64 x (R + 128) x 4 bytes), so the launcher takes the 16-byte
+    register-load path; it still matches the oracle."""
+    check(*run_pair(1, 2, 128, R, 300, 300, torch.float32, seed=R), torch.float32)
+
+
 @pytest.mark.parametrize("split_k", [1, 2, 3, 6, 7, 12, 64])
 def test_split_counts(split_k):
     check(*run_pair(2, 4, 64, 16, 1000, 1000, torch.bfloat16, seed=10 + split_k, split_k=split_k), torch.bfloat16)
