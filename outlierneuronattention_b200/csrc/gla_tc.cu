@@ -20,8 +20,9 @@
 //   B  gla_tc_scan_kernel    (one thread per state element of a head)
 //        S_0 = state_init or 0;  start_c = S before chunk c;  S <- exp(G_C) S + dS_c
 //        start_c overwrites dS_c in the workspace; the last S goes to state_out
-//   C  gla_tc_out_kernel     (one CTA per chunk c; at D = 64 Y2 and then Y1 reuse A's
-//                             upper TMEM columns once P is formed: 128 columns, 3 CTAs/SM)
+//   C  gla_tc_out_kernel     (one CTA per chunk c; at D = 64 -- the per-channel decay --
+//                             Y2 and then Y1 reuse A's upper TMEM columns once P is
+//                             formed: 128 columns)
 //        A   = Q_I K_I^T            tcgen05.mma M=128, N=128, K=J (A/B K-major)
 //        Y2  = Q_I start_c          tcgen05.mma M=128, N=D,   K=J (start_c as a bf16
 //                                   MN-major operand)
@@ -72,9 +73,10 @@ struct Geo {
   static constexpr bool SHARE = D == 64;
   static constexpr uint32_t OUT_COLS = SHARE ? 128 : 512;
   static constexpr size_t STATE_SMEM = 3 * OP + 1024 + 256 + 4 * D;   // K (then Kd hi), V, Kd lo; alpha
-  // D = 64: 80 KB keeps <= 2 CTAs (2 x 256 TMEM columns) per SM; D = 128: one CTA
+  // D = 64: about 69 KB, three CTAs per SM; D = 128: one CTA
   static constexpr size_t OUT_SMEM = 4 * OP + 1024 + 4096 + 4 * D;
   // per-channel decay: two more tiles for the lo terms of the decayed Q and K
+  // (D = 64: about 101 KB, two CTAs per SM)
   static constexpr size_t OUT_SMEM_ALPHA = 6 * OP + 1024 + 4096 + 4 * D;
 };
 
